@@ -1,0 +1,459 @@
+#!/usr/bin/env python3
+"""bench.py — int4 expert-FFN decode throughput on B200 (GB/s of expert weights).
+
+Workload (OLMoE-shaped MoE block): hidden 2048, 64 experts,
+top-8, SwiGLU experts int4 group-64 (gate/up 1024x2048, down 2048x1024), bf16
+router [64x2048], decode batch 1.  A step is one decode token through the MoE
+blocks of 16 layers with distinct weights (OLMoE's layer count), each layer's
+output feeding the next layer; the 16 expert tables (3.6 GB) keep every step's
+451 MB of expert reads far above the 126 MB L2.  Synthetic seeded weights.
+
+value    = algorithmic bytes (distinct experts read x 3,538,944 B + router
+           262,144 B, per layer) per step x steps / device time of the steps,
+           inputs resident in HBM, all steps replayed from one CUDA graph.
+e2e      = the same bytes through the reference-facing synchronous C-ABI call
+           (m1moe_cuda_moe_layer_host, one per layer, like runLayer's
+           commitSync) with pinned host buffers; copies inside the timed region.
+N GPUs   = expert parallel: rank r holds experts [r*64/N, (r+1)*64/N) of every
+           layer and owns one decode token; per layer the tokens are
+           all-gathered, each rank applies its experts to every token routed to
+           them, and a reduce-scatter returns each token's sum (weak scaling).
+--impl reference  times the CPU oracle (a C restatement of the reference's
+           Metal/Swift arithmetic; the reference itself is Swift+Metal and cannot
+           run on this box) on a bounded sample, on all host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "int4 expert matvec GB/s (% of HBM peak); decode tok/s at 1/2/4/8 B200"
+WORKLOADS = {
+    "olmoe": dict(name="olmoe_moe_decode_b1x16L", h=2048, I=1024, E=64, K=8, gs=64, layers=16,
+                  norm=False),
+    "mixtral": dict(name="mixtral_moe_decode_b1x4L", h=4096, I=14336, E=8, K=2, gs=64, layers=4,
+                    norm=True),
+}
+SEED = 20251201
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["m1moe", "reference"], default="m1moe")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="olmoe")
+    ap.add_argument("--tokens-per-rank", type=int, default=1)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU-baseline sample length (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """Polls NVML (what nvidia-smi reads) for SM clock and throttle reasons."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._period = period_s
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._h = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _sample(self):
+        nv = self._nv
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+        self.reasons |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+            try:
+                self._sample()
+            except Exception:
+                pass
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml_unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------- CPU oracle --
+def cpu_sample(wl: dict, host_layers, routers, seconds: float, threads: int) -> dict:
+    """Time the CPU oracle (MoE block, batch 1) over host layers until `seconds` pass."""
+    import oracle
+    oracle.build()
+    from m1moe_b200 import synth
+    h = wl["h"]
+    x = synth.bf16_to_f32(synth.hidden_states(SEED + 99, 1, h))
+    res = x.copy()
+    n, nbytes, t0 = 0, 0, time.perf_counter()
+    while True:
+        L = n % len(host_layers)
+        out, idx, _ = oracle.moe_layer(host_layers[L], routers[L], x, res, h=h, inter=wl["I"],
+                                       E=wl["E"], K=wl["K"], gs=wl["gs"], norm=wl["norm"],
+                                       nthreads=threads)
+        nbytes += len(set(idx[0].tolist())) * expert_bytes(wl) + router_bytes(wl)
+        x = res = out
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds and n >= 2:
+            break
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{n} layer-tokens of the {wl['name']} MoE block over {len(host_layers)} "
+                      f"synthetic layers, C oracle with {threads} threads, {dt:.1f} s"}
+
+
+def expert_bytes(wl):
+    from m1moe_b200.spec import expert_bytes as eb
+    return eb(wl["h"], wl["I"], wl["gs"])
+
+
+def router_bytes(wl):
+    return wl["E"] * wl["h"] * 2
+
+
+def host_layers_for_cpu(wl, n_layers: int, device=None):
+    from m1moe_b200 import synth
+    if device is not None:
+        return [synth.layer_image_device(wl["E"], wl["h"], wl["I"], wl["gs"], seed=SEED + L,
+                                         device=device).cpu().numpy() for L in range(n_layers)]
+    return [synth.layer_image(SEED + L, wl["E"], wl["h"], wl["I"], wl["gs"])
+            for L in range(n_layers)]
+
+
+def run_reference(args, wl) -> None:
+    """CPU arm: the oracle (C restatement of the reference path), all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from m1moe_b200 import synth
+    threads = os.cpu_count() or 1
+    layers = host_layers_for_cpu(wl, 2)
+    routers = [synth.router_weights(SEED + 1000 + L, wl["E"], wl["h"]) for L in range(2)]
+    import oracle
+    oracle.build()
+    x = synth.bf16_to_f32(synth.hidden_states(SEED + 99, 1, wl["h"]))
+    res = x.copy()
+
+    def step():
+        nonlocal x, res
+        nb = 0
+        for L in range(2):
+            out, idx, _ = oracle.moe_layer(layers[L], routers[L], x, res, h=wl["h"],
+                                           inter=wl["I"], E=wl["E"], K=wl["K"], gs=wl["gs"],
+                                           norm=wl["norm"], nthreads=threads)
+            nb += len(set(idx[0].tolist())) * expert_bytes(wl) + router_bytes(wl)
+            x = res = out
+        return nb
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    nbytes = sum(step() for _ in range(args.steps))
+    dt = time.perf_counter() - t0
+    val = nbytes / dt / 1e9
+    sample = (f"each step: one token through 2 synthetic {wl['name']} MoE layers "
+              f"(C oracle, {threads} threads)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl["name"], "tokens_per_step": 1, "layers_per_step": 2},
+        "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# -------------------------------------------------------------- GPU arm ----
+def run_gpu(args, wl) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from m1moe_b200 import MoEBlock, _lib, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    E, h, I, K, L = wl["E"], wl["h"], wl["I"], wl["K"], wl["layers"]
+    if E % world:
+        raise SystemExit(f"{E} experts do not shard over {world} GPUs")
+    b = args.tokens_per_rank
+    B = b * world  # tokens every rank applies its experts to
+    if B > 8:
+        raise SystemExit("at most 8 tokens per MoE call")
+    ne = E // world
+    e0 = rank * ne
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, group_size=wl["gs"],
+                   num_layers=L, norm_topk_prob=wl["norm"], max_batch=B, device=local,
+                   expert_begin=e0, expert_count=ne)
+    for layer in range(L):
+        img = synth.layer_image_device(E, h, I, wl["gs"], seed=SEED + layer, device=dev)
+        blk.load_expert_layer(layer, img)
+        del img
+        blk.load_router(layer, synth.router_weights(SEED + 1000 + layer, E, h))
+    torch.cuda.synchronize()
+
+    x0 = torch.from_numpy(synth.hidden_states(SEED + 7 + rank, b, h).view(np.int16)).to(dev)
+    x0 = x0.view(torch.bfloat16)
+    xa = torch.zeros((B, h), dtype=torch.float32, device=dev)   # gathered layer inputs
+    res = torch.zeros((B, h), dtype=torch.float32, device=dev)  # own rows only, else 0
+    part = torch.zeros((B, h), dtype=torch.float32, device=dev)  # partial sums (EP)
+    own = torch.zeros((b, h), dtype=torch.float32, device=dev)   # this rank's token state
+    own.copy_(x0.float())
+    idx_log = torch.zeros((L, B, K), dtype=torch.int32, device=dev)
+    w_log = torch.zeros((L, B, K), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    # Single GPU: ping-pong own/part so every layer reads the previous output
+    # (x and the residual are both the previous layer's f32 output).
+    if world == 1:
+        bufs = [own, part]
+
+        def one_step(events=None):
+            for layer in range(L):
+                if events is not None:
+                    events[layer].record()
+                src, dst = bufs[layer % 2], bufs[(layer + 1) % 2]
+                _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, src.data_ptr(), 0,
+                          src.data_ptr(), 0, dst.data_ptr(), 0, B, idx_log[layer].data_ptr(),
+                          w_log[layer].data_ptr(), stream.cuda_stream)
+            if L % 2:  # result must end in bufs[0] for the next step
+                bufs[0].copy_(bufs[1])
+            if events is not None:
+                events[L].record()
+    else:
+        def one_step(events=None):
+            for layer in range(L):
+                if events is not None:
+                    events[layer].record()
+                dist.all_gather_into_tensor(xa, own)
+                res[rank * b:(rank + 1) * b].copy_(own)
+                _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, xa.data_ptr(), 0,
+                          res.data_ptr(), 0, part.data_ptr(), 0, B, idx_log[layer].data_ptr(),
+                          w_log[layer].data_ptr(), stream.cuda_stream)
+                dist.reduce_scatter_tensor(own, part)
+            if events is not None:
+                events[L].record()
+
+    launches_per_step = 3 * L
+    # Eager warm-up (initialises NCCL communicators before capture).
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            one_step()
+    torch.cuda.synchronize()
+
+    ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(L + 1)]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        one_step(ev)
+    torch.cuda.synchronize()
+
+    def replay(n):
+        for _ in range(n):
+            graph.replay()
+
+    with torch.cuda.stream(stream):
+        replay(args.warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    layer_ms = []
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            t_start.record(stream)
+            replay(args.steps)
+            t_end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = t_start.elapsed_time(t_end)
+    # per-layer launch-sequence durations of the last replay
+    layer_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(L)]
+
+    # Distinct local experts per layer from the last step's routing.
+    idx_last = idx_log.cpu().numpy()
+    eb = expert_bytes(wl)
+    step_bytes_local = sum(
+        len({e for e in idx_last[layer].ravel().tolist() if e0 <= e < e0 + ne}) * eb
+        + router_bytes(wl) for layer in range(L))
+
+    t = torch.tensor([ms, float(step_bytes_local)], dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = t[:1].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tb = t[1:].clone()
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+        ms_max, job_step_bytes = float(tmax.item()), float(tb.item())
+    else:
+        ms_max, job_step_bytes = ms, float(step_bytes_local)
+    value = job_step_bytes * args.steps / (ms_max * 1e-3) / 1e9
+
+    # Dominant launch sequence: one layer's MoE block (router + gate/up + down)
+    # on this rank; bytes = distinct local experts + router of that layer.
+    per_layer_bytes = step_bytes_local / L
+    peak, peak_kind = measured_peaks()
+    lay_ms = float(np.mean(layer_ms))
+    achieved = per_layer_bytes / (lay_ms * 1e-3) / 1e9
+
+    # e2e: reference-facing synchronous host call (N=1), or host I/O around the
+    # captured step (N>1), timed over the same number of steps.
+    e2e = None
+    if world == 1:
+        hx = torch.empty((B, h), dtype=torch.float32).pin_memory()
+        hx.copy_(x0.float().cpu())
+        hout = torch.empty_like(hx).pin_memory()
+        hidx = torch.empty((B, K), dtype=torch.int32).pin_memory()
+        hw = torch.empty((B, K), dtype=torch.float32).pin_memory()
+        n_e2e = max(1, min(args.steps, 200))
+
+        def host_step():
+            for layer in range(L):
+                _lib.call("m1moe_cuda_moe_layer_host", blk._ctx, layer, hx.data_ptr(),
+                          hx.data_ptr(), hout.data_ptr(), B, hidx.data_ptr(), hw.data_ptr())
+                hx.copy_(hout)
+
+        for _ in range(min(args.warmup, 5)):
+            host_step()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            host_step()
+        dt = time.perf_counter() - t0
+        e2e = {"value": job_step_bytes * n_e2e / dt / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": L * 2 * B * h * 4,
+               "d2h_bytes_per_step": L * (B * h * 4 + 2 * B * K * 4),
+               "steps": n_e2e, "api": "m1moe_cuda_moe_layer_host per layer (synchronous)"}
+    else:
+        hin = torch.empty((b, h), dtype=torch.float32).pin_memory()
+        hout = torch.empty((b, h), dtype=torch.float32).pin_memory()
+        hin.copy_(x0.float().cpu())
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            s0.record(stream)
+            for _ in range(args.steps):
+                own.copy_(hin, non_blocking=True)
+                graph.replay()
+                hout.copy_(own, non_blocking=True)
+            s1.record(stream)
+        torch.cuda.synchronize()
+        te = torch.tensor([s0.elapsed_time(s1)], dtype=torch.float64, device=dev)
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": job_step_bytes * args.steps / (te.item() * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": b * h * 4, "d2h_bytes_per_step": b * h * 4,
+               "api": "pinned H2D + captured EP step + D2H per step"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        host = host_layers_for_cpu(wl, 2, device=dev)
+        routers = [synth.router_weights(SEED + 1000 + layer, E, h) for layer in range(2)]
+        cpu = cpu_sample(wl, host, routers, args.cpu_seconds, os.cpu_count() or 1)
+
+    if rank == 0:
+        toks = b * world * args.steps / (ms_max * 1e-3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": wl["name"], "hidden": h, "intermediate": I, "experts": E,
+                       "top_k": K, "group_size": wl["gs"], "layers_per_step": L,
+                       "tokens_per_rank": b, "parallelism": f"ep{world}",
+                       "l2": "inputs larger than L2 (distinct 16-layer tables, 3.6 GB)"},
+            "tok_s": toks,
+            "hbm_frac_of_step": value / world / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "one MoE layer: k_router_logits + k_moe_gateup + k_moe_down",
+                         "peak_source": peak_kind, "layer_us": lay_ms * 1e3},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches_per_step * (args.steps + 0),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    blk.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_gpu(args, wl)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,188 @@
+/*
+ * m1moe_cuda.h — C ABI of the B200 (sm_100a) int4 expert-FFN library.
+ *
+ * This is the drop-in boundary for M1MoE's MoE block.  In the reference the
+ * block is private Swift in InferenceEngine (Sources/M1MoE/InferenceEngine.swift
+ * :240-266 router + expert load + CMD3, :401-478 encoders, :490-519 router)
+ * driving Metal pipelines built in MetalContext.swift:101-111 whose kernel ABI
+ * is "buffer index + setBytes scalar" (Shaders.metal:29-51).  A SwiftPM C
+ * module target exposing this header replaces those encoders one for one; the
+ * comment on each entry point names the reference code it replaces.
+ *
+ * Conventions
+ *  - Every entry point returns an m1moe_status (0 = success).  Nothing throws
+ *    across the ABI and nothing calls exit().  m1moe_cuda_last_error() gives a
+ *    thread-local message for the last failure on the calling thread.
+ *  - Pointers named d_* are device pointers; h_* are host pointers.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = the legacy default
+ *    stream).  Functions taking a stream are stream-ordered and do not
+ *    synchronise; the *_host variants are synchronous like the reference's
+ *    commitSync (InferenceEngine.swift:289-294).
+ *  - Weights use the reference's on-disk format unchanged (scripts/
+ *    extract_olmoe.py:20-38): per projection W uint32[rows][cols/8] with
+ *    nibble b of word w = column 8w+b, then S and B as bf16[rows][cols/gs];
+ *    dequant w = q*S + B.  One expert block is
+ *    [gateW|gateS|gateB|upW|upS|upB|downW|downS|downB] (ModelSpec.swift:36-52).
+ *  - Matvec arithmetic is fp32 (fp32 FMA accumulation); activations may be
+ *    passed as f32 or bf16 and outputs written as f32 or bf16.
+ */
+#ifndef M1MOE_CUDA_H
+#define M1MOE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define M1MOE_CUDA_ABI_VERSION 1
+
+/* Exported symbols (the library is built with hidden default visibility). */
+#if defined(__GNUC__)
+#define M1MOE_API __attribute__((visibility("default")))
+#else
+#define M1MOE_API
+#endif
+
+typedef enum m1moe_status {
+    M1MOE_OK = 0,
+    M1MOE_ERR_INVALID_ARG = 1,   /* bad pointer, size, dtype or shape       */
+    M1MOE_ERR_OUT_OF_MEMORY = 2, /* cudaMalloc / cudaHostAlloc failed        */
+    M1MOE_ERR_CUDA = 3,          /* any other CUDA runtime error             */
+    M1MOE_ERR_NOT_LOADED = 4,    /* layer weights or router not loaded yet   */
+    M1MOE_ERR_DEVICE = 5,        /* a kernel raised the context's error word */
+    M1MOE_ERR_UNSUPPORTED = 6    /* valid but unsupported shape (e.g. gs%32) */
+} m1moe_status;
+
+typedef enum m1moe_dtype {
+    M1MOE_DTYPE_F32 = 0,
+    M1MOE_DTYPE_BF16 = 1
+} m1moe_dtype;
+
+/* Dimensions of one MoE model; field meanings follow ModelSpec.swift
+ * (hiddenDim, MoESpec.intermediateDim/numExperts/topK/normTopkProb,
+ * QuantSpec.groupSize, numLayers). */
+typedef struct m1moe_cuda_cfg {
+    int32_t hidden_dim;
+    int32_t intermediate_dim;
+    int32_t num_experts;
+    int32_t top_k;
+    int32_t group_size;
+    int32_t num_layers;
+    int32_t norm_topk_prob;
+    int32_t max_batch;     /* tokens per call, 1..8                              */
+    int32_t device;        /* CUDA device ordinal                                */
+    int32_t expert_begin;  /* expert-parallel shard: first expert held here      */
+    int32_t expert_count;  /* experts held here; 0 = all num_experts             */
+} m1moe_cuda_cfg;
+
+typedef struct m1moe_cuda_ctx m1moe_cuda_ctx;
+
+/* ABI version of the loaded library (M1MOE_CUDA_ABI_VERSION at build time). */
+M1MOE_API int32_t m1moe_cuda_abi_version(void);
+
+/* Thread-local message for the last failed call on this thread ("" if none). */
+M1MOE_API const char *m1moe_cuda_last_error(void);
+
+/* Bytes of one packed expert block.  Replaces ModelSpec.expertBytes4Bit
+ * (ModelSpec.swift:36-52); 0 if the shape is invalid. */
+M1MOE_API size_t m1moe_cuda_expert_bytes(int32_t hidden_dim, int32_t intermediate_dim,
+                               int32_t group_size);
+
+/* Create a context on cfg->device: allocates the HBM expert table for every
+ * layer (the experts this shard holds), the router table and the per-call
+ * scratch.  Replaces the expert-slot and MoE buffers of MetalContext.swift
+ * :150-178 and the expert fds/offsets of InferenceEngine.init (:62-97). */
+M1MOE_API m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_ctx);
+
+/* Free everything the context owns.  NULL is accepted. */
+M1MOE_API m1moe_status m1moe_cuda_destroy(m1moe_cuda_ctx *ctx);
+
+/* Fill one layer of the HBM expert table from the exact bytes of
+ * packed_experts/layer_NN.bin (num_experts blocks back to back), copied through
+ * pinned host staging.  Only this shard's experts are kept.  Replaces the
+ * per-token pread of loadExpert (InferenceEngine.swift:271-280); the copy
+ * happens once, at cold start.  nbytes must equal num_experts*expert_bytes. */
+M1MOE_API m1moe_status m1moe_cuda_load_expert_layer(m1moe_cuda_ctx *ctx, int32_t layer,
+                                          const void *h_layer_bytes, size_t nbytes);
+
+/* Same as above from device memory (stream-ordered), for callers that already
+ * hold the layer image in HBM. */
+M1MOE_API m1moe_status m1moe_cuda_load_expert_layer_device(m1moe_cuda_ctx *ctx, int32_t layer,
+                                                 const void *d_layer_bytes, size_t nbytes,
+                                                 void *stream);
+
+/* Load one layer's router (mlp.gate.weight / block_sparse_moe.gate.weight,
+ * bf16 [num_experts][hidden_dim]).  Replaces the bf16->f32 router preconvert
+ * of InferenceEngine.init (:99-113); the table stays bf16 in HBM and is
+ * upcast exactly inside the kernel. */
+M1MOE_API m1moe_status m1moe_cuda_load_router(m1moe_cuda_ctx *ctx, int32_t layer,
+                                    const uint16_t *h_router_bf16, size_t count);
+
+/* Stateless int4 group-quantised matvec for `batch` tokens (1..8):
+ *   y[t][r] = sum_j (q[r][j]*S[r][j/gs] + B[r][j/gs]) * x[t][j]
+ * x is [batch][in_dim] (x_dtype), y is [batch][out_dim] (y_dtype).
+ * Replaces encode4BitMV + matvec4bit (InferenceEngine.swift:446-465,
+ * Shaders.metal:39-92).  Requires in_dim % 64 == 0, gs % 32 == 0,
+ * in_dim % gs == 0 and 16-byte-aligned d_w. */
+M1MOE_API m1moe_status m1moe_cuda_matvec4(const uint32_t *d_w, const uint16_t *d_scales,
+                                const uint16_t *d_biases, const void *d_x, int32_t x_dtype,
+                                void *d_y, int32_t y_dtype, int32_t out_dim, int32_t in_dim,
+                                int32_t group_size, int32_t batch, void *stream);
+
+/* The same matvec over `num_mats` matrices that sit `mat_stride_bytes` apart
+ * (e.g. the gate projection of every expert in a layer table), all applied to
+ * the same x:  y[m][t][r].  The expert table's experts are such a strided set. */
+M1MOE_API m1moe_status m1moe_cuda_matvec4_strided(const uint32_t *d_w, const uint16_t *d_scales,
+                                        const uint16_t *d_biases, int64_t mat_stride_bytes,
+                                        int32_t num_mats, const void *d_x, int32_t x_dtype,
+                                        void *d_y, int32_t y_dtype, int32_t out_dim,
+                                        int32_t in_dim, int32_t group_size, int32_t batch,
+                                        void *stream);
+
+/* Unpack nibbles to bytes: q[r][c] = (W[r][c/8] >> 4*(c%8)) & 0xF, the exact
+ * unpack the matvec uses (Shaders.metal:73-74).  For bit-exact checks. */
+M1MOE_API m1moe_status m1moe_cuda_unpack4(const uint32_t *d_w, uint8_t *d_q, int32_t rows,
+                                int32_t cols, void *stream);
+
+/* Router for `batch` tokens: scores = softmax(W_r x) and the top-K experts,
+ * descending, ties to the lower index, renormalised if norm_topk_prob.
+ * Replaces computeRouterScores + selectTopK (InferenceEngine.swift:490-519).
+ * d_scores_out [batch][num_experts] may be NULL. */
+M1MOE_API m1moe_status m1moe_cuda_router_topk(m1moe_cuda_ctx *ctx, int32_t layer, const void *d_x,
+                                    int32_t x_dtype, int32_t batch, int32_t *d_topk_idx,
+                                    float *d_topk_w, float *d_scores_out, void *stream);
+
+/* One MoE block for `batch` tokens (stream-ordered, device pointers):
+ *   out[t] = residual[t] + sum_{k ascending} w[t][k] * Expert_{idx[t][k]}(x[t])
+ * with Expert(x) = W_down (silu(W_gate x) * (W_up x)).  Replaces the MoE part of
+ * runLayer (InferenceEngine.swift:240-266): router, loadExpert x K, CMD3
+ * (encodeExpertForward x K, encodeMoECombine) and the copy-back.
+ * d_residual may be NULL (treated as zero).  Expert-parallel shards sum only
+ * the experts they hold; the caller reduces over shards.  d_topk_idx/d_topk_w
+ * ([batch][top_k]) may be NULL. */
+M1MOE_API m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *ctx, int32_t layer, const void *d_x,
+                                  int32_t x_dtype, const void *d_residual, int32_t res_dtype,
+                                  void *d_out, int32_t out_dtype, int32_t batch,
+                                  int32_t *d_topk_idx, float *d_topk_w, void *stream);
+
+/* Synchronous host-buffer form of m1moe_cuda_moe_layer with the reference's
+ * f32 buffers (buf_h_mid, buf_residual -> buf_moe_out, MetalContext.swift
+ * :134-152): copies in, runs, copies out and waits.  h_topk_* may be NULL. */
+M1MOE_API m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *ctx, int32_t layer,
+                                       const float *h_x, const float *h_residual,
+                                       float *h_out, int32_t batch, int32_t *h_topk_idx,
+                                       float *h_topk_w);
+
+/* Wait for all work of the context and report (then clear) its device error
+ * word: M1MOE_ERR_DEVICE if any kernel flagged an error since the last call. */
+M1MOE_API m1moe_status m1moe_cuda_synchronize(m1moe_cuda_ctx *ctx);
+
+/* Number of kernels this library has launched in the calling process. */
+M1MOE_API int64_t m1moe_cuda_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* M1MOE_CUDA_H */

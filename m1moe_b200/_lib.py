@@ -1,0 +1,88 @@
+"""ctypes binding of the C ABI declared in include/m1moe_cuda.h.
+
+The shared library is the product: there is no Python or CPU fallback.  If
+libm1moe_cuda.so is missing, importing the ops raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libm1moe_cuda.so"
+
+M1MOE_OK = 0
+STATUS_NAMES = {
+    0: "OK", 1: "INVALID_ARG", 2: "OUT_OF_MEMORY", 3: "CUDA", 4: "NOT_LOADED", 5: "DEVICE",
+    6: "UNSUPPORTED",
+}
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+
+
+class M1MoECudaError(RuntimeError):
+    """A C-ABI call returned a non-zero m1moe_status."""
+
+    def __init__(self, status: int, func: str, message: str):
+        self.status = status
+        super().__init__(f"{func}: M1MOE_ERR_{STATUS_NAMES.get(status, status)}: {message}")
+
+
+class Cfg(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "hidden_dim", "intermediate_dim", "num_experts", "top_k", "group_size", "num_layers",
+        "norm_topk_prob", "max_batch", "device", "expert_begin", "expert_count")]
+
+
+_lib = None
+
+# (name, restype, argtypes) for every entry point in include/m1moe_cuda.h.
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_SIGS = [
+    ("m1moe_cuda_abi_version", ctypes.c_int32, []),
+    ("m1moe_cuda_last_error", ctypes.c_char_p, []),
+    ("m1moe_cuda_expert_bytes", ctypes.c_size_t, [_i32, _i32, _i32]),
+    ("m1moe_cuda_create", ctypes.c_int, [ctypes.POINTER(Cfg), ctypes.POINTER(_vp)]),
+    ("m1moe_cuda_destroy", ctypes.c_int, [_vp]),
+    ("m1moe_cuda_load_expert_layer", ctypes.c_int, [_vp, _i32, _vp, ctypes.c_size_t]),
+    ("m1moe_cuda_load_expert_layer_device", ctypes.c_int, [_vp, _i32, _vp, ctypes.c_size_t, _vp]),
+    ("m1moe_cuda_load_router", ctypes.c_int, [_vp, _i32, _vp, ctypes.c_size_t]),
+    ("m1moe_cuda_matvec4", ctypes.c_int,
+     [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
+    ("m1moe_cuda_matvec4_strided", ctypes.c_int,
+     [_vp, _vp, _vp, ctypes.c_int64, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
+    ("m1moe_cuda_unpack4", ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
+    ("m1moe_cuda_router_topk", ctypes.c_int, [_vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
+    ("m1moe_cuda_moe_layer", ctypes.c_int,
+     [_vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp]),
+    ("m1moe_cuda_moe_layer_host", ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp]),
+    ("m1moe_cuda_synchronize", ctypes.c_int, [_vp]),
+    ("m1moe_cuda_launch_count", ctypes.c_int64, []),
+]
+
+
+def lib() -> ctypes.CDLL:
+    """Load libm1moe_cuda.so (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m m1moe_b200.build` "
+                "(m1moe_b200 has no CPU fallback)")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, res, args in _SIGS:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int, func: str) -> None:
+    if status != M1MOE_OK:
+        msg = lib().m1moe_cuda_last_error()
+        raise M1MoECudaError(status, func, msg.decode() if msg else "")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)

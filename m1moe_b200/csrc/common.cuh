@@ -1,0 +1,130 @@
+// common.cuh — device helpers shared by the int4 expert-FFN kernels (sm_100a).
+//
+// Weight format (the reference's, unchanged; scripts/extract_olmoe.py:20-38,
+// :145-150): a projection with `rows` outputs and `cols` inputs is
+//   W  uint32[rows][cols/8]   nibble b of word w is column 8w+b (low nibble first)
+//   S  bf16  [rows][cols/gs]  per-group scale
+//   B  bf16  [rows][cols/gs]  per-group bias
+// and dequantises as w = q*S + B (Shaders.metal:73-77).
+//
+// Arithmetic: a lane owns one 16-byte "chunk" = 4 words = 32 consecutive
+// columns, which lie inside one group because gs % 32 == 0.  Per chunk
+//   sum_j (q_j*s + b)*x_j = s * sum_j q_j*x_j + b * sum_j x_j
+// so the inner loop is one exact nibble->float conversion and one fp32 FMA
+// per weight; the scale/bias terms are applied once per chunk.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace m1 {
+
+constexpr int kWarp = 32;
+constexpr int kChunkCols = 32;  // columns per 16-byte weight chunk
+
+__device__ __forceinline__ float bf16_bits(uint32_t b16) { return __uint_as_float(b16 << 16); }
+
+// 16-byte streaming load of weights: read-only path, no L1 allocation
+// (each weight byte is used exactly once per call).
+__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint16_t ld_u16(const void *p) {
+    return __ldg(reinterpret_cast<const unsigned short *>(p));
+}
+
+// Exact nibble -> float: 2^23 + q has q in its low mantissa bits; subtracting
+// 2^23 is exact.  (A float with exponent 150 has ulp 1.)
+__device__ __forceinline__ float nib_to_f32(uint32_t word, int b) {
+    return __uint_as_float(0x4B000000u | ((word >> (4 * b)) & 0xFu)) - 8388608.0f;
+}
+
+// Q = sum_{j<32} q_j * x_j for one 16-byte chunk (exact q, fp32 FMA).
+__device__ __forceinline__ float dot_chunk(const uint4 w, const float (&x)[32]) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t u = ws[i];
+        a0 = fmaf(nib_to_f32(u, 0), x[8 * i + 0], a0);
+        a1 = fmaf(nib_to_f32(u, 1), x[8 * i + 1], a1);
+        a2 = fmaf(nib_to_f32(u, 2), x[8 * i + 2], a2);
+        a3 = fmaf(nib_to_f32(u, 3), x[8 * i + 3], a3);
+        a0 = fmaf(nib_to_f32(u, 4), x[8 * i + 4], a0);
+        a1 = fmaf(nib_to_f32(u, 5), x[8 * i + 5], a1);
+        a2 = fmaf(nib_to_f32(u, 6), x[8 * i + 6], a2);
+        a3 = fmaf(nib_to_f32(u, 7), x[8 * i + 7], a3);
+    }
+    return (a0 + a1) + (a2 + a3);
+}
+
+// Load 32 consecutive activations (f32 or bf16, selected at run time) into
+// registers as f32, and return their sum.
+__device__ __forceinline__ float load_x32(const void *xbase, int is_bf16, int col,
+                                          float (&x)[32]) {
+    if (is_bf16) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(
+            reinterpret_cast<const uint16_t *>(xbase) + col);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 v = __ldg(p + i);
+            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                x[8 * i + 2 * j] = __uint_as_float(vv[j] << 16);
+                x[8 * i + 2 * j + 1] = __uint_as_float(vv[j] & 0xFFFF0000u);
+            }
+        }
+    } else {
+        const float4 *p = reinterpret_cast<const float4 *>(
+            reinterpret_cast<const float *>(xbase) + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 v = __ldg(p + i);
+            x[4 * i + 0] = v.x;
+            x[4 * i + 1] = v.y;
+            x[4 * i + 2] = v.z;
+            x[4 * i + 3] = v.w;
+        }
+    }
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+        s0 += x[j];
+        s1 += x[j + 1];
+    }
+    return s0 + s1;
+}
+
+__device__ __forceinline__ float load_act(const void *base, int is_bf16, size_t i) {
+    if (is_bf16) return bf16_bits(ld_u16(reinterpret_cast<const uint16_t *>(base) + i));
+    return __ldg(reinterpret_cast<const float *>(base) + i);
+}
+
+__device__ __forceinline__ void store_act(void *base, int is_bf16, size_t i, float v) {
+    if (is_bf16)
+        reinterpret_cast<__nv_bfloat16 *>(base)[i] = __float2bfloat16_rn(v);
+    else
+        reinterpret_cast<float *>(base)[i] = v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Balanced contiguous split of `total` items over `parts`: [begin, end) of part p.
+__device__ __forceinline__ void split_range(long long total, int parts, int p, long long &b,
+                                            long long &e) {
+    b = total * p / parts;
+    e = total * (p + 1) / parts;
+}
+
+}  // namespace m1

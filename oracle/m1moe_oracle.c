@@ -1,0 +1,256 @@
+/*
+ * m1moe_oracle.c — CPU restatement of M1MoE's int4 expert-FFN arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY: the parity checker and the timed CPU baseline.
+ * The product (m1moe_b200) never links or calls it.  Each function cites the
+ * reference file:line it restates; see m1moe_oracle.h for the parity pin.
+ *
+ * Build: gcc -O3 -march=native -ffp-contract=off -fPIC -shared -pthread
+ * (-ffp-contract=off keeps every FMA exactly where the reference writes one).
+ */
+#include "m1moe_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+float orc_bf16_to_f32(uint16_t b) {
+    /* Shaders.metal:11-14: uint(b) << 16 reinterpreted as float. */
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+uint16_t orc_f32_to_bf16(float f) {
+    /* extract_olmoe.py:104-111: u32 + 0x7FFF + bit16, then >> 16. */
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    uint32_t rounding_bias = (u >> 16) & 1u;
+    return (uint16_t)((u + 0x7FFFu + rounding_bias) >> 16);
+}
+
+size_t orc_expert_bytes(int hidden, int inter, int gs) {
+    /* ModelSpec.swift:36-52. */
+    size_t h = (size_t)hidden, i = (size_t)inter;
+    size_t gw = i * (h / 8) * 4, gsb = i * (h / (size_t)gs) * 2;
+    size_t dw = h * (i / 8) * 4, dsb = h * (i / (size_t)gs) * 2;
+    return gw + gsb * 2 + gw + gsb * 2 + dw + dsb * 2;
+}
+
+void orc_expert_offsets(int hidden, int inter, int gs, size_t off[9]) {
+    /* InferenceEngine.swift:79-97. */
+    size_t h = (size_t)hidden, i = (size_t)inter;
+    size_t gw = i * (h / 8) * 4, gsb = i * (h / (size_t)gs) * 2;
+    size_t dw = h * (i / 8) * 4, dsb = h * (i / (size_t)gs) * 2;
+    off[0] = 0;              /* gateW */
+    off[1] = off[0] + gw;    /* gateS */
+    off[2] = off[1] + gsb;   /* gateB */
+    off[3] = off[2] + gsb;   /* upW   */
+    off[4] = off[3] + gw;    /* upS   */
+    off[5] = off[4] + gsb;   /* upB   */
+    off[6] = off[5] + gsb;   /* downW */
+    off[7] = off[6] + dw;    /* downS */
+    off[8] = off[7] + dsb;   /* downB */
+}
+
+#define ORC_TG 64 /* threads per threadgroup, InferenceEngine.swift:463-464 */
+
+void orc_matvec4bit_rows(const uint32_t *W, const uint16_t *S, const uint16_t *B,
+                         const float *x, float *y, int out_dim, int in_dim, int gs,
+                         int row0, int row1) {
+    /* Shaders.metal:39-92. */
+    const unsigned numWords = (unsigned)in_dim / 8;
+    const unsigned numGroups = (unsigned)in_dim / (unsigned)gs;
+    float shared[ORC_TG];
+    for (int row = row0; row < row1 && row < out_dim; ++row) {
+        const uint32_t *wRow = W + (size_t)row * numWords;
+        const uint16_t *sRow = S + (size_t)row * numGroups;
+        const uint16_t *bRow = B + (size_t)row * numGroups;
+        for (unsigned lid = 0; lid < ORC_TG; ++lid) {
+            float acc = 0.0f;
+            for (unsigned w = lid; w < numWords; w += ORC_TG) {
+                uint32_t packed = wRow[w];
+                unsigned g = (w * 8) / (unsigned)gs;
+                float scale = orc_bf16_to_f32(sRow[g]);
+                float bias = orc_bf16_to_f32(bRow[g]);
+                unsigned base = w * 8;
+                for (unsigned b = 0; b < 8; ++b) {
+                    float nibble = (float)((packed >> (b * 4)) & 0xFu);
+                    float xv = x[base + b];
+                    /* Shaders.metal:77 */
+                    acc = fmaf(nibble, scale * xv, fmaf(bias, xv, acc));
+                }
+            }
+            shared[lid] = acc;
+        }
+        /* Shaders.metal:86-90: tree reduction. */
+        for (unsigned s = ORC_TG / 2; s > 0; s >>= 1)
+            for (unsigned lid = 0; lid < s; ++lid) shared[lid] += shared[lid + s];
+        y[row] = shared[0];
+    }
+}
+
+void orc_matvec4bit(const uint32_t *W, const uint16_t *S, const uint16_t *B,
+                    const float *x, float *y, int out_dim, int in_dim, int gs) {
+    orc_matvec4bit_rows(W, S, B, x, y, out_dim, in_dim, gs, 0, out_dim);
+}
+
+typedef struct {
+    const uint32_t *W;
+    const uint16_t *S, *B;
+    const float *x;
+    float *y;
+    int out_dim, in_dim, gs, row0, row1;
+} orc_mv_job;
+
+static void *orc_mv_worker(void *p) {
+    orc_mv_job *j = (orc_mv_job *)p;
+    orc_matvec4bit_rows(j->W, j->S, j->B, j->x, j->y, j->out_dim, j->in_dim, j->gs, j->row0,
+                        j->row1);
+    return NULL;
+}
+
+void orc_matvec4bit_mt(const uint32_t *W, const uint16_t *S, const uint16_t *B,
+                       const float *x, float *y, int out_dim, int in_dim, int gs,
+                       int nthreads) {
+    /* The reference dispatches one threadgroup per row (InferenceEngine.swift:463);
+     * here rows are partitioned over host threads. */
+    if (nthreads <= 1 || out_dim < 2 * nthreads) {
+        orc_matvec4bit(W, S, B, x, y, out_dim, in_dim, gs);
+        return;
+    }
+    if (nthreads > 256) nthreads = 256;
+    pthread_t th[256];
+    orc_mv_job jobs[256];
+    int per = (out_dim + nthreads - 1) / nthreads;
+    int started = 0;
+    for (int t = 0; t < nthreads; ++t) {
+        jobs[t] = (orc_mv_job){W, S, B, x, y, out_dim, in_dim, gs, t * per,
+                               (t + 1) * per < out_dim ? (t + 1) * per : out_dim};
+        if (jobs[t].row0 >= jobs[t].row1) break;
+        if (pthread_create(&th[t], NULL, orc_mv_worker, &jobs[t]) != 0) {
+            orc_mv_worker(&jobs[t]); /* run inline if a thread cannot start */
+            continue;
+        }
+        th[started] = th[t];
+        ++started;
+    }
+    for (int t = 0; t < started; ++t) pthread_join(th[t], NULL);
+}
+
+void orc_swiglu(const float *gate, const float *up, float *act, int n) {
+    /* Shaders.metal:138-149 (the reference compiles with fastMath; this uses expf). */
+    for (int i = 0; i < n; ++i) {
+        float g = gate[i];
+        act[i] = (g / (1.0f + expf(-g))) * up[i];
+    }
+}
+
+void orc_moe_combine(const float *expert_outs, const float *w, const float *residual,
+                     float *out, int K, int h) {
+    /* Shaders.metal:360-376: residual first, then k ascending. */
+    for (int i = 0; i < h; ++i) {
+        float acc = residual[i];
+        for (int k = 0; k < K; ++k) acc += w[k] * expert_outs[(size_t)k * h + i];
+        out[i] = acc;
+    }
+}
+
+void orc_router_scores(const uint16_t *router_bf16, const float *x, int E, int h,
+                       float *scores) {
+    /* InferenceEngine.swift:490-508. */
+    for (int e = 0; e < E; ++e) {
+        float dot = 0.0f;
+        const uint16_t *row = router_bf16 + (size_t)e * h;
+        for (int d = 0; d < h; ++d) dot += orc_bf16_to_f32(row[d]) * x[d];
+        scores[e] = dot;
+    }
+    float mx = scores[0];
+    for (int e = 1; e < E; ++e)
+        if (scores[e] > mx) mx = scores[e];
+    float sum = 0.0f;
+    for (int e = 0; e < E; ++e) {
+        scores[e] = expf(scores[e] - mx);
+        sum += scores[e];
+    }
+    float inv = 1.0f / sum;
+    for (int e = 0; e < E; ++e) scores[e] *= inv;
+}
+
+void orc_select_topk(const float *scores, int E, int K, int norm, int32_t *idx, float *w) {
+    /* InferenceEngine.swift:510-519: selection of the K largest, descending,
+     * ties to the lower index (a stable descending sort prefix). */
+    unsigned char taken[4096];
+    memset(taken, 0, sizeof(taken));
+    for (int k = 0; k < K; ++k) {
+        int best = -1;
+        for (int e = 0; e < E; ++e) {
+            if (taken[e]) continue;
+            if (best < 0 || scores[e] > scores[best]) best = e;
+        }
+        taken[best] = 1;
+        idx[k] = best;
+        w[k] = scores[best];
+    }
+    if (norm) {
+        /* reduce(0) { $0 + $1.1 }: sum in selection order, then divide. */
+        float s = 0.0f;
+        for (int k = 0; k < K; ++k) s += w[k];
+        for (int k = 0; k < K; ++k) w[k] = w[k] / s;
+    }
+}
+
+static void orc_expert_forward_mt(const uint8_t *block, const float *x, int hidden, int inter,
+                                  int gs, float *y, float *scratch, int nthreads) {
+    /* InferenceEngine.swift:401-444. */
+    size_t off[9];
+    orc_expert_offsets(hidden, inter, gs, off);
+    float *gate = scratch, *up = scratch + inter, *act = scratch + 2 * (size_t)inter;
+    orc_matvec4bit_mt((const uint32_t *)(block + off[0]), (const uint16_t *)(block + off[1]),
+                      (const uint16_t *)(block + off[2]), x, gate, inter, hidden, gs, nthreads);
+    orc_matvec4bit_mt((const uint32_t *)(block + off[3]), (const uint16_t *)(block + off[4]),
+                      (const uint16_t *)(block + off[5]), x, up, inter, hidden, gs, nthreads);
+    orc_swiglu(gate, up, act, inter);
+    orc_matvec4bit_mt((const uint32_t *)(block + off[6]), (const uint16_t *)(block + off[7]),
+                      (const uint16_t *)(block + off[8]), act, y, hidden, inter, gs, nthreads);
+}
+
+void orc_expert_forward(const uint8_t *block, const float *x, int hidden, int inter, int gs,
+                        float *y, float *scratch) {
+    orc_expert_forward_mt(block, x, hidden, inter, gs, y, scratch, 1);
+}
+
+int orc_moe_layer(const uint8_t *table, const uint16_t *router_bf16, const float *h_mid,
+                  const float *residual, float *out, int B, int hidden, int inter, int E,
+                  int K, int gs, int norm, int32_t *idx, float *w, int nthreads) {
+    /* InferenceEngine.swift:240-266 (router, per-slot expert forward, combine). */
+    if (E <= 0 || E > 4096 || K <= 0 || K > E) return -1;
+    size_t eb = orc_expert_bytes(hidden, inter, gs);
+    float *scores = (float *)malloc(sizeof(float) * (size_t)E);
+    float *outs = (float *)malloc(sizeof(float) * (size_t)K * hidden);
+    float *scratch = (float *)malloc(sizeof(float) * 3 * (size_t)inter);
+    if (!scores || !outs || !scratch) {
+        free(scores);
+        free(outs);
+        free(scratch);
+        return -2;
+    }
+    for (int t = 0; t < B; ++t) {
+        const float *x = h_mid + (size_t)t * hidden;
+        orc_router_scores(router_bf16, x, E, hidden, scores);
+        orc_select_topk(scores, E, K, norm, idx + (size_t)t * K, w + (size_t)t * K);
+        for (int k = 0; k < K; ++k) {
+            const uint8_t *block = table + (size_t)idx[(size_t)t * K + k] * eb;
+            orc_expert_forward_mt(block, x, hidden, inter, gs, outs + (size_t)k * hidden,
+                                  scratch, nthreads);
+        }
+        orc_moe_combine(outs, w + (size_t)t * K, residual + (size_t)t * hidden,
+                        out + (size_t)t * hidden, K, hidden);
+    }
+    free(scores);
+    free(outs);
+    free(scratch);
+    return 0;
+}

@@ -1,0 +1,195 @@
+"""CUDA MoE block (router + top-K + SwiGLU experts + combine) vs the CPU oracle.
+
+Bars: expert indices equal wherever the oracle's K-th and (K+1)-th scores
+differ by more than 1e-5; routing weights within 1e-5 relative; outputs
+max |out - ref| <= 1e-3 * ||ref||_2 (fp32 accumulation).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_max_err
+from m1moe_b200 import synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+GAP = 1e-5
+
+
+def _bf16_dev(a: np.ndarray, dtype=torch.bfloat16) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda().view(torch.bfloat16)
+    return t if dtype == torch.bfloat16 else t.to(dtype)
+
+
+def _block(img, routers, *, h, I, E, K, norm, max_batch=8, expert_begin=0, expert_count=0):
+    from m1moe_b200 import MoEBlock
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, group_size=64,
+                   num_layers=len(routers), norm_topk_prob=norm, max_batch=max_batch,
+                   expert_begin=expert_begin, expert_count=expert_count)
+    for L, r in enumerate(routers):
+        blk.load_router(L, r)
+        blk.load_expert_layer(L, img[L] if isinstance(img, list) else img)
+    return blk
+
+
+def _check_routing(idx, w, ref_idx, ref_w, x_f32, router, K):
+    import oracle
+    for t in range(idx.shape[0]):
+        scores = oracle.router_scores(router, x_f32[t])
+        srt = np.sort(scores)[::-1]
+        if K < len(scores) and srt[K - 1] - srt[K] <= GAP:
+            continue  # near-tie at the selection boundary: order not defined
+        ok = [k for k in range(K) if k == 0 or srt[k - 1] - srt[k] > GAP]
+        assert set(idx[t].tolist()) == set(ref_idx[t].tolist()), t
+        for k in ok:
+            assert idx[t][k] == ref_idx[t][k], (t, k)
+        wd = dict(zip(idx[t].tolist(), w[t].tolist()))
+        rd = dict(zip(ref_idx[t].tolist(), ref_w[t].tolist()))
+        assert all(abs(wd[e] - rd[e]) <= 1e-5 * abs(rd[e]) + 1e-7 for e in rd), t
+
+
+def _run_case(oracle_lib, img, router, *, h, I, E, K, norm, B, xdt=torch.bfloat16,
+              odt=torch.float32, with_res=True, seed=0):
+    blk = _block([img], [router], h=h, I=I, E=E, K=K, norm=norm)
+    xb = synth.hidden_states(seed + 1, B, h)
+    rb = synth.hidden_states(seed + 2, B, h)
+    xf, rf = synth.bf16_to_f32(xb), synth.bf16_to_f32(rb)
+    out, idx, w = blk.forward(0, _bf16_dev(xb, xdt), _bf16_dev(rb, torch.float32) if with_res else None,
+                              out_dtype=odt, return_topk=True)
+    out = out.float().cpu().numpy()
+    idx, w = idx.cpu().numpy(), w.cpu().numpy()
+    ref, ridx, rw = oracle_lib.moe_layer(img, router, xf, rf if with_res else None, h=h, inter=I,
+                                         E=E, K=K, gs=64, norm=norm, nthreads=8)
+    _check_routing(idx, w, ridx, rw, xf, router, K)
+    for t in range(B):
+        if set(idx[t].tolist()) == set(ridx[t].tolist()):
+            assert rel_max_err(out[t], ref[t]) < TOL, t
+    blk.close()
+    return out, idx, w
+
+
+@pytest.mark.parametrize("name,K,norm", [("olmoe_tiny", 2, False), ("mixtral_tiny", 2, True),
+                                         ("olmoe_tiny", 4, True)])
+@pytest.mark.parametrize("B", [1, 2, 5, 8])
+def test_moe_layer_on_reference_extracted_layers(golden, oracle_lib, name, K, norm, B):
+    from golden.make_golden import router_weights
+    g = golden(name)
+    L, E, h, I, gs, seed = (int(v) for v in g["meta"])
+    _run_case(oracle_lib, g["layer_00"], router_weights(seed, L, E, h)[0], h=h, I=I, E=E, K=K,
+              norm=norm, B=B, seed=B)
+
+
+def _device_layer(E, h, I, seed):
+    return synth.layer_image_device(E, h, I, 64, seed=seed, device="cuda").cpu().numpy()
+
+
+@pytest.mark.parametrize("B", [1, 4, 8])
+def test_moe_layer_olmoe_shape(oracle_lib, B):
+    """Config 1: h 2048, 64 experts, top-8, I 1024, no renormalisation."""
+    h, I, E, K = 2048, 1024, 64, 8
+    img = _device_layer(E, h, I, 7)
+    _run_case(oracle_lib, img, synth.router_weights(8, E, h), h=h, I=I, E=E, K=K, norm=False, B=B,
+              seed=10 * B)
+
+
+@pytest.mark.parametrize("B", [1, 8])
+def test_moe_layer_mixtral_shape(oracle_lib, B):
+    """Config 3 decode: h 4096, 8 experts, top-2 renormalised, I 14336."""
+    h, I, E, K = 4096, 14336, 8, 2
+    img = _device_layer(E, h, I, 17)
+    _run_case(oracle_lib, img, synth.router_weights(18, E, h), h=h, I=I, E=E, K=K, norm=True, B=B,
+              seed=20 * B)
+
+
+@pytest.mark.parametrize("xdt,odt", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
+                                     (torch.float32, torch.bfloat16)])
+def test_moe_layer_dtypes_and_no_residual(golden, oracle_lib, xdt, odt):
+    from golden.make_golden import router_weights
+    g = golden("olmoe_tiny")
+    L, E, h, I, gs, seed = (int(v) for v in g["meta"])
+    _run_case(oracle_lib, g["layer_01"], router_weights(seed, L, E, h)[1], h=h, I=I, E=E, K=2,
+              norm=False, B=3, xdt=xdt, odt=odt, with_res=False, seed=3)
+
+
+def test_forward_host_matches_device_path(golden):
+    from golden.make_golden import router_weights
+    g = golden("olmoe_tiny")
+    L, E, h, I, gs, seed = (int(v) for v in g["meta"])
+    routers = router_weights(seed, L, E, h)
+    blk = _block([g["layer_00"], g["layer_01"]], routers, h=h, I=I, E=E, K=2, norm=False)
+    x = synth.bf16_to_f32(synth.hidden_states(1, 4, h))
+    r = synth.bf16_to_f32(synth.hidden_states(2, 4, h))
+    for layer in range(2):
+        oh, ih, wh = blk.forward_host(layer, x, r)
+        od, idd, wd = blk.forward(layer, torch.from_numpy(x).cuda(), torch.from_numpy(r).cuda(),
+                                  return_topk=True)
+        assert np.array_equal(oh, od.cpu().numpy())
+        assert np.array_equal(ih, idd.cpu().numpy()) and np.array_equal(wh, wd.cpu().numpy())
+    blk.close()
+
+
+def test_expert_parallel_shards_sum_to_full(golden):
+    """Shards holding experts [0,2) and [2,4) produce partial sums whose total
+    (residual added by one shard) equals the single-GPU result."""
+    from golden.make_golden import router_weights
+    g = golden("mixtral_tiny")
+    L, E, h, I, gs, seed = (int(v) for v in g["meta"])
+    router = router_weights(seed, L, E, h)[0]
+    full = _block([g["layer_00"]], [router], h=h, I=I, E=E, K=2, norm=True)
+    s0 = _block([g["layer_00"]], [router], h=h, I=I, E=E, K=2, norm=True, expert_begin=0,
+                expert_count=2)
+    s1 = _block([g["layer_00"]], [router], h=h, I=I, E=E, K=2, norm=True, expert_begin=2,
+                expert_count=2)
+    x = _bf16_dev(synth.hidden_states(4, 8, h))
+    r = _bf16_dev(synth.hidden_states(5, 8, h), torch.float32)
+    ref = full.forward(0, x, r)
+    p0 = s0.forward(0, x, r)
+    p1 = s1.forward(0, x, None)
+    tot = (p0 + p1).cpu().numpy()
+    for t in range(8):
+        assert rel_max_err(tot[t], ref[t].cpu().numpy()) < 1e-5
+    for b in (full, s0, s1):
+        b.close()
+
+
+def test_router_topk_ties_lowest_index():
+    """Identical router rows give exactly tied scores; the lower index wins."""
+    from m1moe_b200 import MoEBlock
+    h, E, K = 128, 8, 3
+    router = synth.router_weights(1, E, h)
+    router[5] = router[2]
+    router[7] = router[2]
+    x = synth.hidden_states(2, 1, h)
+    xf = synth.bf16_to_f32(x)[0]
+    logits = synth.bf16_to_f32(router).astype(np.float64) @ xf
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=64, num_experts=E, top_k=K, num_layers=1)
+    blk.load_router(0, router)
+    idx, w, scores = blk.route(0, _bf16_dev(x))
+    idx = idx.cpu().numpy()[0]
+    tied = [e for e in idx.tolist() if e in (2, 5, 7)]
+    assert tied == sorted(tied)  # equal scores leave in ascending expert order
+    assert logits[2] == logits[5] == logits[7]
+    assert scores.cpu().numpy()[0][2] == scores.cpu().numpy()[0][5] == scores.cpu().numpy()[0][7]
+    # all-equal scores: the K lowest indices, ascending
+    blk2 = MoEBlock(hidden_dim=h, intermediate_dim=64, num_experts=E, top_k=K, num_layers=1)
+    blk2.load_router(0, np.tile(router[0], (E, 1)))
+    idx2, w2, _ = blk2.route(0, _bf16_dev(x))
+    assert idx2.cpu().numpy()[0].tolist() == [0, 1, 2]
+    assert np.allclose(w2.cpu().numpy(), 1.0 / E)
+    blk.close()
+    blk2.close()
+
+
+def test_moe_layer_not_loaded_is_an_error():
+    from m1moe_b200 import M1MoECudaError, MoEBlock
+    blk = MoEBlock(hidden_dim=128, intermediate_dim=64, num_experts=4, top_k=2, num_layers=2)
+    x = torch.zeros((1, 128), device="cuda")
+    with pytest.raises(M1MoECudaError, match="NOT_LOADED"):
+        blk.forward(0, x)
+    with pytest.raises(M1MoECudaError, match="INVALID_ARG"):
+        blk.forward(2, x)
+    with pytest.raises(M1MoECudaError, match="INVALID_ARG"):
+        blk.load_expert_layer(0, np.zeros(10, np.uint8))
+    blk.close()

@@ -182,6 +182,17 @@ M1MOE_API m1moe_status m1moe_cuda_synchronize(m1moe_cuda_ctx *ctx);
 /* Number of kernels this library has launched in the calling process. */
 M1MOE_API int64_t m1moe_cuda_launch_count(void);
 
+/* Phase tracing (the reference only has wall-clock timing, bench/main.swift
+ * :51-54).  With a non-NULL device buffer of 3 x 160 x 8 uint64, every MoE
+ * call made afterwards records the GPU's global nanosecond timer per kernel
+ * (router, gate/up, down), per CTA (first 160) and per phase event; NULL turns
+ * tracing off (the default).  Events: router 0 start, 1 predecessor done,
+ * 2 router rows landed, 3 logits done, 4 route done (last CTA); gate/up
+ * 0 start, 1 predecessor done, 2 route and x staged, 3 all tiles issued,
+ * 4 first tile landed, 5 all work items done, 6 end; down 0 start, 1 route
+ * read, 2 all tiles issued, 3 gate/up done, 4 all work items done, 5 end. */
+M1MOE_API m1moe_status m1moe_cuda_set_trace(m1moe_cuda_ctx *ctx, uint64_t *d_trace);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,7 @@ _SIGS = [
     ("m1moe_cuda_moe_layer_host", ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp]),
     ("m1moe_cuda_synchronize", ctypes.c_int, [_vp]),
     ("m1moe_cuda_launch_count", ctypes.c_int64, []),
+    ("m1moe_cuda_set_trace", ctypes.c_int, [_vp, _vp]),
 ]
 
 

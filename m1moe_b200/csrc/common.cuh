@@ -120,6 +120,134 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Reduce N values (N a power of two, 1..32) over the lanes of a warp with
+// N-1 + log2(32/N) shuffles instead of 5N: each stage exchanges half of the
+// remaining values.  Afterwards lane l holds, in v[0], the warp total of value
+// l / (32/N).
+template <int N>
+__device__ __forceinline__ float warp_reduce_multi(float (&v)[N]) {
+    static_assert(N >= 1 && N <= 32 && (N & (N - 1)) == 0, "N must be a power of two <= 32");
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int st = 0; st < 5; ++st) {
+        const int o = 16 >> st;
+        if ((N >> st) > 1) {
+            const int half = N >> (st + 1);
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (i < half) {
+                    const float send = up ? v[i] : v[i + half];
+                    const float keep = up ? v[i + half] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+        }
+    }
+    return v[0];
+}
+
+// ---------------------------------------------------------------------------
+// bf16 inner loop (the decode hot path).
+//
+// Weights: one 32-bit word holds 8 nibbles q0..q7 (columns 8w..8w+7).  A single
+// LOP3 turns nibbles k and k+4 into the bf16 pair (128+q_k, 128+q_{k+4}):
+// 0x4300 is bf16 128.0, whose mantissa ulp is 1, so OR-ing q into the low
+// mantissa bits is exact.  Activations are bf16 pairs (x_k, x_{k+4}) in the
+// same order ("pair-permuted").  fma.rn.f32.bf16 multiplies two bf16 values
+// exactly into fp32 and accumulates in fp32, so per chunk
+//     A = sum_j (128 + q_j) * x_j = 128*X + Q,   X = sum_j x_j,
+// and the projection row accumulates  s*A + (b - 128*s)*X.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t q_pair(uint32_t word, int k) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;"  // (a & b) | c
+        : "=r"(d)
+        : "r"(word >> (4 * k)), "r"(0x000F000Fu), "r"(0x43004300u));
+    return d;
+}
+
+// acc + a.lo*b.lo + a.hi*b.hi, exact bf16 products, fp32 accumulation.
+__device__ __forceinline__ float fma_pair(uint32_t a, uint32_t b, float acc) {
+    float d;
+    asm("{ .reg .b16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %1;\n\t"
+        "mov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, al, bl, %3;\n\t"
+        "fma.rn.f32.bf16 %0, ah, bh, %0; }"
+        : "=f"(d)
+        : "r"(a), "r"(b), "f"(acc));
+    return d;
+}
+
+// A = sum_j (128 + q_j) x_j over one 16-byte weight chunk; xp holds the
+// chunk's 16 pair-permuted bf16 pairs (word i, pair k at xp[4*i + k]).
+__device__ __forceinline__ float dot_chunk_bf16(const uint4 w, const uint32_t (&xp)[16]) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        a0 = fma_pair(q_pair(w.x, k), xp[0 + k], a0);
+        a1 = fma_pair(q_pair(w.y, k), xp[4 + k], a1);
+        a2 = fma_pair(q_pair(w.z, k), xp[8 + k], a2);
+        a3 = fma_pair(q_pair(w.w, k), xp[12 + k], a3);
+    }
+    return (a0 + a1) + (a2 + a3);
+}
+
+// Pair-permuted chunk-transposed bf16 activation layout.  A vector of
+// n = 32*nch values is stored as nch chunks of 32; chunk c holds 4 words x 4
+// pairs; pair (i, k) of chunk c is the 32-bit element (i*nch + c)*4 + k and
+// holds (v[32c+8i+k], v[32c+8i+k+4]).  A warp whose lane L reads chunk L for
+// fixed i loads 512 contiguous bytes.  Returns the bf16 element index of v[j].
+__device__ __forceinline__ int ppos(int j, int nch) {
+    const int c = j >> 5, rem = j & 31, i = rem >> 3, r8 = rem & 7;
+    return ((((i * nch + c) << 2) + (r8 & 3)) << 1) + (r8 >> 2);
+}
+
+// The 16 pairs of chunk c (read-only cached loads).
+__device__ __forceinline__ void load_pairs(const uint16_t *vT, int nch, int c, uint32_t (&xp)[16]) {
+    const uint4 *p = reinterpret_cast<const uint4 *>(vT);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 v = __ldg(p + (size_t)i * nch + c);
+        xp[4 * i + 0] = v.x;
+        xp[4 * i + 1] = v.y;
+        xp[4 * i + 2] = v.z;
+        xp[4 * i + 3] = v.w;
+    }
+}
+
+// As load_pairs, through a generic pointer (shared or global memory).
+__device__ __forceinline__ void load_pairs_any(const uint16_t *vT, int nch, int c,
+                                               uint32_t (&xp)[16]) {
+    const uint4 *p = reinterpret_cast<const uint4 *>(vT);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 v = p[(size_t)i * nch + c];
+        xp[4 * i + 0] = v.x;
+        xp[4 * i + 1] = v.y;
+        xp[4 * i + 2] = v.z;
+        xp[4 * i + 3] = v.w;
+    }
+}
+
+// Sum of the 32 bf16 values of a chunk, in fp32.
+__device__ __forceinline__ float pair_sum(const uint32_t (&xp)[16]) {
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        s0 += __uint_as_float(xp[i] << 16);
+        s1 += __uint_as_float(xp[i] & 0xFFFF0000u);
+    }
+    return s0 + s1;
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16_rn(float v) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
 // Balanced contiguous split of `total` items over `parts`: [begin, end) of part p.
 __device__ __forceinline__ void split_range(long long total, int parts, int p, long long &b,
                                             long long &e) {

@@ -19,6 +19,7 @@
 #include "common.cuh"
 #include "matvec4.cuh"
 #include "moe_decode.cuh"
+#include "pipeline.cuh"
 
 namespace {
 
@@ -102,9 +103,13 @@ struct m1moe_cuda_ctx {
     uint16_t *router = nullptr;   // [layers][E][h]
     std::vector<uint8_t> layer_loaded, router_loaded;
     float *logits = nullptr;      // [max_batch][E]
-    int *route_idx = nullptr;     // [max_batch][K]
-    float *route_w = nullptr;     // [max_batch][K]
-    float *act = nullptr;         // [max_batch*K][I]
+    uint16_t *xT = nullptr;       // [max_batch][h] bf16, pair-permuted chunk-transposed
+    float *xsum = nullptr;        // [max_batch][h/32]
+    uint16_t *actT = nullptr;     // [max_batch*K][I] bf16, pair-permuted chunk-transposed
+    int *err = nullptr;           // device error word (pipeline.cuh kErr*)
+    m1::RouteInfo *route = nullptr;  // routing decision of the current call
+    int *ticket = nullptr;        // router grid's last-CTA ticket
+    unsigned long long *trace = nullptr;  // optional phase timestamps (caller-owned)
     // synchronous host-buffer path
     float *hx = nullptr, *hres = nullptr, *hout = nullptr;
     int *hidx = nullptr;
@@ -135,9 +140,12 @@ void free_ctx(m1moe_cuda_ctx *c) {
     cudaFree(c->table);
     cudaFree(c->router);
     cudaFree(c->logits);
-    cudaFree(c->route_idx);
-    cudaFree(c->route_w);
-    cudaFree(c->act);
+    cudaFree(c->xT);
+    cudaFree(c->xsum);
+    cudaFree(c->actT);
+    cudaFree(c->err);
+    cudaFree(c->route);
+    cudaFree(c->ticket);
     cudaFree(c->hx);
     cudaFree(c->hres);
     cudaFree(c->hout);
@@ -168,38 +176,124 @@ m1::MoeParams moe_params(m1moe_cuda_ctx *c, int layer, int B) {
     p.ne = c->ne;
     p.ntok = B;
     p.logits = c->logits;
-    p.route_idx = c->route_idx;
-    p.route_w = c->route_w;
-    p.act = c->act;
+    p.xT = c->xT;
+    p.xsum = c->xsum;
+    p.actT = c->actT;
+    p.err = c->err;
+    p.route = c->route;
+    p.ticket = c->ticket;
+    p.trace = c->trace;
     return p;
 }
 
+// Shared-memory pipeline geometry.  A gate/up CTA and a down CTA are sized to
+// be resident on one SM together (so the down grid can prefetch while gate/up
+// runs): rings of ~100 KB and ~88 KB.
+struct Geometry {
+    int grid, router_grid;
+    size_t gu_smem, dn_smem, router_smem;
+};
+
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+constexpr size_t kMaxDynSmem = 227 * 1024;  // per-CTA opt-in limit on sm_100
+
+// Pipeline geometry for a batch of NT (template) tokens; rt_gu / rt_dn are the
+// kernels' rows per tile (TileRows<NT>).  Each ring gets the shared memory left
+// after the kernel's fixed parts.
+Geometry plan_geometry(m1::MoeParams &p, int num_sms, int nt, int rt_gu, int rt_dn) {
+    Geometry g{};
+    g.grid = num_sms;
+    const int srb_h = (p.h / p.gs) * 2, srb_i = (p.I / p.gs) * 2;
+    const int nch = p.h / m1::kChunkCols, nchI = p.I / m1::kChunkCols;
+    const int maxU = std::min(p.ntok * p.K, p.ne);
+    // ---- gate/up: tile = rt rows of gate and of up, each W + S span + B span
+    // (a span rounded out to 16 bytes adds at most 32 bytes).
+    const int pair_bytes = 2 * (p.h / 2) + 4 * srb_h;
+    p.gu_stage_bytes = round_up(rt_gu * pair_bytes + 4 * 32, 128);
+    p.gu_nslices = nt <= 2 ? (nch + 31) / 32 : 1;
+    const long long gu_units = (long long)maxU * (p.I / rt_gu);
+    p.gu_rows_max = (int)((gu_units + g.grid - 1) / g.grid) * rt_gu;
+    p.x_smem = (size_t)nt * p.h * 2 <= 32 * 1024;
+    size_t gu_fixed = sizeof(m1::Ctl) + 16;
+    if (p.x_smem) gu_fixed += (size_t)nt * p.h * 2 + (size_t)nt * nch * 4;
+    if (p.gu_nslices > 1) gu_fixed += (size_t)p.gu_rows_max * p.gu_nslices * 2 * nt * 4;
+    p.gu_nstages = (int)std::min<size_t>(
+        m1::kMaxStages, (kMaxDynSmem - gu_fixed) / (p.gu_stage_bytes + 2 * sizeof(uint64_t)));
+    g.gu_smem = (size_t)p.gu_nstages * (p.gu_stage_bytes + 2 * sizeof(uint64_t)) + gu_fixed;
+    // ---- down: tile = up to rt rows of down of one expert
+    const int row_bytes = p.I / 2 + 2 * srb_i;
+    p.dn_stage_bytes = round_up(rt_dn * row_bytes + 2 * 32, 128);
+    p.dn_nslices = nt <= 2 ? (nchI + 31) / 32 : 1;
+    p.dn_rows_max = (p.h + g.grid - 1) / g.grid;
+    const size_t dn_fixed = sizeof(m1::Ctl) + 16 +
+                            (size_t)p.ntok * p.K * p.dn_rows_max * p.dn_nslices * sizeof(float);
+    p.dn_nstages = (int)std::min<size_t>(
+        m1::kMaxStages, (kMaxDynSmem - dn_fixed) / (p.dn_stage_bytes + 2 * sizeof(uint64_t)));
+    g.dn_smem = (size_t)p.dn_nstages * (p.dn_stage_bytes + 2 * sizeof(uint64_t)) + dn_fixed;
+    // ---- router
+    g.router_grid = std::min(num_sms, std::max(p.E, 1));
+    const int per = (p.E + g.router_grid - 1) / g.router_grid;
+    g.router_smem = (size_t)per * p.h * 2 + 16 + 8 * m1::kMaxTok * sizeof(float);
+    return g;
+}
+
+template <typename Kern>
+cudaError_t allow_smem(Kern kern, size_t bytes) {
+    // Idempotent; called before every launch so each instantiation is covered.
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// Launch with Programmatic Dependent Launch enabled: the kernel may start while
+// its stream predecessor is still running; griddepcontrol.wait inside the
+// kernel orders it after the predecessor's completion.
+template <typename Kern>
+cudaError_t launch_pdl(Kern kern, int grid, int block, size_t smem, cudaStream_t st,
+                       const m1::MoeParams &p) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+#define M1_TRY_LAUNCH(expr)                                      \
+    do {                                                         \
+        cudaError_t e_ = (expr);                                 \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #expr);      \
+        g_launches.fetch_add(1, std::memory_order_relaxed);      \
+    } while (0)
+
+// route_only: router + routing (no expert work), for m1moe_cuda_router_topk.
 template <int NT>
-m1moe_status launch_router(const m1::MoeParams &p, cudaStream_t st) {
-    m1::k_router_logits<NT><<<(p.E + 7) / 8, 256, 0, st>>>(p);
-    M1_LAUNCHED();
+m1moe_status launch_moe(m1moe_cuda_ctx *c, m1::MoeParams p, cudaStream_t st, bool route_only) {
+    Geometry g = plan_geometry(p, c->num_sms, NT, m1::TileRows<NT>::gu, m1::TileRows<NT>::dn);
+    if (g.gu_smem > kMaxDynSmem || g.dn_smem > kMaxDynSmem || p.gu_nstages < 2 || p.dn_nstages < 2)
+        return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
+    M1_CK(allow_smem(m1::k_router<NT>, g.router_smem));
+    M1_TRY_LAUNCH(launch_pdl(m1::k_router<NT>, g.router_grid, m1::kRouterThreads, g.router_smem,
+                             st, p));
+    if (route_only) return M1MOE_OK;  // the router grid's last CTA wrote the outputs
+    M1_CK(allow_smem(m1::k_moe_gateup<NT>, g.gu_smem));
+    M1_TRY_LAUNCH(launch_pdl(m1::k_moe_gateup<NT>, g.grid, m1::kPipeThreads, g.gu_smem, st, p));
+    M1_CK(allow_smem(m1::k_moe_down<NT>, g.dn_smem));
+    M1_TRY_LAUNCH(launch_pdl(m1::k_moe_down<NT>, g.grid, m1::kPipeThreads, g.dn_smem, st, p));
     return M1MOE_OK;
 }
 
-template <int NT>
-m1moe_status launch_moe(m1moe_cuda_ctx *c, const m1::MoeParams &p, cudaStream_t st) {
-    // Down: 2 rows per warp in 4-warp CTAs so that h = 2048 rows spread over
-    // 256 CTAs (>= one per SM).
-    constexpr int RG = 2, RD = 2, DOWN_THREADS = 128;
-    m1::k_router_logits<NT><<<(p.E + 7) / 8, 256, 0, st>>>(p);
-    M1_LAUNCHED();
-    // Upper bound on distinct local experts this call can touch.
-    const int maxU = std::min(p.ntok * p.K, p.ne);
-    const long long gu_groups = (long long)maxU * (p.I / RG);
-    int grid_gu = (int)std::min<long long>((gu_groups + 7) / 8, 2LL * c->num_sms);
-    m1::k_moe_gateup<NT, RG><<<std::max(grid_gu, 1), 256, 0, st>>>(p);
-    M1_LAUNCHED();
-    const long long d_groups = (p.h + RD - 1) / RD;
-    const int dwarps = DOWN_THREADS / 32;
-    int grid_d = (int)std::min<long long>((d_groups + dwarps - 1) / dwarps, 4LL * c->num_sms);
-    m1::k_moe_down<NT, RD><<<std::max(grid_d, 1), DOWN_THREADS, 0, st>>>(p);
-    M1_LAUNCHED();
-    return M1MOE_OK;
+m1moe_status dispatch_moe(m1moe_cuda_ctx *c, const m1::MoeParams &p, cudaStream_t st,
+                          bool route_only) {
+    if (p.ntok == 1) return launch_moe<1>(c, p, st, route_only);
+    if (p.ntok == 2) return launch_moe<2>(c, p, st, route_only);
+    if (p.ntok <= 4) return launch_moe<4>(c, p, st, route_only);
+    return launch_moe<8>(c, p, st, route_only);
 }
 
 m1moe_status check_layer(m1moe_cuda_ctx *c, int32_t layer) {
@@ -218,6 +312,12 @@ int32_t m1moe_cuda_abi_version(void) { return M1MOE_CUDA_ABI_VERSION; }
 const char *m1moe_cuda_last_error(void) { return g_last_error.c_str(); }
 
 int64_t m1moe_cuda_launch_count(void) { return g_launches.load(); }
+
+m1moe_status m1moe_cuda_set_trace(m1moe_cuda_ctx *c, uint64_t *d_trace) {
+    if (!c) return fail(M1MOE_ERR_INVALID_ARG, "ctx is NULL");
+    c->trace = reinterpret_cast<unsigned long long *>(d_trace);
+    return M1MOE_OK;
+}
 
 size_t m1moe_cuda_expert_bytes(int32_t h, int32_t I, int32_t gs) {
     if (h <= 0 || I <= 0 || gs <= 0 || h % gs || I % gs || h % 8 || I % 8) return 0;
@@ -274,18 +374,30 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
         free_ctx(c);                                                \
         return st_;                                                 \
     }
-    M1_ALLOC(c->table, (size_t)g.num_layers * ne * c->expert_bytes);
+    // +64: tile copies round scale/bias ranges out to 16-byte boundaries and
+    // may read up to 15 bytes past the last array of the last expert.
+    M1_ALLOC(c->table, (size_t)g.num_layers * ne * c->expert_bytes + 64);
     M1_ALLOC(c->router, (size_t)g.num_layers * E * g.hidden_dim * 2);
     M1_ALLOC(c->logits, B * E * 4);
-    M1_ALLOC(c->route_idx, B * K * 4);
-    M1_ALLOC(c->route_w, B * K * 4);
-    M1_ALLOC(c->act, B * K * g.intermediate_dim * 4);
+    M1_ALLOC(c->xT, B * g.hidden_dim * 2);
+    M1_ALLOC(c->xsum, B * (g.hidden_dim / 32) * 4);
+    M1_ALLOC(c->actT, B * K * g.intermediate_dim * 2);
+    M1_ALLOC(c->err, 4);
+    M1_ALLOC(c->route, sizeof(m1::RouteInfo));
+    M1_ALLOC(c->ticket, 4);
     M1_ALLOC(c->hx, B * g.hidden_dim * 4);
     M1_ALLOC(c->hres, B * g.hidden_dim * 4);
     M1_ALLOC(c->hout, B * g.hidden_dim * 4);
     M1_ALLOC(c->hidx, B * K * 4);
     M1_ALLOC(c->hw, B * K * 4);
 #undef M1_ALLOC
+    e = cudaMemset(c->err, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(c->ticket, 0, 4);
+    if (e != cudaSuccess) {
+        m1moe_status st = cuda_fail(e, "cudaMemset err");
+        free_ctx(c);
+        return st;
+    }
     e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         m1moe_status st = cuda_fail(e, "cudaStreamCreate");
@@ -454,23 +566,7 @@ m1moe_status m1moe_cuda_router_topk(m1moe_cuda_ctx *c, int32_t layer, const void
     p.user_idx = d_idx;
     p.user_w = d_w;
     p.user_scores = d_scores;
-    // Route only: the gate/up kernel with zero distinct-expert work would still
-    // need an expert table, so a shard-free copy of the params with ne = 0
-    // makes every expert non-local and the kernel stops after routing.
-    p.ne = 0;
-    cudaStream_t st = as_stream(stream);
-    m1moe_status s;
-    if (B == 1) s = launch_router<1>(p, st);
-    else if (B == 2) s = launch_router<2>(p, st);
-    else if (B <= 4) s = launch_router<4>(p, st);
-    else s = launch_router<8>(p, st);
-    if (s) return s;
-    if (B == 1) m1::k_moe_gateup<1, 2><<<1, 256, 0, st>>>(p);
-    else if (B == 2) m1::k_moe_gateup<2, 2><<<1, 256, 0, st>>>(p);
-    else if (B <= 4) m1::k_moe_gateup<4, 2><<<1, 256, 0, st>>>(p);
-    else m1::k_moe_gateup<8, 2><<<1, 256, 0, st>>>(p);
-    M1_LAUNCHED();
-    return M1MOE_OK;
+    return dispatch_moe(c, p, as_stream(stream), true);
 }
 
 m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *d_x,
@@ -497,11 +593,7 @@ m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *
     p.out_bf16 = out_dtype == M1MOE_DTYPE_BF16;
     p.user_idx = d_idx;
     p.user_w = d_w;
-    cudaStream_t st = as_stream(stream);
-    if (B == 1) return launch_moe<1>(c, p, st);
-    if (B == 2) return launch_moe<2>(c, p, st);
-    if (B <= 4) return launch_moe<4>(c, p, st);
-    return launch_moe<8>(c, p, st);
+    return dispatch_moe(c, p, as_stream(stream), false);
 }
 
 m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *c, int32_t layer, const float *h_x,
@@ -530,6 +622,12 @@ m1moe_status m1moe_cuda_synchronize(m1moe_cuda_ctx *c) {
     if (!c) return fail(M1MOE_ERR_INVALID_ARG, "ctx is NULL");
     DeviceGuard dg(c->cfg.device);
     M1_CK(cudaDeviceSynchronize());
+    int word = 0;
+    M1_CK(cudaMemcpy(&word, c->err, 4, cudaMemcpyDeviceToHost));
+    if (word) {
+        M1_CK(cudaMemset(c->err, 0, 4));
+        return fail(M1MOE_ERR_DEVICE, "device error word 0x%x (1: pipeline wait timed out)", word);
+    }
     return M1MOE_OK;
 }
 

@@ -1,0 +1,127 @@
+// pipeline.cuh — sm_100a primitives for the shared-memory weight pipelines:
+// 1-D bulk async copies (cp.async.bulk, the TMA engine's linear mode) that
+// complete on an mbarrier, bounded mbarrier waits, L2 eviction hints and
+// Programmatic Dependent Launch (griddepcontrol).
+//
+// No cluster multicast is used anywhere: every CTA fetches its own tiles from
+// this GPU's memory.
+#pragma once
+
+#include <stdint.h>
+
+namespace m1 {
+
+// Device error word bits (m1moe_cuda_synchronize reports them as M1MOE_ERR_DEVICE).
+constexpr int kErrWaitTimeout = 1;   // an mbarrier wait exceeded its iteration limit
+constexpr int kErrBadExpert = 2;     // a routed expert index was out of range
+
+// A wait gives up after this many try_wait polls (each poll may suspend the
+// thread for a hardware-defined interval), i.e. far longer than any copy.
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+// Make mbarrier initialisation visible to the async (bulk-copy) proxy.
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+        "selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.  On timeout
+// the CTA's abort flag and the device error word are set and false returned;
+// callers then stop consuming and unwind.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                          int *err) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+    }
+    *abort = 1;
+    if (err) atomicOr(err, kErrWaitTimeout);
+    return false;
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Linear bulk copy global -> this CTA's shared memory; completes `bytes` of
+// transaction count on `bar`.  dst, src 16-byte aligned; bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+// Programmatic Dependent Launch: wait until the preceding grid in the stream
+// has completed and its memory is visible (a no-op without a PDL predecessor);
+// allow the following grid to start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Phase tracing: when `trace` is non-null, slot [kernel][cta][event] receives
+// the global nanosecond timer (off by default; m1moe_cuda_set_trace).
+constexpr int kTraceEvents = 8;
+constexpr int kTraceCtas = 160;
+__device__ __forceinline__ void trace_event(unsigned long long *trace, int kernel, int event) {
+    if (trace == nullptr) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (blockIdx.x < kTraceCtas)
+        trace[((size_t)kernel * kTraceCtas + blockIdx.x) * kTraceEvents + event] = t;
+}
+
+// Named barrier over the first `nthreads` threads (a multiple of 32).
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// A [begin, end) byte range rounded out to 16-byte boundaries for a bulk copy;
+// `skew` is the offset of the wanted bytes inside the copied range.
+struct Span16 {
+    const uint8_t *src;
+    uint32_t bytes;
+    uint32_t skew;
+};
+
+__device__ __forceinline__ Span16 span16(const uint8_t *p, size_t n) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uintptr_t a0 = a & ~uintptr_t(15), a1 = (a + n + 15) & ~uintptr_t(15);
+    return {reinterpret_cast<const uint8_t *>(a0), static_cast<uint32_t>(a1 - a0),
+            static_cast<uint32_t>(a - a0)};
+}
+
+}  // namespace m1

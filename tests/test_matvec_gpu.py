@@ -63,7 +63,13 @@ def test_matvec_vs_oracle(oracle_lib, out_dim, in_dim, batch):
             y = matvec4(_dev(W), _dev(S), _dev(B), _x_dev(xb, xdt), out_dtype=ydt)
             yc = y.float().cpu().numpy()
             for t in range(batch):
-                assert rel_max_err(yc[t], refs[t]) < TOL, (xdt, ydt, t)
+                if ydt == torch.bfloat16:
+                    # bf16 output: the arithmetic bar plus the output's own rounding
+                    # (half an ulp, 2^-9 relative, of each element).
+                    bound = TOL * np.linalg.norm(refs[t]) + 2.0 ** -8 * np.abs(refs[t])
+                    assert np.all(np.abs(yc[t] - refs[t]) <= bound), (xdt, ydt, t)
+                else:
+                    assert rel_max_err(yc[t], refs[t]) < TOL, (xdt, ydt, t)
 
 
 def test_matvec_group_size_128(oracle_lib):

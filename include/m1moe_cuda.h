@@ -183,14 +183,16 @@ M1MOE_API m1moe_status m1moe_cuda_synchronize(m1moe_cuda_ctx *ctx);
 M1MOE_API int64_t m1moe_cuda_launch_count(void);
 
 /* Phase tracing (the reference only has wall-clock timing, bench/main.swift
- * :51-54).  With a non-NULL device buffer of 3 x 160 x 8 uint64, every MoE
- * call made afterwards records the GPU's global nanosecond timer per kernel
- * (router, gate/up, down), per CTA (first 160) and per phase event; NULL turns
- * tracing off (the default).  Events: router 0 start, 1 predecessor done,
- * 2 router rows landed, 3 logits done, 4 route done (last CTA); gate/up
- * 0 start, 1 predecessor done, 2 route and x staged, 3 all tiles issued,
- * 4 first tile landed, 5 all work items done, 6 end; down 0 start, 1 route
- * read, 2 all tiles issued, 3 gate/up done, 4 all work items done, 5 end. */
+ * :51-54).  With a non-NULL device buffer of 160 x 24 uint64, every MoE call
+ * made afterwards records, per CTA (first 160), the SM cycle counter at each
+ * phase event in slots 0-19 and the global nanosecond timer at events 0 and 10
+ * in slots 20 and 21; NULL turns tracing off (the default).  Events: 0 start,
+ * 1 x staged, 2 logits written, 3 grid barrier 1 passed, 4 routed, 5 first
+ * gate/up tile landed, 6 gate/up done, 7 grid barrier 2 passed, 8 down done,
+ * 9 producer issued every tile, 10 end, 11 producer issued its first tile,
+ * 12 routing: logits loaded, 13 softmax done, 14 top-K ranked, 15 x loaded,
+ * 16 x stored to shared memory, 17 gate/up items done, 18 first down item
+ * started, 19 producer started. */
 M1MOE_API m1moe_status m1moe_cuda_set_trace(m1moe_cuda_ctx *ctx, uint64_t *d_trace);
 
 #ifdef __cplusplus

@@ -18,8 +18,9 @@
 #include "m1moe_cuda.h"
 #include "common.cuh"
 #include "matvec4.cuh"
-#include "moe_decode.cuh"
+#include "moe_layer.cuh"
 #include "pipeline.cuh"
+#include "tiled_layout.cuh"
 
 namespace {
 
@@ -81,10 +82,8 @@ void expert_offsets(int h, int I, int gs, long long off[9]) {
 }
 
 template <int NT>
-cudaError_t launch_matvec_nt(const m1::MatvecParams &p, long long groups, int grid_cap,
-                             cudaStream_t st) {
+cudaError_t launch_matvec_nt(const m1::MatvecParams &p, int grid_cap, cudaStream_t st) {
     constexpr int R = 4;
-    (void)groups;
     const long long warps_needed = (long long)p.num_mats * ((p.out_dim + R - 1) / R);
     long long grid = std::min<long long>((warps_needed + 7) / 8, grid_cap);
     if (grid < 1) grid = 1;
@@ -92,31 +91,34 @@ cudaError_t launch_matvec_nt(const m1::MatvecParams &p, long long groups, int gr
     return cudaGetLastError();
 }
 
+constexpr size_t kMaxDynSmem = 227 * 1024;  // per-CTA opt-in shared memory on sm_100
+constexpr size_t kStageTarget = 32 * 1024;  // bulk copies this large run at HBM speed
+constexpr size_t kStagingBytes = 256u << 20;  // device staging for cold-start repacking
+
 }  // namespace
 
 struct m1moe_cuda_ctx {
     m1moe_cuda_cfg cfg{};
     int e0 = 0, ne = 0;
-    size_t expert_bytes = 0;
-    long long off[9] = {};
-    uint8_t *table = nullptr;     // [layers][ne][expert_bytes]
+    size_t expert_bytes = 0;      // reference block size (ModelSpec.expertBytes4Bit)
+    long long off[9] = {};        // reference block offsets
+    m1::TiledLayout tl{};         // HBM table block layout
+    uint8_t *table = nullptr;     // [layers][ne] tiled blocks
     uint16_t *router = nullptr;   // [layers][E][h]
     std::vector<uint8_t> layer_loaded, router_loaded;
-    float *logits = nullptr;      // [max_batch][E]
-    uint16_t *xT = nullptr;       // [max_batch][h] bf16, pair-permuted chunk-transposed
-    float *xsum = nullptr;        // [max_batch][h/32]
-    uint16_t *actT = nullptr;     // [max_batch*K][I] bf16, pair-permuted chunk-transposed
+    unsigned long long *xlog = nullptr;  // [max_batch][E] tagged logits
+    uint32_t *actT = nullptr;            // [max_batch*K][I/2] bf16 activation pairs
+    unsigned *epochs = nullptr;          // per-CTA call counters (moe_layer.cuh)
     int *err = nullptr;           // device error word (pipeline.cuh kErr*)
-    m1::RouteInfo *route = nullptr;  // routing decision of the current call
-    int *ticket = nullptr;        // router grid's last-CTA ticket
     unsigned long long *trace = nullptr;  // optional phase timestamps (caller-owned)
+    uint8_t *staging = nullptr;   // device staging for repacking host layer images
+    size_t staging_bytes = 0;
     // synchronous host-buffer path
     float *hx = nullptr, *hres = nullptr, *hout = nullptr;
     int *hidx = nullptr;
     float *hw = nullptr;
     cudaStream_t stream = nullptr;  // for the *_host calls and staging copies
     void *pinned[2] = {nullptr, nullptr};
-    size_t pinned_bytes = 0;
     cudaEvent_t staged[2] = {nullptr, nullptr};
     int num_sms = 148;
 };
@@ -139,13 +141,11 @@ void free_ctx(m1moe_cuda_ctx *c) {
     if (!c) return;
     cudaFree(c->table);
     cudaFree(c->router);
-    cudaFree(c->logits);
-    cudaFree(c->xT);
-    cudaFree(c->xsum);
+    cudaFree(c->xlog);
     cudaFree(c->actT);
+    cudaFree(c->epochs);
     cudaFree(c->err);
-    cudaFree(c->route);
-    cudaFree(c->ticket);
+    cudaFree(c->staging);
     cudaFree(c->hx);
     cudaFree(c->hres);
     cudaFree(c->hout);
@@ -159,12 +159,22 @@ void free_ctx(m1moe_cuda_ctx *c) {
     delete c;
 }
 
-m1::MoeParams moe_params(m1moe_cuda_ctx *c, int layer, int B) {
-    m1::MoeParams p{};
+constexpr size_t kEpochBytes = (size_t)m1::kMaxCtas * m1::kEpochStride * sizeof(unsigned);
+
+// Zero the epoch words and the tagged logits (tag 0 is never a call's tag,
+// so no stale word can match after this).
+cudaError_t clear_exchange(m1moe_cuda_ctx *c) {
     const m1moe_cuda_cfg &g = c->cfg;
-    p.table = c->table + (size_t)layer * c->ne * c->expert_bytes;
-    p.expert_bytes = (long long)c->expert_bytes;
-    for (int i = 0; i < 9; ++i) p.off[i] = c->off[i];
+    cudaError_t e = cudaMemset(c->epochs, 0, kEpochBytes);
+    if (e == cudaSuccess) e = cudaMemset(c->xlog, 0, (size_t)g.max_batch * g.num_experts * 8);
+    return e;
+}
+
+m1::LayerParams layer_params(m1moe_cuda_ctx *c, int layer, int B) {
+    m1::LayerParams p{};
+    const m1moe_cuda_cfg &g = c->cfg;
+    p.table = c->table + (size_t)layer * c->ne * c->tl.block;
+    p.tl = c->tl;
     p.router = c->router + (size_t)layer * g.num_experts * g.hidden_dim;
     p.E = g.num_experts;
     p.K = g.top_k;
@@ -175,131 +185,141 @@ m1::MoeParams moe_params(m1moe_cuda_ctx *c, int layer, int B) {
     p.e0 = c->e0;
     p.ne = c->ne;
     p.ntok = B;
-    p.logits = c->logits;
-    p.xT = c->xT;
-    p.xsum = c->xsum;
+    p.xlog = c->xlog;
     p.actT = c->actT;
+    p.epochs = c->epochs;
     p.err = c->err;
-    p.route = c->route;
-    p.ticket = c->ticket;
     p.trace = c->trace;
     return p;
 }
 
-// Shared-memory pipeline geometry.  A gate/up CTA and a down CTA are sized to
-// be resident on one SM together (so the down grid can prefetch while gate/up
-// runs): rings of ~100 KB and ~88 KB.
-struct Geometry {
-    int grid, router_grid;
-    size_t gu_smem, dn_smem, router_smem;
-};
+size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
+// Largest divisor of n that is a multiple of m and at most cap (>= m).
+int divisor_tile(int n, int m, long long cap) {
+    int best = m;
+    for (int d = m; d <= n; d += m)
+        if (n % d == 0 && d <= cap) best = d;
+    return best;
+}
 
-int round_up(int v, int m) { return (v + m - 1) / m * m; }
-
-constexpr size_t kMaxDynSmem = 227 * 1024;  // per-CTA opt-in limit on sm_100
-
-// Pipeline geometry for a batch of NT (template) tokens; rt_gu / rt_dn are the
-// kernels' rows per tile (TileRows<NT>).  Each ring gets the shared memory left
-// after the kernel's fixed parts.
-Geometry plan_geometry(m1::MoeParams &p, int num_sms, int nt, int rt_gu, int rt_dn) {
-    Geometry g{};
-    g.grid = num_sms;
-    const int srb_h = (p.h / p.gs) * 2, srb_i = (p.I / p.gs) * 2;
+// Plan tiles, stages and the shared-memory map of k_moe_layer<nt>.  Returns
+// the dynamic shared memory size, or 0 if the shape does not fit an SM.
+size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg, int rd) {
+    const m1::TiledLayout &tl = p.tl;
     const int nch = p.h / m1::kChunkCols, nchI = p.I / m1::kChunkCols;
     const int maxU = std::min(p.ntok * p.K, p.ne);
-    // ---- gate/up: tile = rt rows of gate and of up, each W + S span + B span
-    // (a span rounded out to 16 bytes adds at most 32 bytes).
-    const int pair_bytes = 2 * (p.h / 2) + 4 * srb_h;
-    p.gu_stage_bytes = round_up(rt_gu * pair_bytes + 4 * 32, 128);
+    // gate/up tile: GT pair-rows, GT | I and 8 | GT (row pairs R, R+4 stay in
+    // one tile), as large as kStageTarget allows
+    p.gu_tile_rows = divisor_tile(p.I, 8, std::max<long long>(8, kStageTarget / tl.pr));
+    (void)pg;
+    // down tile: the CTA's rows of one expert, cut to kStageTarget
+    p.dn_rows_max = (p.h + grid - 1) / grid;
+    p.dn_tile_rows = (int)std::max<long long>(
+        1, std::min<long long>(p.dn_rows_max, (long long)(kStageTarget / tl.dr)));
+    p.stage_bytes = (int)m1::round_up_ll(
+        std::max<long long>(p.gu_tile_rows * tl.pr, p.dn_tile_rows * tl.dr), 128);
     p.gu_nslices = nt <= 2 ? (nch + 31) / 32 : 1;
-    const long long gu_units = (long long)maxU * (p.I / rt_gu);
-    p.gu_rows_max = (int)((gu_units + g.grid - 1) / g.grid) * rt_gu;
-    p.x_smem = (size_t)nt * p.h * 2 <= 32 * 1024;
-    size_t gu_fixed = sizeof(m1::Ctl) + 16;
-    if (p.x_smem) gu_fixed += (size_t)nt * p.h * 2 + (size_t)nt * nch * 4;
-    if (p.gu_nslices > 1) gu_fixed += (size_t)p.gu_rows_max * p.gu_nslices * 2 * nt * 4;
-    p.gu_nstages = (int)std::min<size_t>(
-        m1::kMaxStages, (kMaxDynSmem - gu_fixed) / (p.gu_stage_bytes + 2 * sizeof(uint64_t)));
-    g.gu_smem = (size_t)p.gu_nstages * (p.gu_stage_bytes + 2 * sizeof(uint64_t)) + gu_fixed;
-    // ---- down: tile = up to rt rows of down of one expert
-    const int row_bytes = p.I / 2 + 2 * srb_i;
-    p.dn_stage_bytes = round_up(rt_dn * row_bytes + 2 * 32, 128);
-    p.dn_nslices = nt <= 2 ? (nchI + 31) / 32 : 1;
-    p.dn_rows_max = (p.h + g.grid - 1) / g.grid;
-    const size_t dn_fixed = sizeof(m1::Ctl) + 16 +
-                            (size_t)p.ntok * p.K * p.dn_rows_max * p.dn_nslices * sizeof(float);
-    p.dn_nstages = (int)std::min<size_t>(
-        m1::kMaxStages, (kMaxDynSmem - dn_fixed) / (p.dn_stage_bytes + 2 * sizeof(uint64_t)));
-    g.dn_smem = (size_t)p.dn_nstages * (p.dn_stage_bytes + 2 * sizeof(uint64_t)) + dn_fixed;
-    // ---- router
-    g.router_grid = std::min(num_sms, std::max(p.E, 1));
-    const int per = (p.E + g.router_grid - 1) / g.router_grid;
-    g.router_smem = (size_t)per * p.h * 2 + 16 + 8 * m1::kMaxTok * sizeof(float);
-    return g;
+    p.dn_nslices = (nchI + 31) / 32;  // one 32-value chunk per lane and slice
+    // down rows per work item: the whole tile (each activation chunk is then
+    // read once per tile), halved while that leaves consumer warps idle
+    {
+        const int mt = (p.dn_rows_max + p.dn_tile_rows - 1) / p.dn_tile_rows;
+        auto items = [&](int dg) {
+            return (long long)maxU * mt * ((p.dn_tile_rows + dg - 1) / dg) * p.dn_nslices;
+        };
+        int dg = p.dn_tile_rows;
+        while (dg > rd && items(dg) < m1::kConsumerWarps) dg = std::max(rd, (dg + 1) / 2);
+        p.dn_group = dg;
+    }
+    const long long units = (long long)maxU * (p.I / 8);
+    p.gu_rows_max = (int)((units + grid - 1) / grid) * 8;
+    p.router_rows = (p.E + grid - 1) / grid;
+    // fixed part of the shared-memory map (after the ring and its barriers)
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off = align16(off + bytes);
+        return at;
+    };
+    const size_t ctl = take(sizeof(m1::Ctl));
+    const size_t xs = take((size_t)nt * p.h * 2);
+    const size_t xsum = take((size_t)nt * nch * 4);
+    const size_t rrows = take((size_t)p.router_rows * p.h * 2);
+    const size_t gup = take(p.gu_nslices > 1 ? (size_t)p.gu_rows_max * p.gu_nslices * 2 * nt * 4 : 16);
+    const size_t dnp = take((size_t)p.ntok * p.K * p.dn_rows_max * p.dn_nslices * 4);
+    const size_t keys = take((size_t)nt * p.E * 8);
+    const size_t lpart = take(8 * m1::kMaxTok * 4);
+    const size_t res = take((size_t)nt * p.dn_rows_max * 4);
+    const size_t fixed = off;
+    const size_t per_stage = (size_t)p.stage_bytes + 2 * sizeof(uint64_t);
+    if (fixed + 2 * per_stage + 16 > kMaxDynSmem) return 0;
+    p.nstages = (int)std::min<size_t>(m1::kMaxStages, (kMaxDynSmem - fixed - 16) / per_stage);
+    const size_t bars = (size_t)p.nstages * p.stage_bytes;
+    const size_t base = align16(bars + 2 * sizeof(uint64_t) * p.nstages);
+    p.off_bars = (int)bars;
+    p.off_ctl = (int)(base + ctl);
+    p.off_xs = (int)(base + xs);
+    p.off_xsum = (int)(base + xsum);
+    p.off_rrows = (int)(base + rrows);
+    p.off_gup = (int)(base + gup);
+    p.off_dnp = (int)(base + dnp);
+    p.off_keys = (int)(base + keys);
+    p.off_lpart = (int)(base + lpart);
+    p.off_res = (int)(base + res);
+    return base + fixed;
 }
 
-template <typename Kern>
-cudaError_t allow_smem(Kern kern, size_t bytes) {
-    // Idempotent; called before every launch so each instantiation is covered.
-    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-}
-
-// Launch with Programmatic Dependent Launch enabled: the kernel may start while
-// its stream predecessor is still running; griddepcontrol.wait inside the
-// kernel orders it after the predecessor's completion.
-template <typename Kern>
-cudaError_t launch_pdl(Kern kern, int grid, int block, size_t smem, cudaStream_t st,
-                       const m1::MoeParams &p) {
+template <int NT>
+m1moe_status launch_layer(m1moe_cuda_ctx *c, m1::LayerParams p, cudaStream_t st) {
+    const int grid = std::min(c->num_sms, m1::kMaxCtas);
+    const size_t smem = plan_layer(p, grid, NT, m1::ItemRows<NT>::pairs, m1::ItemRows<NT>::dn);
+    if (smem == 0 || smem > kMaxDynSmem)
+        return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
+    M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(block);
+    cfg.blockDim = dim3(m1::kLayerThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
+    // Cooperative: every CTA is resident at once, which the grid barriers need.
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, p);
-}
-
-#define M1_TRY_LAUNCH(expr)                                      \
-    do {                                                         \
-        cudaError_t e_ = (expr);                                 \
-        if (e_ != cudaSuccess) return cuda_fail(e_, #expr);      \
-        g_launches.fetch_add(1, std::memory_order_relaxed);      \
-    } while (0)
-
-// route_only: router + routing (no expert work), for m1moe_cuda_router_topk.
-template <int NT>
-m1moe_status launch_moe(m1moe_cuda_ctx *c, m1::MoeParams p, cudaStream_t st, bool route_only) {
-    Geometry g = plan_geometry(p, c->num_sms, NT, m1::TileRows<NT>::gu, m1::TileRows<NT>::dn);
-    if (g.gu_smem > kMaxDynSmem || g.dn_smem > kMaxDynSmem || p.gu_nstages < 2 || p.dn_nstages < 2)
-        return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
-    M1_CK(allow_smem(m1::k_router<NT>, g.router_smem));
-    M1_TRY_LAUNCH(launch_pdl(m1::k_router<NT>, g.router_grid, m1::kRouterThreads, g.router_smem,
-                             st, p));
-    if (route_only) return M1MOE_OK;  // the router grid's last CTA wrote the outputs
-    M1_CK(allow_smem(m1::k_moe_gateup<NT>, g.gu_smem));
-    M1_TRY_LAUNCH(launch_pdl(m1::k_moe_gateup<NT>, g.grid, m1::kPipeThreads, g.gu_smem, st, p));
-    M1_CK(allow_smem(m1::k_moe_down<NT>, g.dn_smem));
-    M1_TRY_LAUNCH(launch_pdl(m1::k_moe_down<NT>, g.grid, m1::kPipeThreads, g.dn_smem, st, p));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, m1::k_moe_layer<NT>, p);
+    if (e != cudaSuccess) return cuda_fail(e, "k_moe_layer launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     return M1MOE_OK;
 }
 
-m1moe_status dispatch_moe(m1moe_cuda_ctx *c, const m1::MoeParams &p, cudaStream_t st,
-                          bool route_only) {
-    if (p.ntok == 1) return launch_moe<1>(c, p, st, route_only);
-    if (p.ntok == 2) return launch_moe<2>(c, p, st, route_only);
-    if (p.ntok <= 4) return launch_moe<4>(c, p, st, route_only);
-    return launch_moe<8>(c, p, st, route_only);
+m1moe_status dispatch_layer(m1moe_cuda_ctx *c, const m1::LayerParams &p, cudaStream_t st) {
+    if (p.ntok == 1) return launch_layer<1>(c, p, st);
+    if (p.ntok == 2) return launch_layer<2>(c, p, st);
+    if (p.ntok <= 4) return launch_layer<4>(c, p, st);
+    return launch_layer<8>(c, p, st);
 }
 
 m1moe_status check_layer(m1moe_cuda_ctx *c, int32_t layer) {
     if (!c) return fail(M1MOE_ERR_INVALID_ARG, "ctx is NULL");
     if (layer < 0 || layer >= c->cfg.num_layers)
         return fail(M1MOE_ERR_INVALID_ARG, "layer %d out of range [0,%d)", layer, c->cfg.num_layers);
+    return M1MOE_OK;
+}
+
+// Repack `n` reference-layout expert blocks at d_src (device) into the table.
+m1moe_status repack_experts(m1moe_cuda_ctx *c, const uint8_t *d_src, uint8_t *d_dst, int n,
+                            cudaStream_t st) {
+    m1::RefOffsets ro;
+    for (int i = 0; i < 9; ++i) ro.off[i] = c->off[i];
+    const long long rows = (long long)n * (c->cfg.intermediate_dim + c->cfg.hidden_dim);
+    const int grid = (int)std::min<long long>(rows, 64LL * c->num_sms);
+    m1::k_repack_tiled<<<grid, 128, 0, st>>>(d_src, (long long)c->expert_bytes, d_dst, c->tl, ro, n,
+                                              c->cfg.hidden_dim, c->cfg.intermediate_dim,
+                                              c->cfg.group_size);
+    M1_LAUNCHED();
     return M1MOE_OK;
 }
 
@@ -362,6 +382,7 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     c->ne = ne;
     c->expert_bytes = m1moe_cuda_expert_bytes(g.hidden_dim, g.intermediate_dim, g.group_size);
     expert_offsets(g.hidden_dim, g.intermediate_dim, g.group_size, c->off);
+    c->tl = m1::make_tiled_layout(g.hidden_dim, g.intermediate_dim, g.group_size);
     c->layer_loaded.assign(g.num_layers, 0);
     c->router_loaded.assign(g.num_layers, 0);
     c->num_sms = sm_count();
@@ -374,17 +395,12 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
         free_ctx(c);                                                \
         return st_;                                                 \
     }
-    // +64: tile copies round scale/bias ranges out to 16-byte boundaries and
-    // may read up to 15 bytes past the last array of the last expert.
-    M1_ALLOC(c->table, (size_t)g.num_layers * ne * c->expert_bytes + 64);
+    M1_ALLOC(c->table, (size_t)g.num_layers * ne * c->tl.block);
     M1_ALLOC(c->router, (size_t)g.num_layers * E * g.hidden_dim * 2);
-    M1_ALLOC(c->logits, B * E * 4);
-    M1_ALLOC(c->xT, B * g.hidden_dim * 2);
-    M1_ALLOC(c->xsum, B * (g.hidden_dim / 32) * 4);
-    M1_ALLOC(c->actT, B * K * g.intermediate_dim * 2);
+    M1_ALLOC(c->xlog, B * E * 8);
+    M1_ALLOC(c->actT, B * K * (g.intermediate_dim / 2) * 4);
+    M1_ALLOC(c->epochs, kEpochBytes);
     M1_ALLOC(c->err, 4);
-    M1_ALLOC(c->route, sizeof(m1::RouteInfo));
-    M1_ALLOC(c->ticket, 4);
     M1_ALLOC(c->hx, B * g.hidden_dim * 4);
     M1_ALLOC(c->hres, B * g.hidden_dim * 4);
     M1_ALLOC(c->hout, B * g.hidden_dim * 4);
@@ -392,15 +408,11 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     M1_ALLOC(c->hw, B * K * 4);
 #undef M1_ALLOC
     e = cudaMemset(c->err, 0, 4);
-    if (e == cudaSuccess) e = cudaMemset(c->ticket, 0, 4);
+    if (e == cudaSuccess) e = clear_exchange(c);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
-        m1moe_status st = cuda_fail(e, "cudaMemset err");
-        free_ctx(c);
-        return st;
-    }
-    e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
-    if (e != cudaSuccess) {
-        m1moe_status st = cuda_fail(e, "cudaStreamCreate");
+        m1moe_status st = cuda_fail(e, "context setup");
         free_ctx(c);
         return st;
     }
@@ -425,30 +437,41 @@ m1moe_status m1moe_cuda_load_expert_layer(m1moe_cuda_ctx *c, int32_t layer, cons
         return fail(M1MOE_ERR_INVALID_ARG, "layer %d: %zu bytes, expected %zu (= %d x %zu)", layer,
                     nbytes, want, c->cfg.num_experts, c->expert_bytes);
     DeviceGuard dg(c->cfg.device);
-    // Double-buffered pinned staging: memcpy into one bounce buffer while the
-    // other is in flight to HBM.
+    // Host image -> pinned bounce buffers (double-buffered) -> device staging
+    // (whole experts) -> repack into the tiled table.
     const size_t chunk = 32u << 20;
     if (!c->pinned[0]) {
         for (int i = 0; i < 2; ++i) {
             M1_CK(cudaHostAlloc(&c->pinned[i], chunk, cudaHostAllocDefault));
             M1_CK(cudaEventCreateWithFlags(&c->staged[i], cudaEventDisableTiming));
         }
-        c->pinned_bytes = chunk;
+    }
+    const int per = (int)std::max<size_t>(1, kStagingBytes / c->expert_bytes);
+    if (!c->staging) {
+        c->staging_bytes = (size_t)std::min(per, c->ne) * c->expert_bytes;
+        M1_CK(cudaMalloc(&c->staging, c->staging_bytes));
     }
     const uint8_t *src = static_cast<const uint8_t *>(h_bytes) + (size_t)c->e0 * c->expert_bytes;
-    uint8_t *dst = c->table + (size_t)layer * c->ne * c->expert_bytes;
-    const size_t total = (size_t)c->ne * c->expert_bytes;
+    uint8_t *dst = c->table + (size_t)layer * c->ne * c->tl.block;
     int buf = 0;
     bool used[2] = {false, false};
-    for (size_t done = 0; done < total; done += chunk, buf ^= 1) {
-        const size_t n = std::min(chunk, total - done);
-        if (used[buf]) M1_CK(cudaEventSynchronize(c->staged[buf]));
-        memcpy(c->pinned[buf], src + done, n);
-        M1_CK(cudaMemcpyAsync(dst + done, c->pinned[buf], n, cudaMemcpyHostToDevice, c->stream));
-        M1_CK(cudaEventRecord(c->staged[buf], c->stream));
-        used[buf] = true;
+    for (int e = 0; e < c->ne; e += per) {
+        const int n = std::min(per, c->ne - e);
+        const size_t total = (size_t)n * c->expert_bytes;
+        const uint8_t *s = src + (size_t)e * c->expert_bytes;
+        for (size_t done = 0; done < total; done += chunk, buf ^= 1) {
+            const size_t m = std::min(chunk, total - done);
+            if (used[buf]) M1_CK(cudaEventSynchronize(c->staged[buf]));
+            memcpy(c->pinned[buf], s + done, m);
+            M1_CK(cudaMemcpyAsync(c->staging + done, c->pinned[buf], m, cudaMemcpyHostToDevice,
+                                  c->stream));
+            M1_CK(cudaEventRecord(c->staged[buf], c->stream));
+            used[buf] = true;
+        }
+        if (m1moe_status st = repack_experts(c, c->staging, dst + (size_t)e * c->tl.block, n, c->stream))
+            return st;
+        M1_CK(cudaStreamSynchronize(c->stream));  // staging is reused by the next experts
     }
-    M1_CK(cudaStreamSynchronize(c->stream));
     c->layer_loaded[layer] = 1;
     return M1MOE_OK;
 }
@@ -461,10 +484,10 @@ m1moe_status m1moe_cuda_load_expert_layer_device(m1moe_cuda_ctx *c, int32_t laye
     if (nbytes != want)
         return fail(M1MOE_ERR_INVALID_ARG, "layer %d: %zu bytes, expected %zu", layer, nbytes, want);
     DeviceGuard dg(c->cfg.device);
-    M1_CK(cudaMemcpyAsync(c->table + (size_t)layer * c->ne * c->expert_bytes,
-                          static_cast<const uint8_t *>(d_bytes) + (size_t)c->e0 * c->expert_bytes,
-                          (size_t)c->ne * c->expert_bytes, cudaMemcpyDeviceToDevice,
-                          as_stream(stream)));
+    if (m1moe_status st = repack_experts(
+            c, static_cast<const uint8_t *>(d_bytes) + (size_t)c->e0 * c->expert_bytes,
+            c->table + (size_t)layer * c->ne * c->tl.block, c->ne, as_stream(stream)))
+        return st;
     c->layer_loaded[layer] = 1;
     return M1MOE_OK;
 }
@@ -520,10 +543,10 @@ m1moe_status m1moe_cuda_matvec4_strided(const uint32_t *d_w, const uint16_t *d_s
     const int cap = 4 * sm_count();
     cudaStream_t st = as_stream(stream);
     cudaError_t e;
-    if (batch == 1) e = launch_matvec_nt<1>(p, 0, cap, st);
-    else if (batch == 2) e = launch_matvec_nt<2>(p, 0, cap, st);
-    else if (batch <= 4) e = launch_matvec_nt<4>(p, 0, cap, st);
-    else e = launch_matvec_nt<8>(p, 0, cap, st);
+    if (batch == 1) e = launch_matvec_nt<1>(p, cap, st);
+    else if (batch == 2) e = launch_matvec_nt<2>(p, cap, st);
+    else if (batch <= 4) e = launch_matvec_nt<4>(p, cap, st);
+    else e = launch_matvec_nt<8>(p, cap, st);
     if (e != cudaSuccess) return cuda_fail(e, "k_matvec4 launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return M1MOE_OK;
@@ -560,13 +583,14 @@ m1moe_status m1moe_cuda_router_topk(m1moe_cuda_ctx *c, int32_t layer, const void
         return fail(M1MOE_ERR_INVALID_ARG, "batch %d outside [1,%d]", B, c->cfg.max_batch);
     if (!c->router_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "router of layer %d not loaded", layer);
     DeviceGuard dg(c->cfg.device);
-    m1::MoeParams p = moe_params(c, layer, B);
+    m1::LayerParams p = layer_params(c, layer, B);
     p.x = d_x;
     p.x_bf16 = x_dtype == M1MOE_DTYPE_BF16;
     p.user_idx = d_idx;
     p.user_w = d_w;
     p.user_scores = d_scores;
-    return dispatch_moe(c, p, as_stream(stream), true);
+    p.route_only = 1;
+    return dispatch_layer(c, p, as_stream(stream));
 }
 
 m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *d_x,
@@ -579,12 +603,10 @@ m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *
         return fail(M1MOE_ERR_INVALID_ARG, "dtype must be F32 (0) or BF16 (1)");
     if (B < 1 || B > c->cfg.max_batch)
         return fail(M1MOE_ERR_INVALID_ARG, "batch %d outside [1,%d]", B, c->cfg.max_batch);
-    if ((reinterpret_cast<uintptr_t>(d_x) & 15))
-        return fail(M1MOE_ERR_INVALID_ARG, "x must be 16-byte aligned");
     if (!c->router_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "router of layer %d not loaded", layer);
     if (!c->layer_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "experts of layer %d not loaded", layer);
     DeviceGuard dg(c->cfg.device);
-    m1::MoeParams p = moe_params(c, layer, B);
+    m1::LayerParams p = layer_params(c, layer, B);
     p.x = d_x;
     p.x_bf16 = x_dtype == M1MOE_DTYPE_BF16;
     p.res = d_res;
@@ -593,7 +615,7 @@ m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *
     p.out_bf16 = out_dtype == M1MOE_DTYPE_BF16;
     p.user_idx = d_idx;
     p.user_w = d_w;
-    return dispatch_moe(c, p, as_stream(stream), false);
+    return dispatch_layer(c, p, as_stream(stream));
 }
 
 m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *c, int32_t layer, const float *h_x,
@@ -625,8 +647,11 @@ m1moe_status m1moe_cuda_synchronize(m1moe_cuda_ctx *c) {
     int word = 0;
     M1_CK(cudaMemcpy(&word, c->err, 4, cudaMemcpyDeviceToHost));
     if (word) {
+        // A kernel gave up on a wait: clear the word and the exchange buffers
+        // so that the next call starts from a clean state.
         M1_CK(cudaMemset(c->err, 0, 4));
-        return fail(M1MOE_ERR_DEVICE, "device error word 0x%x (1: pipeline wait timed out)", word);
+        M1_CK(clear_exchange(c));
+        return fail(M1MOE_ERR_DEVICE, "device error word 0x%x (1: a bounded wait timed out)", word);
     }
     return M1MOE_OK;
 }

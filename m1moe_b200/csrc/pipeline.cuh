@@ -92,21 +92,40 @@ __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Phase tracing: when `trace` is non-null, slot [kernel][cta][event] receives
-// the global nanosecond timer (off by default; m1moe_cuda_set_trace).
-constexpr int kTraceEvents = 8;
+// Phase tracing: when `trace` is non-null, slot [cta][event] receives the SM
+// cycle counter (exact within a CTA), and slots 20/21 the global nanosecond
+// timer at events 0 and 10, which places each CTA on a common time axis and
+// gives the cycle length (off by default; m1moe_cuda_set_trace).
+constexpr int kTraceEvents = 20;
+constexpr int kTraceSlots = 24;
 constexpr int kTraceCtas = 160;
 __device__ __forceinline__ void trace_event(unsigned long long *trace, int kernel, int event) {
-    if (trace == nullptr) return;
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (blockIdx.x < kTraceCtas)
-        trace[((size_t)kernel * kTraceCtas + blockIdx.x) * kTraceEvents + event] = t;
+    if (trace == nullptr || blockIdx.x >= kTraceCtas) return;
+    unsigned long long *row = trace + ((size_t)kernel * kTraceCtas + blockIdx.x) * kTraceSlots;
+    const unsigned long long c = clock64();
+    row[event] = c;
+    if (event == 0 || event == 10) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        row[event == 0 ? 20 : 21] = t;
+    }
 }
 
 // Named barrier over the first `nthreads` threads (a multiple of 32).
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also ANDs a predicate over the participating threads.
+__device__ __forceinline__ bool named_sync_and(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, %2, %3, p; "
+        "selp.u32 %0, 1, 0, q; }"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
 }
 
 // A [begin, end) byte range rounded out to 16-byte boundaries for a bulk copy;

@@ -92,7 +92,7 @@ cudaError_t launch_matvec_nt(const m1::MatvecParams &p, int grid_cap, cudaStream
 }
 
 constexpr size_t kMaxDynSmem = 227 * 1024;  // per-CTA opt-in shared memory on sm_100
-constexpr size_t kStageTarget = 32 * 1024;  // bulk copies this large run at HBM speed
+constexpr size_t kStageTarget = 40 * 1024;  // bulk copies this large run at HBM speed
 constexpr size_t kStagingBytes = 256u << 20;  // device staging for cold-start repacking
 
 }  // namespace
@@ -107,7 +107,8 @@ struct m1moe_cuda_ctx {
     uint16_t *router = nullptr;   // [layers][E][h]
     std::vector<uint8_t> layer_loaded, router_loaded;
     unsigned long long *xlog = nullptr;  // [max_batch][E] tagged logits
-    uint32_t *actT = nullptr;            // [max_batch*K][I/2] bf16 activation pairs
+    float *acc = nullptr;                // [max_batch][h] fp32 sums for bf16 output
+    int *done = nullptr;                 // CTAs finished with their atomics (bf16 output)
     unsigned *epochs = nullptr;          // per-CTA call counters (moe_layer.cuh)
     int *err = nullptr;           // device error word (pipeline.cuh kErr*)
     unsigned long long *trace = nullptr;  // optional phase timestamps (caller-owned)
@@ -142,7 +143,8 @@ void free_ctx(m1moe_cuda_ctx *c) {
     cudaFree(c->table);
     cudaFree(c->router);
     cudaFree(c->xlog);
-    cudaFree(c->actT);
+    cudaFree(c->acc);
+    cudaFree(c->done);
     cudaFree(c->epochs);
     cudaFree(c->err);
     cudaFree(c->staging);
@@ -166,6 +168,7 @@ constexpr size_t kEpochBytes = (size_t)m1::kMaxCtas * m1::kEpochStride * sizeof(
 cudaError_t clear_exchange(m1moe_cuda_ctx *c) {
     const m1moe_cuda_cfg &g = c->cfg;
     cudaError_t e = cudaMemset(c->epochs, 0, kEpochBytes);
+    if (e == cudaSuccess) e = cudaMemset(c->done, 0, 4);
     if (e == cudaSuccess) e = cudaMemset(c->xlog, 0, (size_t)g.max_batch * g.num_experts * 8);
     return e;
 }
@@ -186,7 +189,8 @@ m1::LayerParams layer_params(m1moe_cuda_ctx *c, int layer, int B) {
     p.ne = c->ne;
     p.ntok = B;
     p.xlog = c->xlog;
-    p.actT = c->actT;
+    p.acc = c->acc;
+    p.done = c->done;
     p.epochs = c->epochs;
     p.err = c->err;
     p.trace = c->trace;
@@ -205,36 +209,28 @@ int divisor_tile(int n, int m, long long cap) {
 
 // Plan tiles, stages and the shared-memory map of k_moe_layer<nt>.  Returns
 // the dynamic shared memory size, or 0 if the shape does not fit an SM.
-size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg, int rd) {
+size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     const m1::TiledLayout &tl = p.tl;
-    const int nch = p.h / m1::kChunkCols, nchI = p.I / m1::kChunkCols;
+    const int nch = p.h / m1::kChunkCols;
     const int maxU = std::min(p.ntok * p.K, p.ne);
+    const int gcb = p.gs / 8;  // column blocks per group
+    if (tl.rc / 32 > m1::kConsumerWarps) return 0;  // see down_row_chunk
+    // down tile: a run of column blocks (a multiple of gcb) of one row chunk,
+    // plus the scale/bias words of its groups; as large as kStageTarget allows
+    const long long per_group = (long long)(gcb + 1) * tl.rc * 4;
+    p.dn_max_cb = gcb * (int)std::max<long long>(1, (long long)kStageTarget / per_group);
+    const long long dn_bytes = (long long)p.dn_max_cb * tl.rc * 4 + (long long)(p.dn_max_cb / gcb) * tl.rc * 4;
     // gate/up tile: GT pair-rows, GT | I and 8 | GT (row pairs R, R+4 stay in
-    // one tile), as large as kStageTarget allows
-    p.gu_tile_rows = divisor_tile(p.I, 8, std::max<long long>(8, kStageTarget / tl.pr));
-    (void)pg;
-    // down tile: the CTA's rows of one expert, cut to kStageTarget
-    p.dn_rows_max = (p.h + grid - 1) / grid;
-    p.dn_tile_rows = (int)std::max<long long>(
-        1, std::min<long long>(p.dn_rows_max, (long long)(kStageTarget / tl.dr)));
-    p.stage_bytes = (int)m1::round_up_ll(
-        std::max<long long>(p.gu_tile_rows * tl.pr, p.dn_tile_rows * tl.dr), 128);
+    // one tile), filling the stage the down tiles need (at least kStageTarget/2)
+    const long long stage_target = std::max<long long>(dn_bytes, kStageTarget / 2);
+    p.gu_tile_rows = divisor_tile(p.I, 8, std::max<long long>(8, stage_target / tl.pr));
+    p.stage_bytes = (int)m1::round_up_ll(std::max<long long>(p.gu_tile_rows * tl.pr, dn_bytes), 128);
     p.gu_nslices = nt <= 2 ? (nch + 31) / 32 : 1;
-    p.dn_nslices = (nchI + 31) / 32;  // one 32-value chunk per lane and slice
-    // down rows per work item: the whole tile (each activation chunk is then
-    // read once per tile), halved while that leaves consumer warps idle
-    {
-        const int mt = (p.dn_rows_max + p.dn_tile_rows - 1) / p.dn_tile_rows;
-        auto items = [&](int dg) {
-            return (long long)maxU * mt * ((p.dn_tile_rows + dg - 1) / dg) * p.dn_nslices;
-        };
-        int dg = p.dn_tile_rows;
-        while (dg > rd && items(dg) < m1::kConsumerWarps) dg = std::max(rd, (dg + 1) / 2);
-        p.dn_group = dg;
-    }
+    (void)pg;
     const long long units = (long long)maxU * (p.I / 8);
     p.gu_rows_max = (int)((units + grid - 1) / grid) * 8;
-    p.router_rows = (p.E + grid - 1) / grid;
+    p.act_cb = p.gu_rows_max / 8;
+    p.xseg_max = p.gu_rows_max / p.gs + 2;
     // fixed part of the shared-memory map (after the ring and its barriers)
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -245,12 +241,12 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg, int rd) {
     const size_t ctl = take(sizeof(m1::Ctl));
     const size_t xs = take((size_t)nt * p.h * 2);
     const size_t xsum = take((size_t)nt * nch * 4);
-    const size_t rrows = take((size_t)p.router_rows * p.h * 2);
     const size_t gup = take(p.gu_nslices > 1 ? (size_t)p.gu_rows_max * p.gu_nslices * 2 * nt * 4 : 16);
-    const size_t dnp = take((size_t)p.ntok * p.K * p.dn_rows_max * p.dn_nslices * 4);
+    const size_t act = take((size_t)nt * p.act_cb * 16);
+    const size_t xseg = take((size_t)nt * p.xseg_max * 4);
     const size_t keys = take((size_t)nt * p.E * 8);
+    const size_t rlog = take((size_t)nt * p.E * 4);
     const size_t lpart = take(8 * m1::kMaxTok * 4);
-    const size_t res = take((size_t)nt * p.dn_rows_max * 4);
     const size_t fixed = off;
     const size_t per_stage = (size_t)p.stage_bytes + 2 * sizeof(uint64_t);
     if (fixed + 2 * per_stage + 16 > kMaxDynSmem) return 0;
@@ -261,19 +257,19 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg, int rd) {
     p.off_ctl = (int)(base + ctl);
     p.off_xs = (int)(base + xs);
     p.off_xsum = (int)(base + xsum);
-    p.off_rrows = (int)(base + rrows);
     p.off_gup = (int)(base + gup);
-    p.off_dnp = (int)(base + dnp);
+    p.off_act = (int)(base + act);
+    p.off_xseg = (int)(base + xseg);
     p.off_keys = (int)(base + keys);
+    p.off_rlog = (int)(base + rlog);
     p.off_lpart = (int)(base + lpart);
-    p.off_res = (int)(base + res);
     return base + fixed;
 }
 
 template <int NT>
 m1moe_status launch_layer(m1moe_cuda_ctx *c, m1::LayerParams p, cudaStream_t st) {
     const int grid = std::min(c->num_sms, m1::kMaxCtas);
-    const size_t smem = plan_layer(p, grid, NT, m1::ItemRows<NT>::pairs, m1::ItemRows<NT>::dn);
+    const size_t smem = plan_layer(p, grid, NT, m1::ItemRows<NT>::pairs);
     if (smem == 0 || smem > kMaxDynSmem)
         return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
     M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -398,7 +394,8 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     M1_ALLOC(c->table, (size_t)g.num_layers * ne * c->tl.block);
     M1_ALLOC(c->router, (size_t)g.num_layers * E * g.hidden_dim * 2);
     M1_ALLOC(c->xlog, B * E * 8);
-    M1_ALLOC(c->actT, B * K * (g.intermediate_dim / 2) * 4);
+    M1_ALLOC(c->acc, B * g.hidden_dim * 4);
+    M1_ALLOC(c->done, 4);
     M1_ALLOC(c->epochs, kEpochBytes);
     M1_ALLOC(c->err, 4);
     M1_ALLOC(c->hx, B * g.hidden_dim * 4);
@@ -605,6 +602,13 @@ m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *
         return fail(M1MOE_ERR_INVALID_ARG, "batch %d outside [1,%d]", B, c->cfg.max_batch);
     if (!c->router_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "router of layer %d not loaded", layer);
     if (!c->layer_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "experts of layer %d not loaded", layer);
+    {
+        // out is written (from the residual) while other CTAs still read x
+        const uintptr_t xb = reinterpret_cast<uintptr_t>(d_x), ob = reinterpret_cast<uintptr_t>(d_out);
+        const uintptr_t xe = xb + (uintptr_t)B * c->cfg.hidden_dim * (x_dtype == M1MOE_DTYPE_BF16 ? 2 : 4);
+        const uintptr_t oe = ob + (uintptr_t)B * c->cfg.hidden_dim * (out_dtype == M1MOE_DTYPE_BF16 ? 2 : 4);
+        if (xb < oe && ob < xe) return fail(M1MOE_ERR_INVALID_ARG, "out must not overlap x");
+    }
     DeviceGuard dg(c->cfg.device);
     m1::LayerParams p = layer_params(c, layer, B);
     p.x = d_x;

@@ -6,44 +6,41 @@
 // K x (gate matvec4bit, up matvec4bit, swiGLU, down matvec4bit) + moeCombine
 // (:401-478; Shaders.metal:39-92, 138-149, 360-376).
 //
-// One CTA per SM (cooperative launch: every CTA is resident, which the
-// cross-CTA waits below need).  Phases:
-//   1. stage x in shared memory as bf16 pair-permuted chunks with fp32 chunk
-//      sums (common.cuh); prefetch this CTA's router rows (bulk copy);
-//   2. logits[t][e] = W_r[e] . x[t] for this CTA's experts (bf16 router
-//      upcast exactly, the caller's x, fp32 FMA, fixed reduction order),
-//      published as TAGGED words (below);
-//   3. every CTA routes every token from the logits (identical,
-//      deterministic): softmax, top-K by rank (descending, ties to the lower
-//      index), optional renormalisation, distinct local experts;
-//   4. a producer warp streams this CTA's gate/up tiles and then its down
-//      tiles through a ring of shared-memory stages, one bulk copy per tile;
-//      24 consumer warps take (tile, row pairs, column slice) work items and
-//      write the SwiGLU activations (bf16) to global memory; the CTA then
-//      publishes them;
-//   5. the consumers compute the down rows of this CTA's h-slice for every
-//      (token, k) from tiles prefetched during phase 4, each 32-row chunk of
-//      an activation as soon as the CTAs that wrote it have published, and
-//      combine per output row in moeCombine's order: residual first, k
-//      ascending.
+// One CTA per SM (cooperative launch: every CTA is resident, which the waits
+// on other CTAs need).  Phases:
+//   1. warps 8..24 stage x in shared memory as bf16 pair-permuted chunks with
+//      fp32 chunk sums (common.cuh) and initialise this CTA's rows of the
+//      output with the residual (or zero); meanwhile
+//   2. warps 0..7 compute logits[t][e] = W_r[e] . x[t] for this CTA's experts
+//      straight from global memory (bf16 router upcast exactly, the caller's
+//      x, fp32 FMA, fixed reduction order), publish them as TAGGED words
+//      (below) and
+//   3. route every token from all logits (identical in every CTA,
+//      deterministic): top-K by rank (descending, ties to the lower index),
+//      distinct local experts; the softmax weights (with optional
+//      renormalisation) are computed beside the expert list;
+//   4. the routed experts' gate/up rows, concatenated, are split over the CTAs
+//      in runs of 8 rows.  A producer warp streams this CTA's gate/up tiles and
+//      then the matching COLUMNS of the down matrices (split-K; the table
+//      stores them column-block major, tiled_layout.cuh) through a ring of
+//      shared-memory stages, one or two bulk copies per tile.  24 consumer
+//      warps compute SwiGLU activations for the CTA's rows into shared memory,
+//      then each row of h's partial sum over those columns, and add
+//      weight_k * partial into the output with fp32 atomics.
 //
-// Cross-CTA exchange without grid barriers.  Every CTA keeps a call counter
-// in its own epoch word (one 128-byte line per CTA); all CTAs start a call
-// with the same value, so tag = epoch + 1 names the call everywhere without
-// communication.  A logit travels as one 64-bit word {tag, f32} (relaxed
-// gpu-scope 64-bit accesses are single-copy atomic), so a reader that sees the
-// tag sees the value.  Activations are plain bf16; a CTA release-stores the
-// tag into its epoch word once all of its activations are written, and a
-// reader acquire-loads the epoch words of the one or two CTAs that wrote the
-// chunk it needs (remembered in a shared-memory bit mask).  Loads that poll
-// touch one word per writer, not the data, which keeps the L2 free for the
-// weight stream.  All waits are bounded; on timeout the CTA sets the device
-// error word and unwinds.
-//
-// Expert weights use the TILED table layout (tiled_layout.cuh): gate/up
-// "pair-rows" [gateW|gateS|gateB|upW|upS|upB] and down rows [W|S|B], so a run
-// of rows is one contiguous bulk copy.  The bytes are the reference's bytes,
-// reordered once at load time.
+// There is no grid-wide barrier.  Every CTA keeps a call counter in its own
+// epoch word (one 128-byte line per CTA); all CTAs start a call with the same
+// value, so tag = epoch + 1 names the call everywhere without communication.
+// A logit travels as one 64-bit word {tag, f32} (relaxed gpu-scope 64-bit
+// accesses are single-copy atomic), so a reader that sees the tag sees the
+// value.  A CTA release-stores the tag into its epoch word once its output
+// rows are initialised; before its first atomic a CTA waits (acquire) until
+// every epoch word carries the tag, which normally holds long before.
+// Expert contributions are summed by atomics in no fixed order: the output is
+// within rounding of the reference's moeCombine order, not bitwise repeatable.
+// For bf16 output the sums go to an fp32 accumulator and the last CTA to
+// finish converts it.  All waits are bounded; on timeout the CTA sets the
+// device error word and unwinds.
 //
 // Experts outside this shard's [e0, e0+ne) are skipped (expert parallelism:
 // the caller sums the shards' partial outputs).
@@ -67,18 +64,15 @@ constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kMaxStages = 32;
 constexpr int kMaxCtas = 1024;
 constexpr int kEpochStride = 32;  // words between two CTAs' epoch words (own 128-byte line)
-constexpr int kLogitsPerLane = kMaxExperts / 32;
 
-// Work-item shapes for NT tokens.  A gate/up item covers PG "row pairs"
-// (rows R and R+4 of an expert, R % 8 < 4: the two rows whose activations
-// share one pair-permuted word), computing RG rows at a time in NPASS passes.
-// A down item covers up to DN rows.
+// Gate/up work items for NT tokens: an item covers PG "row pairs" (rows R and
+// R+4 of an expert, R % 8 < 4: the two rows whose activations share one
+// pair-permuted word), computing RG rows at a time in NPASS passes.
 template <int NT>
 struct ItemRows {
     static constexpr int gu = NT == 1 ? 4 : (NT == 2 ? 2 : 1);  // RG
     static constexpr int pairs = gu >= 2 ? gu / 2 : 1;          // PG
     static constexpr int passes = gu >= 2 ? 1 : 2;              // NPASS
-    static constexpr int dn = NT == 1 ? 8 : 4;  // DN
 };
 
 // The routing decision of one call.
@@ -104,10 +98,11 @@ struct LayerParams {
     int x_bf16;
     const void *res;  // may be null
     int res_bf16;
-    void *out;
+    void *out;        // must not overlap x
     int out_bf16;
+    float *acc;       // [ntok][h] fp32 sums for bf16 output
+    int *done;        // CTAs finished with their atomics (bf16 output)
     unsigned long long *xlog;  // [kMaxTok][E] tagged logits {tag, f32}
-    uint32_t *actT;            // [ntok*K][I/2] bf16 activation pairs, pair-permuted
     unsigned *epochs;          // [kMaxCtas * kEpochStride] per-CTA call counters
     int *user_idx;    // optional [ntok][K]
     float *user_w;    // optional [ntok][K]
@@ -117,33 +112,35 @@ struct LayerParams {
     // geometry (host-planned)
     int stage_bytes, nstages;
     int gu_tile_rows, gu_nslices, gu_rows_max;  // pair-rows per tile (multiple of 8, divides I)
-    int dn_tile_rows, dn_nslices, dn_rows_max, dn_group;
-    int router_rows;  // router rows per CTA (max)
+    int dn_max_cb;    // column blocks per down tile (a multiple of gs/8)
+    int act_cb;       // activation capacity, column blocks per token (gu_rows_max / 8)
+    int xseg_max;     // column-sum capacity, groups per token
     int route_only;   // stop after routing (m1moe_cuda_router_topk)
     // shared-memory offsets (bytes, 16-aligned)
-    int off_bars, off_ctl, off_xs, off_xsum, off_rrows, off_gup, off_dnp, off_keys, off_lpart,
-        off_res;
+    int off_bars, off_ctl, off_xs, off_xsum, off_gup, off_act, off_xseg, off_keys, off_rlog,
+        off_lpart;
 };
 
-// Geometry of the tile in a ring stage: distinct expert u, first row r0
-// (pair-row of the expert for gate/up, row of h for down) and row count nr.
+// The tile in a ring stage.  Gate/up: distinct expert u, first pair-row r0 of
+// the expert, row count nr (ic = -1).  Down: distinct expert u, first column
+// block cb0 (in the concatenated row space, 8 rows per block), ncb blocks,
+// row chunk ic.
 struct StageGeo {
-    int u, r0, nr, pad_;
+    int u, r0, nr, ic;
 };
 
 struct Ctl {
     RouteInfo route;
-    uint64_t rbar;      // router rows landed
     unsigned tag;       // this call's tag (epoch + 1, never 0)
     int abort;
     int next_gu, next_dn;  // work-item counters
     int issued;            // tiles issued by the producer
     int a, b;              // this CTA's gate/up rows [a, b) of the distinct-expert row space
     int ntg, ntd;          // gate/up and down tiles of this CTA
+    int last;              // this CTA finished last (bf16 output)
     int stage_tile[kMaxStages];  // tile whose copy was last issued into each stage
     int stage_done[kMaxStages];  // work items finished on each stage's current tile
     StageGeo geo[kMaxStages];
-    unsigned published[kMaxCtas / 32];  // CTAs seen to have published their activations
 };
 
 __device__ __forceinline__ bool is_local(const LayerParams &p, int e) {
@@ -157,22 +154,14 @@ __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned *p) {
     return v;
 }
 
-__device__ __forceinline__ void st_relaxed_u32(unsigned *p, unsigned v) {
-    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
     unsigned long long v;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
-}
-
-__device__ __forceinline__ void ld_relaxed_2u64(const unsigned long long *p, unsigned long long &a,
-                                                unsigned long long &b) {
-    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];"
-                 : "=l"(a), "=l"(b)
-                 : "l"(p)
-                 : "memory");
 }
 
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v) {
@@ -188,166 +177,165 @@ __device__ __forceinline__ void set_abort(Ctl &ctl, int *err) {
     if (err) atomicOr(err, kErrWaitTimeout);
 }
 
-// Word index, inside one activation vector of I values, of the pair word
-// holding rows R and R+4 (R % 8 < 4) in the pair-permuted chunk-transposed
-// order of common.cuh (ppos / 2).
-__device__ __forceinline__ int act_word(int R, int nchI) {
-    return ((((R >> 3) & 3) * nchI + (R >> 5)) << 2) + (R & 3);
-}
-
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned ld_acquire_cta_shared(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void or_release_cta_shared(unsigned *p, unsigned bits) {
-    asm volatile("red.release.cta.shared::cta.or.b32 [%0], %1;" ::"r"(smem_addr(p)), "r"(bits)
-                 : "memory");
-}
-
-// The 16 pairs of chunk c of an activation vector written by other CTAs in
-// this call (L2-coherent loads).
-__device__ __forceinline__ void load_pairs_cg(const uint32_t *vT, int nchI, int c, uint32_t (&xp)[16]) {
-    const uint4 *p = reinterpret_cast<const uint4 *>(vT);
+// One warp: wait until every CTA's epoch word carries `tag` (all output rows
+// initialised for this call), then fence (acquire).  Loads of a round are all
+// in flight at once; rounds back off.  Returns false on timeout or abort.
+__device__ bool wait_all_epochs(const unsigned *epochs, int G, unsigned tag,
+                                const volatile int *abort) {
+    const int lane = threadIdx.x & 31;
+    for (int w0 = 0; w0 < G; w0 += 256) {
+        bool ok = false;
+        for (uint32_t it = 0, nap = 64; it < kWaitLimit; ++it) {
+            unsigned v[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint4 v = __ldcg(p + (size_t)i * nchI + c);
-        xp[4 * i + 0] = v.x;
-        xp[4 * i + 1] = v.y;
-        xp[4 * i + 2] = v.z;
-        xp[4 * i + 3] = v.w;
+            for (int k = 0; k < 8; ++k) {
+                const int w = w0 + 32 * k + lane;
+                v[k] = w < G ? ld_relaxed_u32(epochs + (size_t)w * kEpochStride) : tag;
+            }
+            bool mine = true;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mine = mine && v[k] == tag;
+            if (__all_sync(0xffffffffu, mine)) {
+                ok = true;
+                break;
+            }
+            if (*abort) break;
+            __nanosleep(nap);
+            nap = min(nap * 2, 512u);
+        }
+        if (!ok) return false;
     }
-}
-
-// Have all CTAs that wrote rows [R, R+32) of the distinct-expert row space
-// published this call's activations?  Gate/up rows are split over the G CTAs
-// in 8-row units, CTA w owning units [units*w/G, units*(w+1)/G), so unit U
-// belongs to CTA ((U+1)*G - 1) / units.
-__device__ __forceinline__ bool writers_published(const unsigned *epochs, unsigned *published, int R,
-                                                  int units, int G, unsigned tag) {
-    const int U0 = R >> 3;
-    const int w0 = ((U0 + 1) * G - 1) / units;
-    const int w1 = (min(U0 + 4, units) * G - 1) / units;
-    for (int w = w0; w <= w1; ++w) {
-        const unsigned bit = 1u << (w & 31);
-        if (ld_acquire_cta_shared(&published[w >> 5]) & bit) continue;
-        if (ld_acquire_u32(epochs + (size_t)w * kEpochStride) != tag) return false;
-        or_release_cta_shared(&published[w >> 5], bit);
-    }
+    __threadfence();
     return true;
 }
 
 // ------------------------------------------------------------------ route ----
-// Warp t routes token t: polls the E tagged logits, softmax (max-subtracted,
-// expf, times 1/sum — InferenceEngine.swift:502-507), top-K by rank
-// (descending, ties to the lower index, NaN lowest — :510-519),
-// renormalisation in k order, then marks its local experts.  Returns false if
-// the logits did not arrive in time.
-__device__ bool route_token(const LayerParams &p, RouteInfo &rs, unsigned long long *keys, int t,
-                            unsigned tag, const volatile int *abort, bool write_user) {
-    const int lane = threadIdx.x & 31, E = p.E, K = p.K;
-    float v[kLogitsPerLane];
+// Top-K (descending, ties to the lower index — InferenceEngine.swift:510-519)
+// by the 256 threads of warps 0..7, then the local-expert marks.  The ranking
+// is taken on the logits, which order like the softmax probabilities (softmax
+// is monotonic), so the softmax itself (route_weights) is off the path to the
+// first weight copy; NaN ranks lowest and -0 equals +0.  rlog/keys: shared
+// [ntok][E].  Returns false if the logits did not arrive in time (uniform
+// over the 256 threads).
+__device__ __forceinline__ unsigned long long logit_key(float v, int e) {
+    const uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
+    uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    if (v != v) ord = 0u;
+    return ((unsigned long long)ord << 32) | (uint32_t)(0xFFFF - e);
+}
+
+__device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
+                          unsigned long long *keys, unsigned tag, const volatile int *abort) {
+    const int tid = threadIdx.x;
+    const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E;
+    // a. collect the tagged logits (all of this thread's loads in flight at once)
+    constexpr int kPer = kMaxTok * kMaxExperts / 256;
     bool ok = false;
-    const unsigned long long *lw = p.xlog + (size_t)t * E;
-    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+    unsigned long long w[kPer];
+    for (uint32_t it = 0, nap = 32; it < kWaitLimit; ++it) {
         bool all = true;
 #pragma unroll
-        for (int j = 0; j < kLogitsPerLane; ++j) {
-            const int e = lane + 32 * j;
-            if (e < E) {
-                const unsigned long long w = ld_relaxed_u64(lw + e);
-                v[j] = __uint_as_float((uint32_t)w);
-                all = all && (unsigned)(w >> 32) == tag;
-            }
+        for (int j = 0; j < kPer; ++j) {
+            const int i = tid + 256 * j;
+            if (i < nel) w[j] = ld_relaxed_u64(p.xlog + i);
         }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+            if (tid + 256 * j < nel) all = all && (unsigned)(w[j] >> 32) == tag;
         if (all) {
             ok = true;
             break;
         }
         if (*abort) break;
-        __nanosleep(32);
+        __nanosleep(nap);
+        nap = min(nap * 2, 256u);
     }
-    if (!__all_sync(0xffffffffu, ok)) return false;
-    float m = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kLogitsPerLane; ++j)
-        if (lane + 32 * j < E) m = fmaxf(m, v[j]);
+    for (int j = 0; j < kPer; ++j) {
+        const int i = tid + 256 * j;
+        if (i < nel) {
+            int t = 0, e = i;
+            while (e >= E) {
+                e -= E;
+                ++t;
+            }
+            const float v = __uint_as_float((uint32_t)w[j]);
+            rlog[i] = v;
+            keys[i] = logit_key(v, e);
+        }
+    }
+    if (!named_sync_and(2, 256, ok)) return false;
+    // b. rank of every (token, expert): P threads per element, each counting
+    //    the keys above it in one slice of the token's E keys
+    int lp = 0;
+    while (lp < 5 && (nel << (lp + 1)) <= 256) ++lp;
+    const int P = 1 << lp;
+    for (int base = 0; base < (nel << lp); base += 256) {
+        const int gidx = base + tid, i = gidx >> lp, part = gidx & (P - 1);
+        int cnt = 0, t = 0, e = i;
+        if (i < nel) {
+            while (e >= E) {
+                e -= E;
+                ++t;
+            }
+            const unsigned long long *kt = keys + (size_t)t * E;
+            const unsigned long long ki = kt[e];
+            for (int f = part; f < E; f += P) cnt += kt[f] > ki ? 1 : 0;
+        }
+        for (int o = 1; o < P; o <<= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+        if (i < nel && part == 0 && cnt < K) rs.idx[t][cnt] = e;
+    }
+    named_sync(2, 256);
+    // c. local-expert marks
+    for (int i = tid; i < ntok * K; i += 256) {
+        int t = 0, k = i;
+        while (k >= K) {
+            k -= K;
+            ++t;
+        }
+        const int e = rs.idx[t][k];
+        if (p.user_idx && blockIdx.x == 0) p.user_idx[i] = e;
+        if (is_local(p, e)) {
+            atomicOr(&rs.tmask[e], 1u << t);
+            rs.kof[e][t] = (unsigned char)k;
+            atomicOr(&rs.emask[e >> 5], 1u << (e & 31));
+        }
+    }
+    named_sync(2, 256);
+    return true;
+}
+
+// The weights of token t's selected experts (one warp): softmax statistics
+// over all E logits, w_k = exp(l_k - max) * (1/sum), optional renormalisation
+// (reduce(0) in k order); CTA 0 also writes the caller's outputs.  Only the
+// final combine reads the weights.
+__device__ void route_weights(const LayerParams &p, RouteInfo &rs, const float *rlog, int t) {
+    const int lane = threadIdx.x & 31, E = p.E, K = p.K;
+    const float *lt = rlog + (size_t)t * E;
+    float m = -INFINITY;
+    for (int e = lane; e < E; e += 32) m = fmaxf(m, lt[e]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < kLogitsPerLane; ++j) {
-        if (lane + 32 * j < E) {
-            v[j] = expf(v[j] - m);
-            s += v[j];
-        }
-    }
+    for (int e = lane; e < E; e += 32) s += expf(lt[e] - m);
     s = warp_sum(s);
     const float inv = 1.0f / s;
-    unsigned long long *kt = keys + (size_t)t * E;
-#pragma unroll
-    for (int j = 0; j < kLogitsPerLane; ++j) {
-        const int e = lane + 32 * j;
-        if (e < E) {
-            v[j] *= inv;
-            if (write_user && p.user_scores) p.user_scores[(size_t)t * E + e] = v[j];
-            // Probabilities are >= 0, so their bit patterns order like the
-            // values; +1 leaves 0 for NaN (lowest).  The low half breaks ties
-            // in favour of the lower index.  All keys are distinct.
-            const uint32_t hi = (v[j] != v[j]) ? 0u : __float_as_uint(v[j]) + 1u;
-            kt[e] = ((unsigned long long)hi << 32) | (uint32_t)(0xFFFF - e);
-        }
-    }
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < kLogitsPerLane; ++j) {
-        const int e = lane + 32 * j;
-        if (e < E) {
-            const unsigned long long ke = kt[e];
-            int rank = 0;
-#pragma unroll 8
-            for (int f = 0; f < E; ++f) rank += kt[f] > ke ? 1 : 0;
-            if (rank < K) {
-                rs.idx[t][rank] = e;
-                rs.w[t][rank] = v[j];
-            }
-        }
-    }
+    const bool user = blockIdx.x == 0;
+    if (user && p.user_scores)
+        for (int e = lane; e < E; e += 32) p.user_scores[(size_t)t * E + e] = expf(lt[e] - m) * inv;
+    if (lane < K) rs.w[t][lane] = expf(lt[rs.idx[t][lane]] - m) * inv;
     __syncwarp();
     if (p.norm) {
         float sum = 0.f;
         if (lane == 0)
-            for (int k = 0; k < K; ++k) sum += rs.w[t][k];  // reduce(0) in k order
+            for (int k = 0; k < K; ++k) sum += rs.w[t][k];
         sum = __shfl_sync(0xffffffffu, sum, 0);
         if (lane < K) rs.w[t][lane] = rs.w[t][lane] / sum;
-        __syncwarp();
     }
-    if (lane < K) {
-        const int e = rs.idx[t][lane];
-        if (write_user) {
-            if (p.user_idx) p.user_idx[t * K + lane] = e;
-            if (p.user_w) p.user_w[t * K + lane] = rs.w[t][lane];
-        }
-        if (is_local(p, e)) {
-            atomicOr(&rs.tmask[e], 1u << t);
-            rs.kof[e][t] = (unsigned char)lane;
-            atomicOr(&rs.emask[e >> 5], 1u << (e & 31));
-        }
-    }
-    return true;
+    if (user && p.user_w && lane < K) p.user_w[t * K + lane] = rs.w[t][lane];
 }
 
+// ------------------------------------------------------------ pipeline ----
 // ------------------------------------------------------------ pipeline ----
 // Wait until tile n occupies stage s and its bytes have landed (warp-uniform).
 // The stage_tile check comes first because mbarrier.try_wait.parity(P) also
@@ -357,13 +345,15 @@ __device__ bool route_token(const LayerParams &p, RouteInfo &rs, unsigned long l
 __device__ __forceinline__ bool wait_tile(uint64_t *full, Ctl &ctl, int s, int n, int nstages,
                                           int *err) {
     bool ok = false;
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    // Spinning warps take issue slots from the working ones: back off.
+    for (uint32_t i = 0, nap = 64; i < kWaitLimit; ++i) {
         if (*reinterpret_cast<volatile int *>(&ctl.stage_tile[s]) == n) {
             ok = true;
             break;
         }
         if (*reinterpret_cast<volatile int *>(&ctl.abort)) break;
-        __nanosleep(20);
+        __nanosleep(nap);
+        nap = min(nap * 2, 512u);
     }
     if (!ok && !*reinterpret_cast<volatile int *>(&ctl.abort)) set_abort(ctl, err);
     if (ok) ok = mbar_wait(&full[s], (n / nstages) & 1, &ctl.abort, err);
@@ -392,12 +382,12 @@ __device__ __forceinline__ float swiglu(float g, float u) {
     return (g / (1.0f + expf(-g))) * u;  // Shaders.metal:147-148: SiLU(gate) * up
 }
 
-// Store the activations of rows R and R+4 of pair `pair` (R % 8 < 4).
-__device__ __forceinline__ void put_act_pair(const LayerParams &p, int pair, int R, float lo,
-                                             float hi) {
-    const int nchI = p.I / kChunkCols;
-    const uint32_t word = (uint32_t)f32_to_bf16_rn(lo) | ((uint32_t)f32_to_bf16_rn(hi) << 16);
-    p.actT[(size_t)pair * (p.I / 2) + act_word(R, nchI)] = word;
+// Activation word of token t for rows R and R+4 (R % 8 < 4, concatenated row
+// space): column block R/8 of this CTA's range, pair R % 4.
+__device__ __forceinline__ void put_act(uint32_t *act, int act_cb, int a8, int t, int R, float lo,
+                                        float hi) {
+    act[(((size_t)t * act_cb + (R >> 3) - a8) << 2) + (R & 3)] =
+        (uint32_t)f32_to_bf16_rn(lo) | ((uint32_t)f32_to_bf16_rn(hi) << 16);
 }
 
 // ---------------------------------------------------------------- kernel ----
@@ -405,7 +395,6 @@ template <int NT>
 __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int RG = ItemRows<NT>::gu, PG = ItemRows<NT>::pairs, NPASS = ItemRows<NT>::passes;
-    constexpr int RD = ItemRows<NT>::dn;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = (int)gridDim.x, blk = (int)blockIdx.x;
     const int NST = p.nstages, STG = p.stage_bytes;
@@ -416,55 +405,153 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     RouteInfo &rs = ctl.route;
     uint16_t *xs = reinterpret_cast<uint16_t *>(smem + p.off_xs);
     float *xsum = reinterpret_cast<float *>(smem + p.off_xsum);
-    uint8_t *rrows = smem + p.off_rrows;
     float *gup = reinterpret_cast<float *>(smem + p.off_gup);
-    float *dnp = reinterpret_cast<float *>(smem + p.off_dnp);
+    uint32_t *act = reinterpret_cast<uint32_t *>(smem + p.off_act);
+    float *xseg = reinterpret_cast<float *>(smem + p.off_xseg);
     unsigned long long *keys = reinterpret_cast<unsigned long long *>(smem + p.off_keys);
+    float *rlog = reinterpret_cast<float *>(smem + p.off_rlog);
     float *lpart = reinterpret_cast<float *>(smem + p.off_lpart);
-    float *resid = reinterpret_cast<float *>(smem + p.off_res);  // [ntok][rows] residual
     const volatile int *vabort = &ctl.abort;
-    const int h = p.h, I = p.I, nch = h / kChunkCols, nchI = I / kChunkCols;
+    const int h = p.h, I = p.I, nch = h / kChunkCols;
     const TiledLayout &tl = p.tl;
     unsigned *my_epoch = p.epochs + (size_t)blk * kEpochStride;
 
-    if (tid == 0) trace_event(p.trace, 0, 0);
-    // ---- phase 1: barriers, router-row prefetch, x staging ----
-    const int nmine = (p.E > blk) ? (p.E - blk + G - 1) / G : 0;
-    const int rowb = h * 2;
-    if (tid == kConsumerThreads) {
-        for (int i = 0; i < NST; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
-            ctl.stage_tile[i] = -1;
-            ctl.stage_done[i] = 0;
-        }
-        mbar_init(&ctl.rbar, 1);
+    if (tid == 0) {
+        trace_event(p.trace, 0, 0);
         ctl.abort = 0;
-        ctl.next_gu = ctl.next_dn = 0;
-        ctl.issued = 0;
-        mbar_fence_init();
-        if (nmine > 0) {
-            const uint64_t pol = l2_evict_first_policy();
-            mbar_arrive_expect_tx(&ctl.rbar, (uint32_t)(nmine * rowb));
-            for (int m = 0; m < nmine; ++m)
-                bulk_g2s(rrows + m * rowb, p.router + (size_t)(blk + m * G) * h, (uint32_t)rowb,
-                         &ctl.rbar, pol);
-        }
-    } else if (tid == kLayerThreads - 1) {
         const unsigned t1 = ld_relaxed_u32(my_epoch) + 1u;
         ctl.tag = t1 ? t1 : 1u;
     }
-    // this CTA's rows of h (down projection, combine)
+    __syncthreads();
+    const unsigned tag = ctl.tag;
+    // this CTA's rows of h (output initialisation)
     const int i0 = (int)((long long)h * blk / G), i1 = (int)((long long)h * (blk + 1) / G);
     const int nrows = i1 - i0;
-    for (int e = tid; e < p.E; e += kLayerThreads) rs.tmask[e] = 0u;
-    if (tid < kMaxExperts / 32) rs.emask[tid] = 0u;
-    for (int i = tid; i < kMaxCtas / 32; i += kLayerThreads) ctl.published[i] = 0u;
-    // x: 4 consecutive values per thread, every load in flight at once
-    {
+    if (warp < 8) {
+        // ---- phase 2: logits of this CTA's experts, straight from global memory ----
+        for (int e = tid; e < p.E; e += 256) rs.tmask[e] = 0u;
+        if (tid < kMaxExperts / 32) rs.emask[tid] = 0u;
+        const int nmine = (p.E > blk) ? (p.E - blk + G - 1) / G : 0;
+        for (int m = 0; m < nmine; ++m) {
+            const int e = blk + m * G;
+            const uint4 *row = reinterpret_cast<const uint4 *>(p.router + (size_t)e * h);
+            float acc[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+            for (int g8 = tid; g8 < h / 8; g8 += 256) {
+                const uint4 wv = __ldg(row + g8);
+                const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+                float wf[8];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    wf[2 * j] = __uint_as_float(ww[j] << 16);
+                    wf[2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
+                }
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if (t < p.ntok) {
+                        float xv[8];
+                        if (p.x_bf16) {
+                            const uint4 r = __ldg(reinterpret_cast<const uint4 *>(
+                                reinterpret_cast<const uint16_t *>(p.x) + (size_t)t * h) + g8);
+                            const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                xv[2 * j] = __uint_as_float(rr[j] << 16);
+                                xv[2 * j + 1] = __uint_as_float(rr[j] & 0xFFFF0000u);
+                            }
+                        } else {
+                            const float4 *xf = reinterpret_cast<const float4 *>(
+                                reinterpret_cast<const float *>(p.x) + (size_t)t * h) + 2 * g8;
+                            const float4 a0 = __ldg(xf), a1 = __ldg(xf + 1);
+                            xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
+                            xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) acc[t] = fmaf(wf[j], xv[j], acc[t]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float v = warp_sum(acc[t]);
+                if (lane == 0) lpart[warp * kMaxTok + t] = v;
+            }
+            named_sync(2, 256);
+            if (tid < p.ntok) {
+                float s = 0.f;
+                for (int w = 0; w < 8; ++w) s += lpart[w * kMaxTok + tid];
+                st_relaxed_u64(p.xlog + (size_t)tid * p.E + e, tagged(tag, __float_as_uint(s)));
+            }
+            named_sync(2, 256);
+        }
+        if (tid == 0) trace_event(p.trace, 0, 2);
+        // ---- phase 3: route (warps 0..7 of every CTA) ----
+        const bool ok = route_cta(p, rs, rlog, keys, tag, vabort);
+        if (tid == 0) trace_event(p.trace, 0, 3);
+        if (!ok) {
+            if (tid == 0) set_abort(ctl, p.err);
+        } else if (warp == 0) {
+            // distinct local experts, ascending, from the expert bit mask
+            unsigned m = lane < kMaxExperts / 32 ? rs.emask[lane] : 0u;
+            const int c = __popc(m);
+            int incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            int pos = incl - c;
+            while (m) {
+                rs.ulist[pos++] = lane * 32 + __ffs(m) - 1;
+                m &= m - 1;
+            }
+            const int nU = __shfl_sync(0xffffffffu, incl, 31);
+            if (lane == 0) {
+                rs.nU = nU;
+                // gate/up rows [a, b) of the distinct-expert row space
+                // (expert u's rows are u*I .. u*I+I-1), cut in units of 8
+                // rows so that row pairs (R, R+4) stay together.
+                const int units = nU * (I / 8);
+                const int a = (int)((long long)units * blk / G) * 8;
+                const int b = (int)((long long)units * (blk + 1) / G) * 8;
+                const int GT = p.gu_tile_rows, MCB = p.dn_max_cb, nic = h / tl.rc;
+                ctl.a = a;
+                ctl.b = b;
+                ctl.ntg = (b > a) ? (b - 1) / GT - a / GT + 1 : 0;
+                // down tiles: per expert segment of [a, b), column-block runs
+                // cut at multiples of MCB, times the row chunks
+                int ntd = 0;
+                for (int cb = a >> 3; cb < (b >> 3);) {
+                    const int uend = (cb / (I / 8) + 1) * (I / 8);
+                    const int cend = min(min(b >> 3, uend), (cb / MCB + 1) * MCB);
+                    ntd += nic;
+                    cb = cend;
+                }
+                ctl.ntd = ntd;
+            }
+        } else {
+            // the routing weights (needed only by the atomics at the end)
+            for (int t = warp - 1; t < p.ntok; t += 7) route_weights(p, rs, rlog, t);
+        }
+    } else {
+        // ---- phase 1 (warps 8..24): pipeline set-up, x staging, output rows ----
+        const int st = tid - 256, nst = kLayerThreads - 256;
+        if (tid == kConsumerThreads) {
+            for (int i = 0; i < NST; ++i) {
+                mbar_init(&full[i], 1);
+                mbar_init(&empty[i], 1);
+                ctl.stage_tile[i] = -1;
+                ctl.stage_done[i] = 0;
+            }
+            ctl.next_gu = ctl.next_dn = 0;
+            ctl.issued = 0;
+            mbar_fence_init();
+        }
+        // x: 4 consecutive values per thread, every load in flight at once
         const int nx4 = p.ntok * h / 4;
 #pragma unroll 4
-        for (int q = tid; q < nx4; q += kLayerThreads) {
+        for (int q = st; q < nx4; q += nst) {
             const int t = (q * 4) / h, j = (q * 4) % h;
             float v[4];
             if (p.x_bf16) {
@@ -482,130 +569,46 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
 #pragma unroll
             for (int u = 0; u < 4; ++u) xs[(size_t)t * h + ppos(j + u, nch)] = f32_to_bf16_rn(v[u]);
         }
-        if (tid == 0) trace_event(p.trace, 0, 15);
-        if (p.res) {
-            for (int q = tid; q < p.ntok * nrows; q += kLayerThreads) {
+        // this CTA's output rows start as the residual (moeCombine adds it
+        // first, Shaders.metal:368) or zero
+        if (!p.route_only) {
+            float *dst = p.out_bf16 ? p.acc : reinterpret_cast<float *>(p.out);
+            for (int q = st; q < p.ntok * nrows; q += nst) {
                 const int t = q / nrows, i = i0 + q % nrows;
-                resid[q] = load_act(p.res, p.res_bf16, (size_t)t * h + i);
+                dst[(size_t)t * h + i] = p.res ? load_act(p.res, p.res_bf16, (size_t)t * h + i) : 0.f;
             }
         }
-    }
-    __syncthreads();
-    if (tid == 0) trace_event(p.trace, 0, 1);
-    const unsigned tag = ctl.tag;
-
-    if (warp < 8) {
-        // ---- phase 2: logits of this CTA's experts (warps 0..7) ----
-        if (nmine > 0) {
-            const bool landed = mbar_wait(&ctl.rbar, 0, &ctl.abort, p.err);
-            if (named_sync_and(2, 256, landed)) {
-                const size_t xtok = (size_t)h * (p.x_bf16 ? 2 : 4);
-                for (int m = 0; m < nmine; ++m) {
-                    const int e = blk + m * G;
-                    const uint8_t *row = rrows + m * rowb;
-                    float acc[NT];
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
-                    for (int g8 = tid; g8 < h / 8; g8 += 256) {
-                        const uint4 wv = *reinterpret_cast<const uint4 *>(row + g8 * 16);
-                        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-                        float wf[8];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            wf[2 * j] = __uint_as_float(ww[j] << 16);
-                            wf[2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
-                        }
-#pragma unroll
-                        for (int t = 0; t < NT; ++t) {
-                            if (t < p.ntok) {
-#pragma unroll
-                                for (int j = 0; j < 8; ++j)
-                                    acc[t] = fmaf(wf[j],
-                                                  load_act(reinterpret_cast<const uint8_t *>(p.x) + t * xtok,
-                                                           p.x_bf16, g8 * 8 + j),
-                                                  acc[t]);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) {
-                        const float v = warp_sum(acc[t]);
-                        if (lane == 0) lpart[warp * kMaxTok + t] = v;
-                    }
-                    named_sync(2, 256);
-                    if (tid < p.ntok) {
-                        float s = 0.f;
-                        for (int w = 0; w < 8; ++w) s += lpart[w * kMaxTok + tid];
-                        st_relaxed_u64(p.xlog + (size_t)tid * p.E + e, tagged(tag, __float_as_uint(s)));
-                    }
-                    named_sync(2, 256);
-                }
-            }
+        named_sync(4, nst);
+        if (tid == 256) {
+            trace_event(p.trace, 0, 1);
+            __threadfence();
+            st_release_u32(my_epoch, tag);
         }
-        if (tid == 0) trace_event(p.trace, 0, 2);
-        // ---- phase 3: route (warps 0..NT-1 of every CTA) ----
-        if (warp < NT) {
-            bool ok = true;
-            if (warp < p.ntok && !*vabort) ok = route_token(p, rs, keys, warp, tag, vabort, blk == 0);
-            if (!ok && lane == 0) set_abort(ctl, p.err);
-            if (tid == 0) trace_event(p.trace, 0, 3);
-            named_sync(3, NT * 32);
-            if (warp == 0) {
-                // distinct local experts, ascending, from the expert bit mask
-                unsigned m = lane < kMaxExperts / 32 ? rs.emask[lane] : 0u;
-                const int c = __popc(m);
-                int incl = c;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += y;
-                }
-                int pos = incl - c;
-                while (m) {
-                    rs.ulist[pos++] = lane * 32 + __ffs(m) - 1;
-                    m &= m - 1;
-                }
-                const int nU = __shfl_sync(0xffffffffu, incl, 31);
-                if (lane == 0) {
-                    rs.nU = nU;
-                    // gate/up rows [a, b) of the distinct-expert row space
-                    // (expert u's rows are u*I .. u*I+I-1), cut in units of 8
-                    // rows so that row pairs (R, R+4) stay together.
-                    const int units = nU * (I / 8);
-                    const int a = (int)((long long)units * blk / G) * 8;
-                    const int b = (int)((long long)units * (blk + 1) / G) * 8;
-                    const int GT = p.gu_tile_rows, DT = p.dn_tile_rows;
-                    ctl.a = a;
-                    ctl.b = b;
-                    ctl.ntg = (b > a) ? (b - 1) / GT - a / GT + 1 : 0;
-                    ctl.ntd = nrows > 0 ? nU * ((nrows + DT - 1) / DT) : 0;
-                }
-            }
-        }
-    }
-    // xsum: the other warps, meanwhile
-    if (tid >= 256) {
-        for (int q = tid - 256; q < p.ntok * nch; q += kLayerThreads - 256) {
+        // chunk sums of x
+        for (int q = st; q < p.ntok * nch; q += nst) {
             const int t = q / nch, c = q % nch;
             uint32_t xp[16];
             load_pairs_any(xs + (size_t)t * h, nch, c, xp);
             xsum[q] = pair_sum(xp);
         }
+        if (warp == 8 && !p.route_only) {
+            if (!wait_all_epochs(p.epochs, G, tag, vabort) && lane == 0) set_abort(ctl, p.err);
+            if (lane == 0) trace_event(p.trace, 0, 7);
+        }
     }
     __syncthreads();
     if (tid == 0) trace_event(p.trace, 0, 4);
-    if (p.route_only || ctl.abort) {
-        // uniform; no copies were issued
-        if (tid == 0) st_relaxed_u32(my_epoch, tag);
-        return;
-    }
+    if (p.route_only || ctl.abort) return;  // uniform; no copies were issued
 
-    // ---- phase 4/5 geometry ----
-    const int GT = p.gu_tile_rows, DT = p.dn_tile_rows, DG = p.dn_group;
+    // ---- phase 4 geometry ----
+    const int GT = p.gu_tile_rows, MCB = p.dn_max_cb, RC = tl.rc, nic = h / RC;
+    const int ncbE = I / 8;  // column blocks per expert
     const int a = ctl.a, b = ctl.b, ntg = ctl.ntg, ntd = ctl.ntd, nU = rs.nU;
-    const int nslg = p.gu_nslices, nsld = p.dn_nslices;
-    const int ipt_g = (GT / 2 / PG) * nslg;          // work items per gate/up tile
-    const int ipt_d = ((DT + DG - 1) / DG) * nsld;  // work items per down tile
+    const int a8 = a >> 3, ag = a / p.gs, gcb = p.gs / 8;
+    const int nslg = p.gu_nslices;
+    const int ipt_g = (GT / 2 / PG) * nslg;  // work items per gate/up tile
+    const int ipt_d = RC / 32;               // work items per down tile (32 rows each)
+    (void)nU;
 
     if (warp == kConsumerWarps) {
         // ================= producer =================
@@ -614,13 +617,15 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             const uint64_t pol = l2_evict_first_policy();
             int n = 0, s = 0, wrap = 0;
             bool ok = true;
-            // Wait for stage s to be free, record its tile, copy.
-            auto issue = [&](int u, int r0, int nr, const uint8_t *src, uint32_t bytes) {
+            // Wait for stage s to be free, record its tile, copy (one or two runs).
+            auto issue = [&](StageGeo g, const uint8_t *src0, uint32_t b0, const uint8_t *src1,
+                             uint32_t b1) {
                 if (n >= NST && !mbar_wait(&empty[s], (wrap - 1) & 1, &ctl.abort, p.err)) return false;
-                ctl.geo[s] = StageGeo{u, r0, nr, 0};
+                ctl.geo[s] = g;
                 __threadfence_block();
-                mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_g2s(ring + (size_t)s * STG, src, bytes, &full[s], pol);
+                mbar_arrive_expect_tx(&full[s], b0 + b1);
+                bulk_g2s(ring + (size_t)s * STG, src0, b0, &full[s], pol);
+                if (b1) bulk_g2s(ring + (size_t)s * STG + b0, src1, b1, &full[s], pol);
                 *reinterpret_cast<volatile int *>(&ctl.stage_tile[s]) = n;
                 if (n == 0) trace_event(p.trace, 0, 11);
                 ++n;
@@ -632,22 +637,34 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             };
             // gate/up tiles: [a, b) cut at multiples of GT (GT | I, so a tile
             // never crosses experts)
-            int R = a, u = ntg ? a / I : 0, bound = (a / GT + 1) * GT;
-            for (int k = 0; k < ntg && ok; ++k) {
-                const int hi = min(bound, b), r0 = R - u * I;
-                ok = issue(u, r0, hi - R,
-                           p.table + (size_t)(rs.ulist[u] - p.e0) * tl.block + (size_t)r0 * tl.pr,
-                           (uint32_t)((hi - R) * tl.pr));
-                R = hi;
-                bound += GT;
-                if (R == (u + 1) * I) ++u;
+            {
+                int R = a, u = ntg ? a / I : 0, bound = (a / GT + 1) * GT;
+                for (int k = 0; k < ntg && ok; ++k) {
+                    const int hi = min(bound, b), r0 = R - u * I;
+                    ok = issue(StageGeo{u, r0, hi - R, -1},
+                               p.table + (size_t)(rs.ulist[u] - p.e0) * tl.block + (size_t)r0 * tl.pr,
+                               (uint32_t)((hi - R) * tl.pr), nullptr, 0);
+                    R = hi;
+                    bound += GT;
+                    if (R == (u + 1) * I) ++u;
+                }
             }
-            // down tiles: expert by expert, this CTA's rows [i0, i1) in runs of DT
-            for (int uu = 0; uu < nU && ok && ntd > 0; ++uu) {
-                const uint8_t *blkp = p.table + (size_t)(rs.ulist[uu] - p.e0) * tl.block + tl.down_off;
-                for (int r0 = i0; r0 < i1 && ok; r0 += DT) {
-                    const int nr = min(DT, i1 - r0);
-                    ok = issue(uu, r0, nr, blkp + (size_t)r0 * tl.dr, (uint32_t)(nr * tl.dr));
+            // down tiles: the same rows as columns of the down matrices, in
+            // runs of at most MCB column blocks (cut at multiples of MCB, so a
+            // group never straddles two tiles); row chunk by row chunk
+            for (int ic = 0; ic < nic && ok && ntd > 0; ++ic) {
+                for (int cb = a8; cb < (b >> 3) && ok;) {
+                    const int u = cb / ncbE, uend = (u + 1) * ncbE;
+                    const int cend = min(min(b >> 3, uend), (cb / MCB + 1) * MCB);
+                    const int lcb = cb - u * ncbE, ncb = cend - cb;
+                    const int lg0 = lcb / gcb, lg1 = (lcb + ncb - 1) / gcb;
+                    const uint8_t *blkp = p.table + (size_t)(rs.ulist[u] - p.e0) * tl.block;
+                    ok = issue(StageGeo{u, cb, ncb, ic},
+                               blkp + tl.dn_w + ((size_t)ic * tl.ncbI + lcb) * RC * 4,
+                               (uint32_t)(ncb * RC * 4),
+                               blkp + tl.dn_sb + ((size_t)ic * tl.ngI + lg0) * RC * 4,
+                               (uint32_t)((lg1 - lg0 + 1) * RC * 4));
+                    cb = cend;
                 }
             }
             ctl.issued = n;
@@ -681,9 +698,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                         const int half = NPASS == 1 ? (r & 1) : pass;
                         trow[r] = 8 * (pu >> 2) + (pu & 3) + 4 * half;
                     }
-                    float acc[kNg];  // [(row * NT + token) * 2 + gate0/up1]
+                    float accg[kNg];  // [(row * NT + token) * 2 + gate0/up1]
 #pragma unroll
-                    for (int i = 0; i < kNg; ++i) acc[i] = 0.f;
+                    for (int i = 0; i < kNg; ++i) accg[i] = 0.f;
                     for (int ch = j * 32 + lane; ch < nch; ch += 32 * nslg) {
                         const int gi = (ch * kChunkCols) / p.gs;
 #pragma unroll
@@ -703,8 +720,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                                 const float bg = bf16_bits(sgp[tl.sbh / 2 + gi]);
                                 const float su = bf16_bits(sup[gi]);
                                 const float bu = bf16_bits(sup[tl.sbh / 2 + gi]);
-                                float &ag = acc[(r * NT + k) * 2 + 0];
-                                float &au = acc[(r * NT + k) * 2 + 1];
+                                float &ag = accg[(r * NT + k) * 2 + 0];
+                                float &au = accg[(r * NT + k) * 2 + 1];
                                 // s*(A - 128X) + b*X with A = sum (128+q) x
                                 ag = fmaf(sg, dot_chunk_bf16(wg, xp), fmaf(fmaf(-128.f, sg, bg), X, ag));
                                 au = fmaf(su, dot_chunk_bf16(wu, xp), fmaf(fmaf(-128.f, su, bu), X, au));
@@ -712,25 +729,25 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                         }
                     }
                     // lane holds value lane / kSg = (r*NT + k)*2 + m
-                    const float tot = warp_reduce_multi(acc);
+                    const float tot = warp_reduce_multi(accg);
                     if (nslg == 1) {
                         const float upv = __shfl_down_sync(0xffffffffu, tot, kSg);
-                        const float act = swiglu(tot, upv);  // meaningful where lane % (2kSg) == 0
+                        const float av = swiglu(tot, upv);  // meaningful where lane % (2kSg) == 0
                         const int jj = lane / (2 * kSg), r = jj / NT, k = jj % NT;
                         const bool lead = (lane % (2 * kSg)) == 0 && ((mask >> k) & 1u);
                         if (NPASS == 1) {
                             // slot r+1 (row R+4) is 2*kSg*NT lanes further on
-                            const float other = __shfl_down_sync(0xffffffffu, act, 2 * kSg * NT);
+                            const float other = __shfl_down_sync(0xffffffffu, av, 2 * kSg * NT);
                             if (lead && (r & 1) == 0) {
                                 const int pu = pg * PG + (r >> 1);
-                                put_act_pair(p, k * p.K + rs.kof[e][k],
-                                             g.r0 + 8 * (pu >> 2) + (pu & 3), act, other);
+                                put_act(act, p.act_cb, a8, k, g.u * I + g.r0 + 8 * (pu >> 2) + (pu & 3),
+                                        av, other);
                             }
                         } else if (pass == 0) {
-                            act_prev = act;
+                            act_prev = av;
                         } else if (lead) {
-                            put_act_pair(p, k * p.K + rs.kof[e][k],
-                                         g.r0 + 8 * (pg >> 2) + (pg & 3), act_prev, act);
+                            put_act(act, p.act_cb, a8, k, g.u * I + g.r0 + 8 * (pg >> 2) + (pg & 3),
+                                    act_prev, av);
                         }
                     } else if (lane % kSg == 0) {
                         const int v = lane / kSg, r = v / (2 * NT), km = v % (2 * NT);
@@ -760,128 +777,130 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                             gv[hh] += gp[0];
                             uv[hh] += gp[1];
                         }
-                    put_act_pair(p, k * p.K + rs.kof[e][k], Ru - u * I, swiglu(gv[0], uv[0]),
-                                 swiglu(gv[1], uv[1]));
+                    put_act(act, p.act_cb, a8, k, Ru, swiglu(gv[0], uv[0]), swiglu(gv[1], uv[1]));
                 }
             }
             named_sync(1, kConsumerThreads);
         }
-        if (tid == 0) {
-            // publish this CTA's activations (also after an abort, so that no
-            // other CTA waits for them until its own time limit)
-            __threadfence();
-            st_release_u32(my_epoch, tag);
-            trace_event(p.trace, 0, 6);
+        // column sums of the activations per (group of this CTA's range, token)
+        const int nseg = b > a ? (b - 1) / p.gs - ag + 1 : 0;
+        for (int i = tid; i < nseg * NT; i += kConsumerThreads) {
+            const int sg = i / NT, k = i % NT;
+            const int c_lo = max((ag + sg) * gcb, a8), c_hi = min((ag + sg + 1) * gcb, b >> 3);
+            float s0 = 0.f, s1 = 0.f;
+            for (int c = c_lo; c < c_hi; ++c) {
+                const uint4 v = reinterpret_cast<const uint4 *>(act)[(size_t)k * p.act_cb + c - a8];
+                const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    s0 += __uint_as_float(vv[q] << 16);
+                    s1 += __uint_as_float(vv[q] & 0xFFFF0000u);
+                }
+            }
+            xseg[i] = s0 + s1;
         }
+        named_sync(1, kConsumerThreads);
+        if (tid == 0) trace_event(p.trace, 0, 6);
 
-        // ================= consumers: down =================
-        // An item is (tile, 32-chunk column slice, DG rows): each lane loads
-        // one 32-value chunk of each routed token's activation once and uses
-        // it for all the item's rows, RD at a time.
-        constexpr int kSd = 32 / RD;
-        const int rmax = p.dn_rows_max, units = nU * (I / 8);
-        const int nd_items = ctl.abort ? 0 : ntd * ipt_d;
+        // ================= consumers: down (split-K) =================
+        // Item = 32 rows of one row chunk (lane = row of h), over all of this
+        // CTA's down tiles of that chunk in ring order.  Per column block: one
+        // weight word, four nibble pairs shared by the tokens; per group:
+        // y += s*A + (b - 128 s)*X; per tile (one expert): total += w_k * y.
+        // One atomic per row and token at the end.
+        const int nsub = nic ? ntd / nic : 0;  // down tiles per row chunk
+        const int nd_items = (ctl.abort || ntd == 0) ? 0 : nic * ipt_d;
+        float *dst = p.out_bf16 ? p.acc : reinterpret_cast<float *>(p.out);
         for (;;) {
             const int q = grab(&ctl.next_dn);
             if (q >= nd_items) break;
-            const int n = q / ipt_d, rem = q - n * ipt_d, grp = rem / nsld, j = rem - grp * nsld;
-            const int s = (ntg + n) % NST;
-            if (!wait_tile(full, ctl, s, ntg + n, NST, p.err)) break;
+            const int ic = q / ipt_d, w32 = q - ic * ipt_d;
+            const int ri = w32 * 32 + lane;
             if (q == 0 && lane == 0) trace_event(p.trace, 0, 18);
-            const StageGeo g = ctl.geo[s];
-            const int rg0 = grp * DG, nr = min(DG, g.nr - rg0);
-            const int ch = j * 32 + lane;
-            const bool have = ch < nchI && nr > 0;
-            // this lane's 32 activation rows were written by one or two CTAs
-            bool ok = !have;
-            if (have) {
-                for (uint32_t it = 0; it < kWaitLimit; ++it) {
-                    if (writers_published(p.epochs, ctl.published, g.u * I + ch * kChunkCols, units,
-                                          G, tag)) {
-                        ok = true;
-                        break;
-                    }
-                    if (*vabort) break;
-                    __nanosleep(64);
+            float tot[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) tot[t] = 0.f;
+            unsigned any = 0u;
+            bool ok = true;
+            for (int jt = 0; jt < nsub; ++jt) {
+                const int n = ntg + ic * nsub + jt, s = n % NST;
+                if (!wait_tile(full, ctl, s, n, NST, p.err)) {
+                    ok = false;
+                    break;
                 }
-            }
-            if (!__all_sync(0xffffffffu, ok)) {
-                if (lane == 0 && !*vabort) set_abort(ctl, p.err);
-                break;
-            }
-            if (lane == 0 && q == 0) trace_event(p.trace, 0, 12);
-            if (nr > 0) {
-                const uint8_t *st = ring + (size_t)s * STG + (size_t)rg0 * tl.dr;
+                const StageGeo g = ctl.geo[s];
                 const int e = rs.ulist[g.u];
                 const unsigned mask = rs.tmask[e];
-                const int gi = have ? (ch * kChunkCols) / p.gs : 0;
-                for (int k = 0; k < NT; ++k) {
-                    if (!((mask >> k) & 1u)) continue;
-                    const int pair = k * p.K + rs.kof[e][k];
-                    uint32_t xp[16];
-                    if (have) {
-                        load_pairs_cg(p.actT + (size_t)pair * (I / 2), nchI, ch, xp);
-                    } else {
+                const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + (size_t)s * STG) + ri;
+                const uint32_t *SBt = Wt + (size_t)g.nr * RC;
+                const int gfirst = g.r0 / gcb;  // first group (concatenated space)
+                float y[NT], A[NT];
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) xp[i] = 0u;
-                    }
-                    const float X = pair_sum(xp);
-                    if (lane == 0 && q == 0) {
-                        asm volatile("" ::"f"(X));
-                        trace_event(p.trace, 0, 14);
-                    }
-                    for (int r0 = 0; r0 < nr; r0 += RD) {
-                        float y[RD];
+                for (int t = 0; t < NT; ++t) y[t] = A[t] = 0.f;
+                int gcur = gfirst, left = gcb - (g.r0 - gfirst * gcb);  // blocks left in gcur
+                auto flush = [&](int gg) {
+                    const uint32_t sb = SBt[(size_t)(gg - gfirst) * RC];
+                    const float sc = bf16_bits(sb & 0xFFFFu), bi = bf16_bits(sb >> 16);
+                    const float cB = fmaf(-128.f, sc, bi);
 #pragma unroll
-                        for (int r = 0; r < RD; ++r) {
-                            y[r] = 0.f;
-                            if (have && r0 + r < nr) {
-                                const uint8_t *pr = st + (size_t)(r0 + r) * tl.dr;
-                                const uint4 w = *reinterpret_cast<const uint4 *>(pr + ch * 16);
-                                const uint16_t *sp = reinterpret_cast<const uint16_t *>(pr + I / 2);
-                                const float sc = bf16_bits(sp[gi]);
-                                const float bi = bf16_bits(sp[tl.sbi / 2 + gi]);
-                                y[r] = fmaf(sc, dot_chunk_bf16(w, xp), fmaf(fmaf(-128.f, sc, bi), X, 0.f));
-                            }
+                    for (int t = 0; t < NT; ++t) {
+                        if ((mask >> t) & 1u) y[t] = fmaf(sc, A[t], fmaf(cB, xseg[(gg - ag) * NT + t], y[t]));
+                        A[t] = 0.f;
+                    }
+                };
+                for (int c = 0; c < g.nr; ++c) {
+                    const uint32_t wd = Wt[(size_t)c * RC];
+                    uint32_t qp[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) qp[k] = q_pair(wd, k);
+                    const uint4 *av = reinterpret_cast<const uint4 *>(act) + (g.r0 + c - a8);
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        if ((mask >> t) & 1u) {
+                            const uint4 v = av[(size_t)t * p.act_cb];
+                            A[t] = fma_pair(qp[3], v.w, fma_pair(qp[2], v.z,
+                                   fma_pair(qp[1], v.y, fma_pair(qp[0], v.x, A[t]))));
                         }
-                        const float tot = warp_reduce_multi(y);
-                        if (lane % kSd == 0) {
-                            const int r = lane / kSd;
-                            if (r0 + r < nr)
-                                dnp[((size_t)pair * rmax + (g.r0 + rg0 + r0 + r - i0)) * nsld + j] = tot;
-                        }
+                    }
+                    if (--left == 0) {
+                        flush(gcur);
+                        ++gcur;
+                        left = gcb;
                     }
                 }
+                if (left != gcb) flush(gcur);
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+                    if ((mask >> t) & 1u) tot[t] = fmaf(rs.w[t][rs.kof[e][t]], y[t], tot[t]);
+                any |= mask;
+                release_item(empty, ctl, s, ipt_d);
             }
-            if (lane == 0 && q == 0) trace_event(p.trace, 0, 13);
-            if (lane == 0 && q == 1) trace_event(p.trace, 0, 16);
-            release_item(empty, ctl, s, ipt_d);
+            if (!ok) break;
+            const int i = ic * RC + ri;
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+                if ((any >> t) & 1u) atomicAdd(dst + (size_t)t * h + i, tot[t]);
         }
-        named_sync(1, kConsumerThreads);
         if (tid == 0) trace_event(p.trace, 0, 8);
-        // moeCombine (Shaders.metal:360-376): residual first, then k ascending;
-        // each expert output is its slices summed in order.  resid[qq] is
-        // token qq / nrows, row i0 + qq % nrows (prefetched at kernel start).
-        if (!ctl.abort) {
-            for (int qq = tid; qq < p.ntok * nrows; qq += kConsumerThreads) {
-                const int t = qq / nrows, i = i0 + qq % nrows;
-                float acc = p.res ? resid[qq] : 0.f;
-                for (int k = 0; k < p.K; ++k) {
-                    if (!is_local(p, rs.idx[t][k])) continue;
-                    const float *pp = dnp + ((size_t)(t * p.K + k) * rmax + (i - i0)) * nsld;
-                    float y = 0.f;
-                    for (int jj = 0; jj < nsld; ++jj) y += pp[jj];
-                    acc = fmaf(rs.w[t][k], y, acc);
-                }
-                store_act(p.out, p.out_bf16, (size_t)t * h + i, acc);
+        if (p.out_bf16) {
+            // the last CTA to finish converts the fp32 sums
+            named_sync(1, kConsumerThreads);
+            if (tid == 0) {
+                __threadfence();
+                ctl.last = atomicAdd(p.done, 1) == G - 1;
+            }
+            named_sync(1, kConsumerThreads);
+            if (ctl.last) {
+                __threadfence();
+                __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(p.out);
+                for (int i = tid; i < p.ntok * h; i += kConsumerThreads)
+                    o[i] = __float2bfloat16_rn(__ldcg(p.acc + i));
+                if (tid == 0) *p.done = 0;
             }
         }
     }
     __syncthreads();
-    if (tid == 0) {
-        trace_event(p.trace, 0, 10);
-        st_relaxed_u32(my_epoch, tag);
-    }
+    if (tid == 0) trace_event(p.trace, 0, 10);
     if (ctl.abort && tid == 0) {
         // wait (bounded) for copies still in flight into this CTA's shared memory
         for (int n = ctl.issued - NST; n < ctl.issued; ++n) {

@@ -62,6 +62,7 @@ def _run_case(oracle_lib, img, router, *, h, I, E, K, norm, B, xdt=torch.bfloat1
     idx, w = idx.cpu().numpy(), w.cpu().numpy()
     ref, ridx, rw = oracle_lib.moe_layer(img, router, xf, rf if with_res else None, h=h, inter=I,
                                          E=E, K=K, gs=64, norm=norm, nthreads=8)
+    blk.synchronize()  # raises if a bounded device wait gave up
     _check_routing(idx, w, ridx, rw, xf, router, K)
     for t in range(B):
         if set(idx[t].tolist()) == set(ridx[t].tolist()):
@@ -125,7 +126,8 @@ def test_forward_host_matches_device_path(golden):
         oh, ih, wh = blk.forward_host(layer, x, r)
         od, idd, wd = blk.forward(layer, torch.from_numpy(x).cuda(), torch.from_numpy(r).cuda(),
                                   return_topk=True)
-        assert np.array_equal(oh, od.cpu().numpy())
+        # expert contributions are summed by atomics in no fixed order
+        assert rel_max_err(oh, od.cpu().numpy()) < 1e-6
         assert np.array_equal(ih, idd.cpu().numpy()) and np.array_equal(wh, wd.cpu().numpy())
     blk.close()
 

@@ -4,9 +4,13 @@
 Workload (OLMoE-shaped MoE block): hidden 2048, 64 experts,
 top-8, SwiGLU experts int4 group-64 (gate/up 1024x2048, down 2048x1024), bf16
 router [64x2048], decode batch 1.  A step is one decode token through the MoE
-blocks of 16 layers with distinct weights (OLMoE's layer count), each layer's
-output feeding the next layer; the 16 expert tables (3.6 GB) keep every step's
-451 MB of expert reads far above the 126 MB L2.  Synthetic seeded weights.
+blocks of 16 layers with distinct weights (OLMoE's layer count); the 16 expert
+tables (3.6 GB) keep every step's ~457 MB of expert reads far above the 126 MB
+L2.  Synthetic seeded weights.  Every layer reads the same N(0,1) hidden state
+(random-init layers chained without the model's RMSNorm overflow to inf within
+a few layers, and NaN logits would route every layer to experts 0..7), so the
+routing, and with it the bytes read, is that of real random hidden states.
+One kernel (k_moe_layer) per layer.
 
 value    = algorithmic bytes (distinct experts read x 3,538,944 B + router
            262,144 B, per layer) per step x steps / device time of the steps,
@@ -119,6 +123,16 @@ class ClockSampler:
         names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
         return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
                 "reasons": names, "samples": len(self.samples)}
+
+
+def traffic_per_launch(wl: dict, world: int):
+    """DRAM bytes (read + write) of one k_moe_layer launch of this workload, from
+    the committed ncu summary (profiles/moe_layer_traffic.json), or None."""
+    try:
+        d = json.loads((ROOT / "profiles" / "moe_layer_traffic.json").read_text())
+        return d.get(f"{wl['name']}/ep{world}")
+    except Exception:
+        return None
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -262,28 +276,25 @@ def run_gpu(args, wl) -> None:
     part = torch.zeros((B, h), dtype=torch.float32, device=dev)  # partial sums (EP)
     own = torch.zeros((b, h), dtype=torch.float32, device=dev)   # this rank's token state
     own.copy_(x0.float())
+    nxt = torch.zeros((b, h), dtype=torch.float32, device=dev)   # reduce-scatter result
     idx_log = torch.zeros((L, B, K), dtype=torch.int32, device=dev)
     w_log = torch.zeros((L, B, K), dtype=torch.float32, device=dev)
     stream = torch.cuda.Stream(device=dev)
 
-    # Single GPU: ping-pong own/part so every layer reads the previous output
-    # (x and the residual are both the previous layer's f32 output).
+    # Single GPU: every layer reads `own` (x and residual) and writes `part`.
     if world == 1:
-        bufs = [own, part]
-
         def one_step(events=None):
             for layer in range(L):
                 if events is not None:
                     events[layer].record()
-                src, dst = bufs[layer % 2], bufs[(layer + 1) % 2]
-                _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, src.data_ptr(), 0,
-                          src.data_ptr(), 0, dst.data_ptr(), 0, B, idx_log[layer].data_ptr(),
+                _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, own.data_ptr(), 0,
+                          own.data_ptr(), 0, part.data_ptr(), 0, B, idx_log[layer].data_ptr(),
                           w_log[layer].data_ptr(), stream.cuda_stream)
-            if L % 2:  # result must end in bufs[0] for the next step
-                bufs[0].copy_(bufs[1])
             if events is not None:
                 events[L].record()
     else:
+        # Expert parallel: gather every rank's token, apply the local experts
+        # to all of them, reduce-scatter the partial sums back to the owners.
         def one_step(events=None):
             for layer in range(L):
                 if events is not None:
@@ -293,11 +304,11 @@ def run_gpu(args, wl) -> None:
                 _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, xa.data_ptr(), 0,
                           res.data_ptr(), 0, part.data_ptr(), 0, B, idx_log[layer].data_ptr(),
                           w_log[layer].data_ptr(), stream.cuda_stream)
-                dist.reduce_scatter_tensor(own, part)
+                dist.reduce_scatter_tensor(nxt, part)
             if events is not None:
                 events[L].record()
 
-    launches_per_step = 3 * L
+    launches_per_step = L  # k_moe_layer, one per layer
     # Eager warm-up (initialises NCCL communicators before capture).
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -354,8 +365,8 @@ def run_gpu(args, wl) -> None:
         ms_max, job_step_bytes = ms, float(step_bytes_local)
     value = job_step_bytes * args.steps / (ms_max * 1e-3) / 1e9
 
-    # Dominant launch sequence: one layer's MoE block (router + gate/up + down)
-    # on this rank; bytes = distinct local experts + router of that layer.
+    # Dominant kernel: k_moe_layer, one launch per layer on this rank; its
+    # algorithmic bytes = distinct local experts + router of that layer.
     per_layer_bytes = step_bytes_local / L
     peak, peak_kind = measured_peaks()
     lay_ms = float(np.mean(layer_ms))
@@ -376,7 +387,6 @@ def run_gpu(args, wl) -> None:
             for layer in range(L):
                 _lib.call("m1moe_cuda_moe_layer_host", blk._ctx, layer, hx.data_ptr(),
                           hx.data_ptr(), hout.data_ptr(), B, hidx.data_ptr(), hw.data_ptr())
-                hx.copy_(hout)
 
         for _ in range(min(args.warmup, 5)):
             host_step()
@@ -401,7 +411,7 @@ def run_gpu(args, wl) -> None:
             for _ in range(args.steps):
                 own.copy_(hin, non_blocking=True)
                 graph.replay()
-                hout.copy_(own, non_blocking=True)
+                hout.copy_(nxt, non_blocking=True)
             s1.record(stream)
         torch.cuda.synchronize()
         te = torch.tensor([s0.elapsed_time(s1)], dtype=torch.float64, device=dev)
@@ -430,9 +440,10 @@ def run_gpu(args, wl) -> None:
             "tok_s": toks,
             "hbm_frac_of_step": value / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
-                         "kernel": "one MoE layer: k_router_logits + k_moe_gateup + k_moe_down",
-                         "peak_source": peak_kind, "layer_us": lay_ms * 1e3},
+                         "frac": achieved / peak, "traffic": traffic_per_launch(wl, world),
+                         "kernel": "k_moe_layer (router + top-K + gate/up + SwiGLU + down + combine)",
+                         "peak_source": peak_kind, "layer_us": lay_ms * 1e3,
+                         "algorithmic_bytes_per_launch": per_layer_bytes},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches_per_step * (args.steps + 0),

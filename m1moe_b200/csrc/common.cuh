@@ -196,6 +196,27 @@ __device__ __forceinline__ float dot_chunk_bf16(const uint4 w, const uint32_t (&
     return (a0 + a1) + (a2 + a3);
 }
 
+// A over two chunks (64 columns) with shared partial accumulators.
+__device__ __forceinline__ float dot_chunk2_bf16(const uint4 w0, const uint32_t (&x0)[16],
+                                                 const uint4 w1, const uint32_t (&x1)[16]) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        a0 = fma_pair(q_pair(w0.x, k), x0[0 + k], a0);
+        a1 = fma_pair(q_pair(w0.y, k), x0[4 + k], a1);
+        a2 = fma_pair(q_pair(w0.z, k), x0[8 + k], a2);
+        a3 = fma_pair(q_pair(w0.w, k), x0[12 + k], a3);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        a0 = fma_pair(q_pair(w1.x, k), x1[0 + k], a0);
+        a1 = fma_pair(q_pair(w1.y, k), x1[4 + k], a1);
+        a2 = fma_pair(q_pair(w1.z, k), x1[8 + k], a2);
+        a3 = fma_pair(q_pair(w1.w, k), x1[12 + k], a3);
+    }
+    return (a0 + a1) + (a2 + a3);
+}
+
 // Pair-permuted chunk-transposed bf16 activation layout.  A vector of
 // n = 32*nch values is stored as nch chunks of 32; chunk c holds 4 words x 4
 // pairs; pair (i, k) of chunk c is the 32-bit element (i*nch + c)*4 + k and
@@ -246,6 +267,104 @@ __device__ __forceinline__ float pair_sum(const uint32_t (&xp)[16]) {
 
 __device__ __forceinline__ uint16_t f32_to_bf16_rn(float v) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+// ---------------------------------------------------------------------------
+// Integer inner loop (dp2a).  x is quantised per 32-value chunk to int16 with
+// scale sx = max|x| / 32767 (round to nearest; the error is below 2^-16 of
+// the chunk's largest value, far inside the 1e-3 parity bar), and stored as
+// 16 words per chunk whose int16 pairs line up with the nibbles that two
+// masks pull out of a weight word:
+//   lo = w & 0x0F0F0F0F holds nibbles (0, 2, 4, 6) in its four bytes,
+//   hi = (w >> 4) & 0x0F0F0F0F holds nibbles (1, 3, 5, 7),
+// and dp2a.lo / dp2a.hi multiply bytes (0, 1) / (2, 3) of b with the two
+// int16 halves of a and add to an int32.  Word (i, k) of chunk c (i = weight
+// word of the chunk, k = 0..3) holds the x pair
+//   k=0: (x[8i], x[8i+2])  k=1: (x[8i+4], x[8i+6])
+//   k=2: (x[8i+1], x[8i+3])  k=3: (x[8i+5], x[8i+7])
+// at element ((i*nch + c)*4 + k), so a lane reading chunk c for fixed i loads
+// 16 contiguous bytes (load_pairs_any).  Per chunk Q = sum q_j * x16_j is
+// exact (|Q| < 2^24), and the row accumulates s*sx*Q + b*X with X the exact
+// fp32 sum of the chunk's x.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int dp2a_lo(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Q = sum_j q_j * x16_j over one 16-byte weight chunk.
+__device__ __forceinline__ int dot_chunk_i16(const uint4 w, const uint32_t (&xq)[16]) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    int a0 = 0, a1 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = ws[i] & 0x0F0F0F0Fu, hi = (ws[i] >> 4) & 0x0F0F0F0Fu;
+        a0 = dp2a_lo(xq[4 * i + 0], lo, a0);
+        a1 = dp2a_hi(xq[4 * i + 1], lo, a1);
+        a0 = dp2a_lo(xq[4 * i + 2], hi, a0);
+        a1 = dp2a_hi(xq[4 * i + 3], hi, a1);
+    }
+    return a0 + a1;
+}
+
+// Quantise one 32-value chunk (v) into its 16 words (strided by nch*4 words
+// per i), returning the scale; *sum receives the exact fp32 sum.
+__device__ __forceinline__ float quant_chunk_i16(const float (&v)[32], uint32_t *xq, int nch, int c,
+                                                 float *sum) {
+    float m = 0.f, s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+        m = fmaxf(m, fmaxf(fabsf(v[j]), fabsf(v[j + 1])));
+        s0 += v[j];
+        s1 += v[j + 1];
+    }
+    *sum = s0 + s1;
+    const float inv = m > 0.f ? 32767.0f / m : 0.f;
+    auto q = [&](float f) { return (uint32_t)(__float2int_rn(f * inv) & 0xFFFF); };
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float *x = v + 8 * i;
+        uint32_t *o = xq + (((size_t)i * nch + c) << 2);
+        o[0] = q(x[0]) | (q(x[2]) << 16);
+        o[1] = q(x[4]) | (q(x[6]) << 16);
+        o[2] = q(x[1]) | (q(x[3]) << 16);
+        o[3] = q(x[5]) | (q(x[7]) << 16);
+    }
+    return m * (1.0f / 32767.0f);
+}
+
+// Load 32 consecutive activations (f32 or bf16) of x as f32.
+__device__ __forceinline__ void load_x32_any(const void *x, int is_bf16, size_t at, float (&v)[32]) {
+    if (is_bf16) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(x) + at);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 r = __ldg(p + i);
+            const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[8 * i + 2 * j] = __uint_as_float(rr[j] << 16);
+                v[8 * i + 2 * j + 1] = __uint_as_float(rr[j] & 0xFFFF0000u);
+            }
+        }
+    } else {
+        const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + at);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 r = __ldg(p + i);
+            v[4 * i] = r.x;
+            v[4 * i + 1] = r.y;
+            v[4 * i + 2] = r.z;
+            v[4 * i + 3] = r.w;
+        }
+    }
 }
 
 // Balanced contiguous split of `total` items over `parts`: [begin, end) of part p.

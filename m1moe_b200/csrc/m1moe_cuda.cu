@@ -81,17 +81,74 @@ void expert_offsets(int h, int I, int gs, long long off[9]) {
     off[8] = off[7] + dsb;
 }
 
+constexpr size_t kMaxDynSmem = 227 * 1024;  // per-CTA opt-in shared memory on sm_100
+size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+
 template <int NT>
-cudaError_t launch_matvec_nt(const m1::MatvecParams &p, int grid_cap, cudaStream_t st) {
-    constexpr int R = 4;
-    const long long warps_needed = (long long)p.num_mats * ((p.out_dim + R - 1) / R);
-    long long grid = std::min<long long>((warps_needed + 7) / 8, grid_cap);
-    if (grid < 1) grid = 1;
-    m1::k_matvec4<NT, R><<<(unsigned)grid, 256, 0, st>>>(p);
+cudaError_t launch_matvec_ring(const m1::MatvecParams &p, const m1::MatvecRing &g, int num_sms,
+                               size_t smem, cudaStream_t st) {
+    cudaError_t e = cudaFuncSetAttribute(m1::k_matvec4_ring<NT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const long long tiles = (long long)p.num_mats * ((p.out_dim + g.tile_rows - 1) / g.tile_rows);
+    const int grid = (int)std::min<long long>(tiles, num_sms);
+    m1::k_matvec4_ring<NT><<<grid, m1::kRingThreads, smem, st>>>(p, g, nullptr);
     return cudaGetLastError();
 }
 
-constexpr size_t kMaxDynSmem = 227 * 1024;  // per-CTA opt-in shared memory on sm_100
+// Ring plan for a matvec stream, or false if the shape does not suit it
+// (rows not 16-byte aligned, or too few tiles to fill the SMs).
+bool plan_matvec_ring(const m1::MatvecParams &p, int nt, int num_sms, m1::MatvecRing &g,
+                      size_t &smem) {
+    const size_t wrow = (size_t)p.in_dim / 2, srow = (size_t)(p.in_dim / p.gs) * 2;
+    if (wrow % 16 || srow % 16 || (p.num_mats > 1 && p.mat_stride % 16)) return false;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(p.w) | reinterpret_cast<uintptr_t>(p.s) |
+                         reinterpret_cast<uintptr_t>(p.b);
+    if (al & 15) return false;
+    const size_t row = wrow + 2 * srow;
+    int tr = (int)std::max<size_t>(m1::kRingRows, (24u << 10) / row);
+    tr = std::max(m1::kRingRows, tr / m1::kRingRows * m1::kRingRows);
+    const long long tiles = (long long)p.num_mats * ((p.out_dim + tr - 1) / tr);
+    if (tiles < 2LL * num_sms) return false;
+    g.tile_rows = tr;
+    g.stage_bytes = (int)m1::round_up_ll((long long)tr * row, 128);
+    size_t off = 0;
+    const size_t xs = (size_t)nt * p.in_dim * 2, xsum = (size_t)nt * (p.in_dim / m1::kChunkCols) * 8;
+    const size_t fixed = align16(sizeof(m1::RingCtl)) + align16(xs) + align16(xsum);
+    const size_t per_stage = (size_t)g.stage_bytes + 16;
+    if (fixed + 2 * per_stage + 16 > kMaxDynSmem) return false;
+    g.nstages = (int)std::min<size_t>(m1::kRingMaxStages, (kMaxDynSmem - fixed - 16) / per_stage);
+    off = (size_t)g.nstages * g.stage_bytes;
+    g.off_bars = (int)off;
+    off = align16(off + 16 * (size_t)g.nstages);
+    g.off_ctl = (int)off;
+    off = align16(off + sizeof(m1::RingCtl));
+    g.off_xs = (int)off;
+    off = align16(off + xs);
+    g.off_xsum = (int)off;
+    off = align16(off + xsum);
+    smem = off;
+    return true;
+}
+
+template <int NT>
+cudaError_t launch_matvec_nt(const m1::MatvecParams &p, int num_sms, cudaStream_t st) {
+    m1::MatvecRing g;
+    size_t rsmem = 0;
+    if (plan_matvec_ring(p, NT, num_sms, g, rsmem)) return launch_matvec_ring<NT>(p, g, num_sms, rsmem, st);
+    constexpr int R = m1::MatvecRows<NT>::R;
+    const long long units = (long long)p.num_mats * ((p.out_dim + R - 1) / R);
+    const long long warps = m1::kMatvecThreads / 32;
+    const long long grid = std::max<long long>(1, std::min<long long>((units + warps - 1) / warps,
+                                                                      3LL * num_sms));
+    const size_t smem = m1::matvec_smem(NT, p.in_dim);
+    cudaError_t e = cudaFuncSetAttribute(m1::k_matvec4<NT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    m1::k_matvec4<NT><<<(unsigned)grid, m1::kMatvecThreads, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
 constexpr size_t kStageTarget = 40 * 1024;  // bulk copies this large run at HBM speed
 constexpr size_t kStagingBytes = 256u << 20;  // device staging for cold-start repacking
 
@@ -197,7 +254,6 @@ m1::LayerParams layer_params(m1moe_cuda_ctx *c, int layer, int B) {
     return p;
 }
 
-size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
 // Largest divisor of n that is a multiple of m and at most cap (>= m).
 int divisor_tile(int n, int m, long long cap) {
@@ -240,10 +296,11 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     };
     const size_t ctl = take(sizeof(m1::Ctl));
     const size_t xs = take((size_t)nt * p.h * 2);
-    const size_t xsum = take((size_t)nt * nch * 4);
+    const size_t xsum = take((size_t)nt * nch * 8);
     const size_t gup = take(p.gu_nslices > 1 ? (size_t)p.gu_rows_max * p.gu_nslices * 2 * nt * 4 : 16);
+    const size_t actf = take((size_t)nt * p.act_cb * 8 * 4);
     const size_t act = take((size_t)nt * p.act_cb * 16);
-    const size_t xseg = take((size_t)nt * p.xseg_max * 4);
+    const size_t xseg = take((size_t)nt * p.xseg_max * 8);
     const size_t keys = take((size_t)nt * p.E * 8);
     const size_t rlog = take((size_t)nt * p.E * 4);
     const size_t lpart = take(8 * m1::kMaxTok * 4);
@@ -258,6 +315,7 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     p.off_xs = (int)(base + xs);
     p.off_xsum = (int)(base + xsum);
     p.off_gup = (int)(base + gup);
+    p.off_actf = (int)(base + actf);
     p.off_act = (int)(base + act);
     p.off_xseg = (int)(base + xseg);
     p.off_keys = (int)(base + keys);
@@ -537,15 +595,31 @@ m1moe_status m1moe_cuda_matvec4_strided(const uint32_t *d_w, const uint16_t *d_s
     p.in_dim = in_dim;
     p.gs = gs;
     p.ntok = batch;
-    const int cap = 4 * sm_count();
+    p.y_ntok = batch;
+    if (m1::matvec_smem(1, in_dim) > kMaxDynSmem)
+        return fail(M1MOE_ERR_UNSUPPORTED, "in_dim %d does not fit shared memory", in_dim);
+    const int nsm = sm_count();
     cudaStream_t st = as_stream(stream);
-    cudaError_t e;
-    if (batch == 1) e = launch_matvec_nt<1>(p, cap, st);
-    else if (batch == 2) e = launch_matvec_nt<2>(p, cap, st);
-    else if (batch <= 4) e = launch_matvec_nt<4>(p, cap, st);
-    else e = launch_matvec_nt<8>(p, cap, st);
-    if (e != cudaSuccess) return cuda_fail(e, "k_matvec4 launch");
-    g_launches.fetch_add(1, std::memory_order_relaxed);
+    // Tokens go in groups whose staged x fits one CTA's shared memory (each
+    // group reads the weights once more).
+    const size_t xtok = (size_t)in_dim * (x_dtype == M1MOE_DTYPE_BF16 ? 2 : 4);
+    for (int t0 = 0; t0 < batch;) {
+        int n = batch - t0;
+        auto nt_of = [](int k) { return k <= 2 ? k : (k <= 4 ? 4 : 8); };
+        while (m1::matvec_smem(nt_of(n), in_dim) > kMaxDynSmem) n = n > 4 ? 4 : (n > 2 ? 2 : 1);
+        m1::MatvecParams q = p;
+        q.x = static_cast<const uint8_t *>(d_x) + (size_t)t0 * xtok;
+        q.ntok = n;
+        q.y_t0 = t0;
+        cudaError_t e;
+        if (n == 1) e = launch_matvec_nt<1>(q, nsm, st);
+        else if (n == 2) e = launch_matvec_nt<2>(q, nsm, st);
+        else if (n <= 4) e = launch_matvec_nt<4>(q, nsm, st);
+        else e = launch_matvec_nt<8>(q, nsm, st);
+        if (e != cudaSuccess) return cuda_fail(e, "k_matvec4 launch");
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        t0 += n;
+    }
     return M1MOE_OK;
 }
 

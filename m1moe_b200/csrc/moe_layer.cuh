@@ -24,9 +24,12 @@
 //      then the matching COLUMNS of the down matrices (split-K; the table
 //      stores them column-block major, tiled_layout.cuh) through a ring of
 //      shared-memory stages, one or two bulk copies per tile.  24 consumer
-//      warps compute SwiGLU activations for the CTA's rows into shared memory,
-//      then each row of h's partial sum over those columns, and add
-//      weight_k * partial into the output with fp32 atomics.
+//      warps compute SwiGLU activations for the CTA's rows into shared memory
+//      (fp32, then int16 per group of gs rows with the group's scale), then
+//      each row of h's partial sum over those columns, and add
+//      weight_k * partial into the output with fp32 atomics.  Both
+//      projections multiply nibbles with int16 activations by dp2a into int32
+//      per chunk or group, scaled in fp32 (common.cuh).
 //
 // There is no grid-wide barrier.  Every CTA keeps a call counter in its own
 // epoch word (one 128-byte line per CTA); all CTAs start a call with the same
@@ -114,10 +117,10 @@ struct LayerParams {
     int gu_tile_rows, gu_nslices, gu_rows_max;  // pair-rows per tile (multiple of 8, divides I)
     int dn_max_cb;    // column blocks per down tile (a multiple of gs/8)
     int act_cb;       // activation capacity, column blocks per token (gu_rows_max / 8)
-    int xseg_max;     // column-sum capacity, groups per token
+    int xseg_max;     // activation groups per token (scale and sum)
     int route_only;   // stop after routing (m1moe_cuda_router_topk)
     // shared-memory offsets (bytes, 16-aligned)
-    int off_bars, off_ctl, off_xs, off_xsum, off_gup, off_act, off_xseg, off_keys, off_rlog,
+    int off_bars, off_ctl, off_xs, off_xsum, off_gup, off_actf, off_act, off_xseg, off_keys, off_rlog,
         off_lpart;
 };
 
@@ -382,12 +385,13 @@ __device__ __forceinline__ float swiglu(float g, float u) {
     return (g / (1.0f + expf(-g))) * u;  // Shaders.metal:147-148: SiLU(gate) * up
 }
 
-// Activation word of token t for rows R and R+4 (R % 8 < 4, concatenated row
-// space): column block R/8 of this CTA's range, pair R % 4.
-__device__ __forceinline__ void put_act(uint32_t *act, int act_cb, int a8, int t, int R, float lo,
+// Activations of token t for rows R and R+4 (concatenated row space), fp32,
+// at row - a of this CTA's range.
+__device__ __forceinline__ void put_act(float *actf, int act_rows, int a, int t, int R, float lo,
                                         float hi) {
-    act[(((size_t)t * act_cb + (R >> 3) - a8) << 2) + (R & 3)] =
-        (uint32_t)f32_to_bf16_rn(lo) | ((uint32_t)f32_to_bf16_rn(hi) << 16);
+    float *f = actf + (size_t)t * act_rows + (R - a);
+    f[0] = lo;
+    f[4] = hi;
 }
 
 // ---------------------------------------------------------------- kernel ----
@@ -403,11 +407,13 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     uint64_t *empty = full + NST;
     Ctl &ctl = *reinterpret_cast<Ctl *>(smem + p.off_ctl);
     RouteInfo &rs = ctl.route;
-    uint16_t *xs = reinterpret_cast<uint16_t *>(smem + p.off_xs);
-    float *xsum = reinterpret_cast<float *>(smem + p.off_xsum);
+    uint32_t *xq = reinterpret_cast<uint32_t *>(smem + p.off_xs);       // [ntok][h/2] int16 pairs
+    float *xsc = reinterpret_cast<float *>(smem + p.off_xsum);          // [ntok][nch] chunk scales
+    float *xsum = xsc + NT * (p.h / kChunkCols);                        // [ntok][nch] chunk sums
+    float *actf = reinterpret_cast<float *>(smem + p.off_actf);         // [ntok][act_cb*8]
     float *gup = reinterpret_cast<float *>(smem + p.off_gup);
-    uint32_t *act = reinterpret_cast<uint32_t *>(smem + p.off_act);
-    float *xseg = reinterpret_cast<float *>(smem + p.off_xseg);
+    uint32_t *act = reinterpret_cast<uint32_t *>(smem + p.off_act);   // [ntok][act_cb][4] int16 pairs
+    float *xseg = reinterpret_cast<float *>(smem + p.off_xseg);        // [seg][ntok] sums, then scales
     unsigned long long *keys = reinterpret_cast<unsigned long long *>(smem + p.off_keys);
     float *rlog = reinterpret_cast<float *>(smem + p.off_rlog);
     float *lpart = reinterpret_cast<float *>(smem + p.off_lpart);
@@ -548,27 +554,6 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             ctl.issued = 0;
             mbar_fence_init();
         }
-        // x: 4 consecutive values per thread, every load in flight at once
-        const int nx4 = p.ntok * h / 4;
-#pragma unroll 4
-        for (int q = st; q < nx4; q += nst) {
-            const int t = (q * 4) / h, j = (q * 4) % h;
-            float v[4];
-            if (p.x_bf16) {
-                const uint2 r = __ldg(reinterpret_cast<const uint2 *>(
-                    reinterpret_cast<const uint16_t *>(p.x) + (size_t)t * h + j));
-                v[0] = __uint_as_float(r.x << 16);
-                v[1] = __uint_as_float(r.x & 0xFFFF0000u);
-                v[2] = __uint_as_float(r.y << 16);
-                v[3] = __uint_as_float(r.y & 0xFFFF0000u);
-            } else {
-                const float4 r = __ldg(reinterpret_cast<const float4 *>(
-                    reinterpret_cast<const float *>(p.x) + (size_t)t * h + j));
-                v[0] = r.x; v[1] = r.y; v[2] = r.z; v[3] = r.w;
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) xs[(size_t)t * h + ppos(j + u, nch)] = f32_to_bf16_rn(v[u]);
-        }
         // this CTA's output rows start as the residual (moeCombine adds it
         // first, Shaders.metal:368) or zero
         if (!p.route_only) {
@@ -584,12 +569,12 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             __threadfence();
             st_release_u32(my_epoch, tag);
         }
-        // chunk sums of x
+        // x as int16 chunks (dp2a layout, common.cuh) with scales and exact sums
         for (int q = st; q < p.ntok * nch; q += nst) {
-            const int t = q / nch, c = q % nch;
-            uint32_t xp[16];
-            load_pairs_any(xs + (size_t)t * h, nch, c, xp);
-            xsum[q] = pair_sum(xp);
+            const int t = q / nch, c = q - t * nch;
+            float v[32];
+            load_x32_any(p.x, p.x_bf16, (size_t)t * h + (size_t)c * kChunkCols, v);
+            xsc[q] = quant_chunk_i16(v, xq + (size_t)t * (h / 2), nch, c, &xsum[q]);
         }
         if (warp == 8 && !p.route_only) {
             if (!wait_all_epochs(p.epochs, G, tag, vabort) && lane == 0) set_abort(ctl, p.err);
@@ -707,8 +692,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                         for (int k = 0; k < NT; ++k) {
                             if (!((mask >> k) & 1u)) continue;
                             uint32_t xp[16];
-                            load_pairs_any(xs + (size_t)k * h, nch, ch, xp);
-                            const float X = xsum[k * nch + ch];
+                            load_pairs_any(reinterpret_cast<const uint16_t *>(xq + (size_t)k * (h / 2)), nch, ch, xp);
+                            const float X = xsum[k * nch + ch], sx = xsc[k * nch + ch];
 #pragma unroll
                             for (int r = 0; r < RG; ++r) {
                                 const uint8_t *pr = st + (size_t)trow[r] * tl.pr;
@@ -722,9 +707,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                                 const float bu = bf16_bits(sup[tl.sbh / 2 + gi]);
                                 float &ag = accg[(r * NT + k) * 2 + 0];
                                 float &au = accg[(r * NT + k) * 2 + 1];
-                                // s*(A - 128X) + b*X with A = sum (128+q) x
-                                ag = fmaf(sg, dot_chunk_bf16(wg, xp), fmaf(fmaf(-128.f, sg, bg), X, ag));
-                                au = fmaf(su, dot_chunk_bf16(wu, xp), fmaf(fmaf(-128.f, su, bu), X, au));
+                                // s*sx*Q + b*X per chunk (Q exact, common.cuh)
+                                ag = fmaf(sg * sx, (float)dot_chunk_i16(wg, xp), fmaf(bg, X, ag));
+                                au = fmaf(su * sx, (float)dot_chunk_i16(wu, xp), fmaf(bu, X, au));
                             }
                         }
                     }
@@ -740,13 +725,13 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                             const float other = __shfl_down_sync(0xffffffffu, av, 2 * kSg * NT);
                             if (lead && (r & 1) == 0) {
                                 const int pu = pg * PG + (r >> 1);
-                                put_act(act, p.act_cb, a8, k, g.u * I + g.r0 + 8 * (pu >> 2) + (pu & 3),
+                                put_act(actf, p.act_cb * 8, a, k, g.u * I + g.r0 + 8 * (pu >> 2) + (pu & 3),
                                         av, other);
                             }
                         } else if (pass == 0) {
                             act_prev = av;
                         } else if (lead) {
-                            put_act(act, p.act_cb, a8, k, g.u * I + g.r0 + 8 * (pg >> 2) + (pg & 3),
+                            put_act(actf, p.act_cb * 8, a, k, g.u * I + g.r0 + 8 * (pg >> 2) + (pg & 3),
                                     act_prev, av);
                         }
                     } else if (lane % kSg == 0) {
@@ -777,27 +762,38 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                             gv[hh] += gp[0];
                             uv[hh] += gp[1];
                         }
-                    put_act(act, p.act_cb, a8, k, Ru, swiglu(gv[0], uv[0]), swiglu(gv[1], uv[1]));
+                    put_act(actf, p.act_cb * 8, a, k, Ru, swiglu(gv[0], uv[0]), swiglu(gv[1], uv[1]));
                 }
             }
             named_sync(1, kConsumerThreads);
         }
-        // column sums of the activations per (group of this CTA's range, token)
+        // quantise the activations per (group of this CTA's range, token):
+        // int16 pairs in the dp2a layout of one column block (4 words per 8
+        // rows, as for x), the group's scale and its exact sum
         const int nseg = b > a ? (b - 1) / p.gs - ag + 1 : 0;
         for (int i = tid; i < nseg * NT; i += kConsumerThreads) {
             const int sg = i / NT, k = i % NT;
             const int c_lo = max((ag + sg) * gcb, a8), c_hi = min((ag + sg + 1) * gcb, b >> 3);
-            float s0 = 0.f, s1 = 0.f;
-            for (int c = c_lo; c < c_hi; ++c) {
-                const uint4 v = reinterpret_cast<const uint4 *>(act)[(size_t)k * p.act_cb + c - a8];
-                const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    s0 += __uint_as_float(vv[q] << 16);
-                    s1 += __uint_as_float(vv[q] & 0xFFFF0000u);
-                }
+            const float *f = actf + (size_t)k * p.act_cb * 8 + (c_lo - a8) * 8;
+            const int n = (c_hi - c_lo) * 8;
+            float m = 0.f, s0 = 0.f, s1 = 0.f;
+            for (int j = 0; j < n; j += 2) {
+                m = fmaxf(m, fmaxf(fabsf(f[j]), fabsf(f[j + 1])));
+                s0 += f[j];
+                s1 += f[j + 1];
             }
-            xseg[i] = s0 + s1;
+            const float inv = m > 0.f ? 32767.0f / m : 0.f;
+            uint32_t *o = act + (((size_t)k * p.act_cb + (c_lo - a8)) << 2);
+            for (int c = 0; c < c_hi - c_lo; ++c) {
+                const float *x = f + 8 * c;
+                auto qz = [&](float v) { return (uint32_t)(__float2int_rn(v * inv) & 0xFFFF); };
+                o[4 * c + 0] = qz(x[0]) | (qz(x[2]) << 16);
+                o[4 * c + 1] = qz(x[4]) | (qz(x[6]) << 16);
+                o[4 * c + 2] = qz(x[1]) | (qz(x[3]) << 16);
+                o[4 * c + 3] = qz(x[5]) | (qz(x[7]) << 16);
+            }
+            xseg[2 * i] = s0 + s1;
+            xseg[2 * i + 1] = m * (1.0f / 32767.0f);
         }
         named_sync(1, kConsumerThreads);
         if (tid == 0) trace_event(p.trace, 0, 6);
@@ -834,32 +830,35 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + (size_t)s * STG) + ri;
                 const uint32_t *SBt = Wt + (size_t)g.nr * RC;
                 const int gfirst = g.r0 / gcb;  // first group (concatenated space)
-                float y[NT], A[NT];
+                float y[NT];
+                int Q[NT];
 #pragma unroll
-                for (int t = 0; t < NT; ++t) y[t] = A[t] = 0.f;
+                for (int t = 0; t < NT; ++t) {
+                    y[t] = 0.f;
+                    Q[t] = 0;
+                }
                 int gcur = gfirst, left = gcb - (g.r0 - gfirst * gcb);  // blocks left in gcur
                 auto flush = [&](int gg) {
                     const uint32_t sb = SBt[(size_t)(gg - gfirst) * RC];
                     const float sc = bf16_bits(sb & 0xFFFFu), bi = bf16_bits(sb >> 16);
-                    const float cB = fmaf(-128.f, sc, bi);
+                    const float *xg = xseg + (size_t)(gg - ag) * NT * 2;
 #pragma unroll
                     for (int t = 0; t < NT; ++t) {
-                        if ((mask >> t) & 1u) y[t] = fmaf(sc, A[t], fmaf(cB, xseg[(gg - ag) * NT + t], y[t]));
-                        A[t] = 0.f;
+                        // s * sa * Q + b * X over the group's columns in this range
+                        if ((mask >> t) & 1u)
+                            y[t] = fmaf(sc * xg[2 * t + 1], (float)Q[t], fmaf(bi, xg[2 * t], y[t]));
+                        Q[t] = 0;
                     }
                 };
                 for (int c = 0; c < g.nr; ++c) {
                     const uint32_t wd = Wt[(size_t)c * RC];
-                    uint32_t qp[4];
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) qp[k] = q_pair(wd, k);
+                    const uint32_t lo = wd & 0x0F0F0F0Fu, hi = (wd >> 4) & 0x0F0F0F0Fu;
                     const uint4 *av = reinterpret_cast<const uint4 *>(act) + (g.r0 + c - a8);
 #pragma unroll
                     for (int t = 0; t < NT; ++t) {
                         if ((mask >> t) & 1u) {
                             const uint4 v = av[(size_t)t * p.act_cb];
-                            A[t] = fma_pair(qp[3], v.w, fma_pair(qp[2], v.z,
-                                   fma_pair(qp[1], v.y, fma_pair(qp[0], v.x, A[t]))));
+                            Q[t] = dp2a_hi(v.w, hi, dp2a_lo(v.z, hi, dp2a_hi(v.y, lo, dp2a_lo(v.x, lo, Q[t]))));
                         }
                     }
                     if (--left == 0) {

@@ -101,6 +101,29 @@ def test_matvec_strided_over_expert_table(oracle_lib):
             assert rel_max_err(yc[e, t], ref) < TOL
 
 
+@pytest.mark.parametrize("batch", [1, 8])
+def test_matvec_strided_stream_of_experts(oracle_lib, batch):
+    """OLMoE-shaped gate projections of 16 experts in one launch: enough row
+    tiles for the bulk-copy ring kernel (one CTA per SM, producer warp)."""
+    from m1moe_b200 import matvec4_strided, spec
+    h, I, E = 2048, 1024, 16
+    img = synth.layer_image(11, E, h, I, 64)
+    o = spec.expert_offsets(h, I, 64)
+    eb = spec.expert_bytes(h, I, 64)
+    d = torch.from_numpy(img).cuda()
+    xb = synth.hidden_states(13, batch, h)
+    xf = synth.bf16_to_f32(xb)
+    y = matvec4_strided(d[o["gate_w"]:], d[o["gate_s"]:], d[o["gate_b"]:], eb, E, I, h,
+                        _x_dev(xb, torch.bfloat16))
+    yc = y.cpu().numpy()
+    for e in range(E):
+        parts = synth.split_block(img[e * eb:(e + 1) * eb], h, I, 64)
+        for t in range(batch):
+            ref = oracle_lib.matvec4bit(parts["gate_w"], parts["gate_s"], parts["gate_b"], xf[t], 64,
+                                        nthreads=8)
+            assert rel_max_err(yc[e, t], ref) < TOL, (e, t)
+
+
 def test_matvec_rejects_bad_shapes():
     from m1moe_b200 import M1MoECudaError, matvec4
     w = torch.zeros((4, 12), dtype=torch.int32, device="cuda")  # in_dim 96: not % 64

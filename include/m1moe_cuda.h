@@ -154,6 +154,29 @@ M1MOE_API m1moe_status m1moe_cuda_router_topk(m1moe_cuda_ctx *ctx, int32_t layer
                                     int32_t x_dtype, int32_t batch, int32_t *d_topk_idx,
                                     float *d_topk_w, float *d_scores_out, void *stream);
 
+/* Router top-K for callers that cannot allocate GPU memory (no counterpart in
+ * the reference).  Same results as m1moe_cuda_router_topk, but needs no
+ * context: the caller passes the bf16 router [num_experts][hidden_dim] and x
+ * (16-byte aligned device pointers) and the outputs; the kernel's scratch is
+ * a fixed 49,408-byte array compiled into this library, present on every GPU
+ * that loads it until the process exits.  It calls no cudaMalloc, cudaFree or
+ * other allocating routine, for callers whose memory is allocated up front
+ * or by someone else (a host runtime that owns the GPU heap, a plugin that
+ * may not grow the process's footprint, code that runs where allocation is
+ * not allowed).  Limits: num_experts <= 256, batch <= 8, top_k <= 16.
+ * The first call on a device (with that device current) looks up and clears
+ * the array and waits for the device; make it before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU race,
+ * so issue them on one stream or otherwise one after another.  d_status
+ * (int32, may be NULL) receives 0, or a nonzero error word if a bounded
+ * device wait gave up; d_topk_idx, d_topk_w ([batch][top_k]) and
+ * d_scores_out ([batch][num_experts]) may be NULL. */
+M1MOE_API m1moe_status m1moe_cuda_router_topk_noalloc(const uint16_t *d_router,
+                                    int32_t num_experts, int32_t hidden_dim, int32_t top_k,
+                                    int32_t norm_topk_prob, const void *d_x, int32_t x_dtype,
+                                    int32_t batch, int32_t *d_topk_idx, float *d_topk_w,
+                                    float *d_scores_out, int32_t *d_status, void *stream);
+
 /* One MoE block for `batch` tokens (stream-ordered, device pointers):
  *   out[t] = residual[t] + sum_{k ascending} w[t][k] * Expert_{idx[t][k]}(x[t])
  * with Expert(x) = W_down (silu(W_gate x) * (W_up x)).  Replaces the MoE part of

@@ -53,6 +53,8 @@ _SIGS = [
      [_vp, _vp, _vp, ctypes.c_int64, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
     ("m1moe_cuda_unpack4", ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
     ("m1moe_cuda_router_topk", ctypes.c_int, [_vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
+    ("m1moe_cuda_router_topk_noalloc", ctypes.c_int,
+     [_vp, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     ("m1moe_cuda_moe_layer", ctypes.c_int,
      [_vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp]),
     ("m1moe_cuda_moe_layer_host", ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp]),

@@ -12,6 +12,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -356,6 +357,74 @@ m1moe_status dispatch_layer(m1moe_cuda_ctx *c, const m1::LayerParams &p, cudaStr
     return launch_layer<8>(c, p, st);
 }
 
+// ---- router top-K without allocation (m1moe_cuda_router_topk_noalloc) ----
+// Scratch of the k_moe_layer routing pass in a file-scope device array instead
+// of a context's cudaMalloc'd buffers: the tagged logits (8 tokens x 256
+// experts x 8 bytes), one 128-byte epoch line per CTA for up to 256 CTAs, and
+// the device error word.  49,408 bytes on every GPU that loads the library.
+constexpr int kNoAllocMaxCtas = 256;
+constexpr size_t kNoAllocXlog = (size_t)m1::kMaxTok * m1::kMaxExperts * 8;
+constexpr size_t kNoAllocEpochs = (size_t)kNoAllocMaxCtas * m1::kEpochStride * 4;
+constexpr size_t kNoAllocBytes = kNoAllocXlog + kNoAllocEpochs + 256;
+static __device__ __align__(256) uint8_t g_route_scratch[kNoAllocBytes];
+
+// Per-device address of g_route_scratch (host code cannot use the symbol as a
+// device address) and SM count, looked up once with that device current.
+constexpr int kNoAllocMaxDevices = 64;
+struct NoAllocDevice {
+    std::atomic<int> ready{0};
+    uint8_t *scratch = nullptr;
+    int num_sms = 0;
+};
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+m1moe_status noalloc_setup(int dev, NoAllocDevice *&out) {
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(M1MOE_ERR_UNSUPPORTED, "device %d beyond %d", dev, kNoAllocMaxDevices);
+    NoAllocDevice &d = g_noalloc_dev[dev];
+    if (!d.ready.load(std::memory_order_acquire)) {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!d.ready.load(std::memory_order_relaxed)) {
+            void *ptr = nullptr;
+            M1_CK(cudaGetSymbolAddress(&ptr, g_route_scratch));
+            // epoch words and logit tags must start equal (zero) on every CTA
+            M1_CK(cudaMemset(ptr, 0, kNoAllocBytes));
+            M1_CK(cudaDeviceSynchronize());
+            int n = 0;
+            M1_CK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+            d.scratch = static_cast<uint8_t *>(ptr);
+            d.num_sms = n > 0 ? n : 148;
+            d.ready.store(1, std::memory_order_release);
+        }
+    }
+    out = &d;
+    return M1MOE_OK;
+}
+
+template <int NT>
+m1moe_status launch_route_noalloc(m1::LayerParams p, int grid, cudaStream_t st) {
+    const size_t smem = plan_layer(p, grid, NT, m1::ItemRows<NT>::pairs);
+    if (smem == 0 || smem > kMaxDynSmem)
+        return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
+    M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(m1::kLayerThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, m1::k_moe_layer<NT>, p);
+    if (e != cudaSuccess) return cuda_fail(e, "k_moe_layer (routing) launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return M1MOE_OK;
+}
+
 m1moe_status check_layer(m1moe_cuda_ctx *c, int32_t layer) {
     if (!c) return fail(M1MOE_ERR_INVALID_ARG, "ctx is NULL");
     if (layer < 0 || layer >= c->cfg.num_layers)
@@ -662,6 +731,62 @@ m1moe_status m1moe_cuda_router_topk(m1moe_cuda_ctx *c, int32_t layer, const void
     p.user_scores = d_scores;
     p.route_only = 1;
     return dispatch_layer(c, p, as_stream(stream));
+}
+
+m1moe_status m1moe_cuda_router_topk_noalloc(const uint16_t *d_router, int32_t num_experts,
+                                            int32_t hidden_dim, int32_t top_k,
+                                            int32_t norm_topk_prob, const void *d_x,
+                                            int32_t x_dtype, int32_t B, int32_t *d_idx, float *d_w,
+                                            float *d_scores, int32_t *d_status, void *stream) {
+    const int E = num_experts, h = hidden_dim, K = top_k;
+    if (!d_router || !d_x || !valid_dtype(x_dtype))
+        return fail(M1MOE_ERR_INVALID_ARG, "router/x/x_dtype invalid");
+    if (E < 1 || E > m1::kMaxExperts)
+        return fail(M1MOE_ERR_INVALID_ARG, "num_experts %d outside [1,%d] (fixed scratch size)", E,
+                    m1::kMaxExperts);
+    if (K < 1 || K > E || K > m1::kMaxTopK)
+        return fail(M1MOE_ERR_INVALID_ARG, "top_k %d invalid", K);
+    if (B < 1 || B > m1::kMaxTok)
+        return fail(M1MOE_ERR_INVALID_ARG, "batch %d outside [1,%d] (fixed scratch size)", B,
+                    m1::kMaxTok);
+    if (h <= 0 || h % 64)
+        return fail(M1MOE_ERR_INVALID_ARG, "hidden_dim %d must be a positive multiple of 64", h);
+    if ((reinterpret_cast<uintptr_t>(d_router) | reinterpret_cast<uintptr_t>(d_x)) & 15)
+        return fail(M1MOE_ERR_INVALID_ARG, "router and x must be 16-byte aligned");
+    int dev = 0;
+    M1_CK(cudaGetDevice(&dev));
+    NoAllocDevice *nd = nullptr;
+    if (m1moe_status st = noalloc_setup(dev, nd)) return st;
+    m1::LayerParams p{};
+    // The routing pass of k_moe_layer reads only the router and x; the tiled
+    // layout and intermediate size (64) only size its shared-memory plan.
+    p.tl = m1::make_tiled_layout(h, 64, 64);
+    p.router = d_router;
+    p.E = E;
+    p.K = K;
+    p.h = h;
+    p.I = 64;
+    p.gs = 64;
+    p.norm = norm_topk_prob ? 1 : 0;
+    p.e0 = 0;
+    p.ne = E;
+    p.ntok = B;
+    p.x = d_x;
+    p.x_bf16 = x_dtype == M1MOE_DTYPE_BF16;
+    p.user_idx = d_idx;
+    p.user_w = d_w;
+    p.user_scores = d_scores;
+    p.xlog = reinterpret_cast<unsigned long long *>(nd->scratch);
+    p.epochs = reinterpret_cast<unsigned *>(nd->scratch + kNoAllocXlog);
+    p.err = d_status ? d_status : reinterpret_cast<int *>(nd->scratch + kNoAllocXlog + kNoAllocEpochs);
+    p.route_only = 1;
+    cudaStream_t st = as_stream(stream);
+    M1_CK(cudaMemsetAsync(p.err, 0, sizeof(int), st));
+    const int grid = std::min(nd->num_sms, kNoAllocMaxCtas);
+    if (B == 1) return launch_route_noalloc<1>(p, grid, st);
+    if (B == 2) return launch_route_noalloc<2>(p, grid, st);
+    if (B <= 4) return launch_route_noalloc<4>(p, grid, st);
+    return launch_route_noalloc<8>(p, grid, st);
 }
 
 m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *d_x,

@@ -210,12 +210,12 @@ M1MOE_API int64_t m1moe_cuda_launch_count(void);
  * made afterwards records, per CTA (first 160), the SM cycle counter at each
  * phase event in slots 0-19 and the global nanosecond timer at events 0 and 10
  * in slots 20 and 21; NULL turns tracing off (the default).  Events: 0 start,
- * 1 x staged, 2 logits written, 3 grid barrier 1 passed, 4 routed, 5 first
- * gate/up tile landed, 6 gate/up done, 7 grid barrier 2 passed, 8 down done,
- * 9 producer issued every tile, 10 end, 11 producer issued its first tile,
- * 12 routing: logits loaded, 13 softmax done, 14 top-K ranked, 15 x loaded,
- * 16 x stored to shared memory, 17 gate/up items done, 18 first down item
- * started, 19 producer started. */
+ * 1 x staged and output rows initialised, 2 this CTA's logits published,
+ * 3 top-K ranked, 4 routing done in the whole CTA, 5 first gate/up tile
+ * landed, 6 activations quantised, 7 every CTA's output rows seen
+ * initialised, 8 down items done, 9 producer issued every tile, 10 end,
+ * 11 producer issued its first tile, 17 gate/up items done, 18 first down
+ * item started, 19 producer started (12-16 unused). */
 M1MOE_API m1moe_status m1moe_cuda_set_trace(m1moe_cuda_ctx *ctx, uint64_t *d_trace);
 
 #ifdef __cplusplus

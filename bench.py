@@ -251,14 +251,12 @@ def run_gpu(args, wl) -> None:
         import datetime
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     E, h, I, K, L = wl["E"], wl["h"], wl["I"], wl["K"], wl["layers"]
-    if E % world:
-        raise SystemExit(f"{E} experts do not shard over {world} GPUs")
+    from m1moe_b200.expert_parallel import shard
     b = args.tokens_per_rank
     B = b * world  # tokens every rank applies its experts to
     if B > 8:
         raise SystemExit("at most 8 tokens per MoE call")
-    ne = E // world
-    e0 = rank * ne
+    e0, ne = shard(E, world, rank)
     blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, group_size=wl["gs"],
                    num_layers=L, norm_topk_prob=wl["norm"], max_batch=B, device=local,
                    expert_begin=e0, expert_count=ne)
@@ -271,12 +269,9 @@ def run_gpu(args, wl) -> None:
 
     x0 = torch.from_numpy(synth.hidden_states(SEED + 7 + rank, b, h).view(np.int16)).to(dev)
     x0 = x0.view(torch.bfloat16)
-    xa = torch.zeros((B, h), dtype=torch.float32, device=dev)   # gathered layer inputs
-    res = torch.zeros((B, h), dtype=torch.float32, device=dev)  # own rows only, else 0
-    part = torch.zeros((B, h), dtype=torch.float32, device=dev)  # partial sums (EP)
+    part = torch.zeros((B, h), dtype=torch.float32, device=dev)  # layer output (1 GPU)
     own = torch.zeros((b, h), dtype=torch.float32, device=dev)   # this rank's token state
     own.copy_(x0.float())
-    nxt = torch.zeros((b, h), dtype=torch.float32, device=dev)   # reduce-scatter result
     idx_log = torch.zeros((L, B, K), dtype=torch.int32, device=dev)
     w_log = torch.zeros((L, B, K), dtype=torch.float32, device=dev)
     stream = torch.cuda.Stream(device=dev)
@@ -293,18 +288,27 @@ def run_gpu(args, wl) -> None:
             if events is not None:
                 events[L].record()
     else:
-        # Expert parallel: gather every rank's token, apply the local experts
-        # to all of them, reduce-scatter the partial sums back to the owners.
+        # Expert parallel (m1moe_b200.expert_parallel): gather every rank's
+        # token, apply the local experts to all of them, reduce-scatter the
+        # partial sums back to the owners.
+        from m1moe_b200.expert_parallel import EPStep
+        cur = {"layer": 0}
+
+        def local(x_all, res_all, out_all):
+            layer = cur["layer"]
+            _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, x_all.data_ptr(), 0,
+                      res_all.data_ptr(), 0, out_all.data_ptr(), 0, B, idx_log[layer].data_ptr(),
+                      w_log[layer].data_ptr(), stream.cuda_stream)
+
+        ep = EPStep(local, b, h, device=dev)
+        nxt = ep.out
+
         def one_step(events=None):
             for layer in range(L):
                 if events is not None:
                     events[layer].record()
-                dist.all_gather_into_tensor(xa, own)
-                res[rank * b:(rank + 1) * b].copy_(own)
-                _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, xa.data_ptr(), 0,
-                          res.data_ptr(), 0, part.data_ptr(), 0, B, idx_log[layer].data_ptr(),
-                          w_log[layer].data_ptr(), stream.cuda_stream)
-                dist.reduce_scatter_tensor(nxt, part)
+                cur["layer"] = layer
+                ep(own)
             if events is not None:
                 events[L].record()
 

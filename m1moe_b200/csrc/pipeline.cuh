@@ -3,8 +3,8 @@
 // complete on an mbarrier, bounded mbarrier waits, L2 eviction hints and
 // Programmatic Dependent Launch (griddepcontrol).
 //
-// No cluster multicast is used anywhere: every CTA fetches its own tiles from
-// this GPU's memory.
+// Every CTA fetches its own tiles from this GPU's memory; no copy is shared
+// between CTAs.
 #pragma once
 
 #include <stdint.h>

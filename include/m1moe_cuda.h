@@ -214,8 +214,10 @@ M1MOE_API int64_t m1moe_cuda_launch_count(void);
  * 3 top-K ranked, 4 routing done in the whole CTA, 5 first gate/up tile
  * landed, 6 activations quantised, 7 every CTA's output rows seen
  * initialised, 8 down items done, 9 producer issued every tile, 10 end,
- * 11 producer issued its first tile, 17 gate/up items done, 18 first down
- * item started, 19 producer started (12-16 unused). */
+ * 11 producer issued its first tile, 12 every logit seen, 13 ranks counted,
+ * 17 gate/up items done, 18 first down item started, 19 producer started;
+ * slots 14 and 15 hold values, not times: the CTA's gate/up row range
+ * (first | end << 32) and its tile counts (gate/up | down << 32); 16 unused. */
 M1MOE_API m1moe_status m1moe_cuda_set_trace(m1moe_cuda_ctx *ctx, uint64_t *d_trace);
 
 #ifdef __cplusplus

@@ -164,7 +164,8 @@ struct m1moe_cuda_ctx {
     uint8_t *table = nullptr;     // [layers][ne] tiled blocks
     uint16_t *router = nullptr;   // [layers][E][h]
     std::vector<uint8_t> layer_loaded, router_loaded;
-    unsigned long long *xlog = nullptr;  // [max_batch][E] tagged logits
+    unsigned long long *xlog = nullptr;  // [nbox][max_batch][E] tagged logits, a box per CTA
+    int nbox = 0;                        // = the layer kernel's grid
     float *acc = nullptr;                // [max_batch][h] fp32 sums for bf16 output
     int *done = nullptr;                 // CTAs finished with their atomics (bf16 output)
     unsigned *epochs = nullptr;          // per-CTA call counters (moe_layer.cuh)
@@ -227,7 +228,7 @@ cudaError_t clear_exchange(m1moe_cuda_ctx *c) {
     const m1moe_cuda_cfg &g = c->cfg;
     cudaError_t e = cudaMemset(c->epochs, 0, kEpochBytes);
     if (e == cudaSuccess) e = cudaMemset(c->done, 0, 4);
-    if (e == cudaSuccess) e = cudaMemset(c->xlog, 0, (size_t)g.max_batch * g.num_experts * 8);
+    if (e == cudaSuccess) e = cudaMemset(c->xlog, 0, (size_t)c->nbox * g.max_batch * g.num_experts * 8);
     return e;
 }
 
@@ -247,6 +248,8 @@ m1::LayerParams layer_params(m1moe_cuda_ctx *c, int layer, int B) {
     p.ne = c->ne;
     p.ntok = B;
     p.xlog = c->xlog;
+    p.nbox = c->nbox;
+    p.box_words = g.max_batch * g.num_experts;
     p.acc = c->acc;
     p.done = c->done;
     p.epochs = c->epochs;
@@ -302,6 +305,7 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     const size_t actf = take((size_t)nt * p.act_cb * 8 * 4);
     const size_t act = take((size_t)nt * p.act_cb * 16);
     const size_t xseg = take((size_t)nt * p.xseg_max * 8);
+    const size_t blk = take((size_t)nt * p.act_cb * 8);
     const size_t keys = take((size_t)nt * p.E * 8);
     const size_t rlog = take((size_t)nt * p.E * 4);
     const size_t lpart = take(8 * m1::kMaxTok * 4);
@@ -319,6 +323,7 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     p.off_actf = (int)(base + actf);
     p.off_act = (int)(base + act);
     p.off_xseg = (int)(base + xseg);
+    p.off_blk = (int)(base + blk);
     p.off_keys = (int)(base + keys);
     p.off_rlog = (int)(base + rlog);
     p.off_lpart = (int)(base + lpart);
@@ -327,7 +332,7 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
 
 template <int NT>
 m1moe_status launch_layer(m1moe_cuda_ctx *c, m1::LayerParams p, cudaStream_t st) {
-    const int grid = std::min(c->num_sms, m1::kMaxCtas);
+    const int grid = c->nbox;  // one CTA per SM, each with its own logit box
     const size_t smem = plan_layer(p, grid, NT, m1::ItemRows<NT>::pairs);
     if (smem == 0 || smem > kMaxDynSmem)
         return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
@@ -509,6 +514,7 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     c->layer_loaded.assign(g.num_layers, 0);
     c->router_loaded.assign(g.num_layers, 0);
     c->num_sms = sm_count();
+    c->nbox = std::min(c->num_sms, m1::kMaxCtas);
     const size_t B = g.max_batch, E = g.num_experts, K = g.top_k;
     cudaError_t e;
 #define M1_ALLOC(ptr, bytes)                                        \
@@ -520,7 +526,7 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     }
     M1_ALLOC(c->table, (size_t)g.num_layers * ne * c->tl.block);
     M1_ALLOC(c->router, (size_t)g.num_layers * E * g.hidden_dim * 2);
-    M1_ALLOC(c->xlog, B * E * 8);
+    M1_ALLOC(c->xlog, (size_t)c->nbox * B * E * 8);
     M1_ALLOC(c->acc, B * g.hidden_dim * 4);
     M1_ALLOC(c->done, 4);
     M1_ALLOC(c->epochs, kEpochBytes);
@@ -777,6 +783,8 @@ m1moe_status m1moe_cuda_router_topk_noalloc(const uint16_t *d_router, int32_t nu
     p.user_w = d_w;
     p.user_scores = d_scores;
     p.xlog = reinterpret_cast<unsigned long long *>(nd->scratch);
+    p.nbox = 1;  // one shared box: the fixed scratch has no room for a box per CTA
+    p.box_words = 0;
     p.epochs = reinterpret_cast<unsigned *>(nd->scratch + kNoAllocXlog);
     p.err = d_status ? d_status : reinterpret_cast<int *>(nd->scratch + kNoAllocXlog + kNoAllocEpochs);
     p.route_only = 1;

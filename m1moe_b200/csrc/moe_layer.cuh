@@ -8,9 +8,9 @@
 //
 // One CTA per SM (cooperative launch: every CTA is resident, which the waits
 // on other CTAs need).  Phases:
-//   1. warps 8..24 stage x in shared memory as bf16 pair-permuted chunks with
-//      fp32 chunk sums (common.cuh) and initialise this CTA's rows of the
-//      output with the residual (or zero); meanwhile
+//   1. warps 8..24 stage x in shared memory as int16 chunks with per-chunk
+//      scales and exact fp32 sums (common.cuh) and initialise this CTA's rows
+//      of the output with the residual (or zero); meanwhile
 //   2. warps 0..7 compute logits[t][e] = W_r[e] . x[t] for this CTA's experts
 //      straight from global memory (bf16 router upcast exactly, the caller's
 //      x, fp32 FMA, fixed reduction order), publish them as TAGGED words
@@ -18,7 +18,7 @@
 //   3. route every token from all logits (identical in every CTA,
 //      deterministic): top-K by rank (descending, ties to the lower index),
 //      distinct local experts; the softmax weights (with optional
-//      renormalisation) are computed beside the expert list;
+//      renormalisation) are computed while the first copies are in flight;
 //   4. the routed experts' gate/up rows, concatenated, are split over the CTAs
 //      in runs of 8 rows.  A producer warp streams this CTA's gate/up tiles and
 //      then the matching COLUMNS of the down matrices (split-K; the table
@@ -105,7 +105,8 @@ struct LayerParams {
     int out_bf16;
     float *acc;       // [ntok][h] fp32 sums for bf16 output
     int *done;        // CTAs finished with their atomics (bf16 output)
-    unsigned long long *xlog;  // [kMaxTok][E] tagged logits {tag, f32}
+    unsigned long long *xlog;  // [nbox][box_words] tagged logits {tag, f32}, box = [ntok][E]
+    int nbox, box_words;       // logit boxes (CTA c reads box c % nbox) and their stride
     unsigned *epochs;          // [kMaxCtas * kEpochStride] per-CTA call counters
     int *user_idx;    // optional [ntok][K]
     float *user_w;    // optional [ntok][K]
@@ -120,7 +121,8 @@ struct LayerParams {
     int xseg_max;     // activation groups per token (scale and sum)
     int route_only;   // stop after routing (m1moe_cuda_router_topk)
     // shared-memory offsets (bytes, 16-aligned)
-    int off_bars, off_ctl, off_xs, off_xsum, off_gup, off_actf, off_act, off_xseg, off_keys, off_rlog,
+    int off_bars, off_ctl, off_xs, off_xsum, off_gup, off_actf, off_act, off_xseg, off_blk, off_keys,
+        off_rlog,
         off_lpart;
 };
 
@@ -141,6 +143,7 @@ struct Ctl {
     int a, b;              // this CTA's gate/up rows [a, b) of the distinct-expert row space
     int ntg, ntd;          // gate/up and down tiles of this CTA
     int last;              // this CTA finished last (bf16 output)
+    int epochs_seen;       // every CTA's output rows are initialised (1)
     int stage_tile[kMaxStages];  // tile whose copy was last issued into each stage
     int stage_done[kMaxStages];  // work items finished on each stage's current tile
     StageGeo geo[kMaxStages];
@@ -173,6 +176,22 @@ __device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned l
 
 __device__ __forceinline__ unsigned long long tagged(unsigned tag, uint32_t payload) {
     return ((unsigned long long)tag << 32) | payload;
+}
+
+__device__ __forceinline__ int ld_acquire_cta_shared(const int *p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];"
+                 : "=r"(v)
+                 : "r"((unsigned)__cvta_generic_to_shared(p))
+                 : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_cta_shared(int *p, int v) {
+    asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(
+                     (unsigned)__cvta_generic_to_shared(p)),
+                 "r"(v)
+                 : "memory");
 }
 
 __device__ __forceinline__ void set_abort(Ctl &ctl, int *err) {
@@ -233,6 +252,7 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
     const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E;
     // a. collect the tagged logits (all of this thread's loads in flight at once)
     constexpr int kPer = kMaxTok * kMaxExperts / 256;
+    const unsigned long long *box = p.xlog + (size_t)(blockIdx.x % p.nbox) * p.box_words;
     bool ok = false;
     unsigned long long w[kPer];
     for (uint32_t it = 0, nap = 32; it < kWaitLimit; ++it) {
@@ -240,7 +260,7 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
             const int i = tid + 256 * j;
-            if (i < nel) w[j] = ld_relaxed_u64(p.xlog + i);
+            if (i < nel) w[j] = ld_relaxed_u64(box + i);
         }
 #pragma unroll
         for (int j = 0; j < kPer; ++j)
@@ -268,6 +288,7 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
         }
     }
     if (!named_sync_and(2, 256, ok)) return false;
+    if (tid == 0) trace_event(p.trace, 0, 12);
     // b. rank of every (token, expert): P threads per element, each counting
     //    the keys above it in one slice of the token's E keys
     int lp = 0;
@@ -289,6 +310,7 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
         if (i < nel && part == 0 && cnt < K) rs.idx[t][cnt] = e;
     }
     named_sync(2, 256);
+    if (tid == 0) trace_event(p.trace, 0, 13);
     // c. local-expert marks
     for (int i = tid; i < ntok * K; i += 256) {
         int t = 0, k = i;
@@ -381,6 +403,18 @@ __device__ __forceinline__ int grab(int *counter) {
     return __shfl_sync(0xffffffffu, q, 0);
 }
 
+// End of the down-tile run that starts at column block cb (this CTA's blocks
+// end at b8; ncbE blocks per expert, gcb per group): a run stays inside one
+// expert, ends on a group boundary unless it ends the CTA's range (a group's
+// bias term b*X uses the CTA's whole part of the group, so a group must not
+// be split between two tiles), and spans at most mcb blocks from the start
+// of cb's group, so it touches at most mcb/gcb groups (the stage holds mcb
+// weight blocks and mcb/gcb scale/bias rows).
+__device__ __forceinline__ int dn_run_end(int cb, int b8, int ncbE, int gcb, int mcb) {
+    const int uend = (cb / ncbE + 1) * ncbE;
+    return min(min(b8, uend), (cb / gcb) * gcb + mcb);
+}
+
 __device__ __forceinline__ float swiglu(float g, float u) {
     return (g / (1.0f + expf(-g))) * u;  // Shaders.metal:147-148: SiLU(gate) * up
 }
@@ -414,6 +448,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     float *gup = reinterpret_cast<float *>(smem + p.off_gup);
     uint32_t *act = reinterpret_cast<uint32_t *>(smem + p.off_act);   // [ntok][act_cb][4] int16 pairs
     float *xseg = reinterpret_cast<float *>(smem + p.off_xseg);        // [seg][ntok] sums, then scales
+    float *bst = reinterpret_cast<float *>(smem + p.off_blk);          // [cb][ntok] block max, sum
     unsigned long long *keys = reinterpret_cast<unsigned long long *>(smem + p.off_keys);
     float *rlog = reinterpret_cast<float *>(smem + p.off_rlog);
     float *lpart = reinterpret_cast<float *>(smem + p.off_lpart);
@@ -425,6 +460,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     if (tid == 0) {
         trace_event(p.trace, 0, 0);
         ctl.abort = 0;
+        ctl.epochs_seen = 0;
         const unsigned t1 = ld_relaxed_u32(my_epoch) + 1u;
         ctl.tag = t1 ? t1 : 1u;
     }
@@ -484,10 +520,20 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 if (lane == 0) lpart[warp * kMaxTok + t] = v;
             }
             named_sync(2, 256);
-            if (tid < p.ntok) {
+            // publish into every CTA's box (each box is polled by its CTAs only)
+            uint32_t sv[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
                 float s = 0.f;
-                for (int w = 0; w < 8; ++w) s += lpart[w * kMaxTok + tid];
-                st_relaxed_u64(p.xlog + (size_t)tid * p.E + e, tagged(tag, __float_as_uint(s)));
+                if (t < p.ntok)
+                    for (int w = 0; w < 8; ++w) s += lpart[w * kMaxTok + t];
+                sv[t] = __float_as_uint(s);
+            }
+            for (int bx = tid; bx < p.nbox; bx += 256) {
+                unsigned long long *box = p.xlog + (size_t)bx * p.box_words + e;
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+                    if (t < p.ntok) st_relaxed_u64(box + (size_t)t * p.E, tagged(tag, sv[t]));
             }
             named_sync(2, 256);
         }
@@ -518,27 +564,24 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 // gate/up rows [a, b) of the distinct-expert row space
                 // (expert u's rows are u*I .. u*I+I-1), cut in units of 8
                 // rows so that row pairs (R, R+4) stay together.
-                const int units = nU * (I / 8);
-                const int a = (int)((long long)units * blk / G) * 8;
-                const int b = (int)((long long)units * (blk + 1) / G) * 8;
+                const int units = nU * (I / 8);  // units * G < 2^31 (kMaxPairs, I, kMaxCtas)
+                const int a = units * blk / G * 8;
+                const int b = units * (blk + 1) / G * 8;
                 const int GT = p.gu_tile_rows, MCB = p.dn_max_cb, nic = h / tl.rc;
                 ctl.a = a;
                 ctl.b = b;
                 ctl.ntg = (b > a) ? (b - 1) / GT - a / GT + 1 : 0;
                 // down tiles: per expert segment of [a, b), column-block runs
-                // cut at multiples of MCB, times the row chunks
+                // (dn_run_end), times the row chunks
+                const int gcb = p.gs / 8;
                 int ntd = 0;
                 for (int cb = a >> 3; cb < (b >> 3);) {
-                    const int uend = (cb / (I / 8) + 1) * (I / 8);
-                    const int cend = min(min(b >> 3, uend), (cb / MCB + 1) * MCB);
+                    const int cend = dn_run_end(cb, b >> 3, I / 8, gcb, MCB);
                     ntd += nic;
                     cb = cend;
                 }
                 ctl.ntd = ntd;
             }
-        } else {
-            // the routing weights (needed only by the atomics at the end)
-            for (int t = warp - 1; t < p.ntok; t += 7) route_weights(p, rs, rlog, t);
         }
     } else {
         // ---- phase 1 (warps 8..24): pipeline set-up, x staging, output rows ----
@@ -576,14 +619,32 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             load_x32_any(p.x, p.x_bf16, (size_t)t * h + (size_t)c * kChunkCols, v);
             xsc[q] = quant_chunk_i16(v, xq + (size_t)t * (h / 2), nch, c, &xsum[q]);
         }
-        if (warp == 8 && !p.route_only) {
-            if (!wait_all_epochs(p.epochs, G, tag, vabort) && lane == 0) set_abort(ctl, p.err);
-            if (lane == 0) trace_event(p.trace, 0, 7);
-        }
     }
     __syncthreads();
-    if (tid == 0) trace_event(p.trace, 0, 4);
-    if (p.route_only || ctl.abort) return;  // uniform; no copies were issued
+    if (tid == 0) {
+        trace_event(p.trace, 0, 4);
+        trace_value(p.trace, 0, 14, (unsigned)ctl.a | ((unsigned long long)(unsigned)ctl.b << 32));
+        trace_value(p.trace, 0, 15, (unsigned)ctl.ntg | ((unsigned long long)(unsigned)ctl.ntd << 32));
+    }
+    // the routing weights: needed only by the caller's outputs and the final
+    // atomics, so warps 1..7 compute them while the first copies are in flight
+    if (warp >= 1 && warp < 8 && !ctl.abort)
+        for (int t = warp - 1; t < p.ntok; t += 7) route_weights(p, rs, rlog, t);
+    if (p.route_only || ctl.abort) {
+        if (p.route_only) __syncthreads();  // user outputs complete before the epoch advances
+        return;  // uniform; no copies were issued
+    }
+    // Every CTA's output rows must be initialised before this CTA's first
+    // atomic, long after this point: warp 8 checks the epoch words here, off
+    // the path to the first weight copy, and the down items wait for its flag.
+    if (warp == 8) {
+        if (wait_all_epochs(p.epochs, G, tag, vabort)) {
+            if (lane == 0) st_release_cta_shared(&ctl.epochs_seen, 1);
+        } else if (lane == 0) {
+            set_abort(ctl, p.err);
+        }
+        if (lane == 0) trace_event(p.trace, 0, 7);
+    }
 
     // ---- phase 4 geometry ----
     const int GT = p.gu_tile_rows, MCB = p.dn_max_cb, RC = tl.rc, nic = h / RC;
@@ -635,12 +696,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 }
             }
             // down tiles: the same rows as columns of the down matrices, in
-            // runs of at most MCB column blocks (cut at multiples of MCB, so a
-            // group never straddles two tiles); row chunk by row chunk
+            // runs (dn_run_end); row chunk by row chunk
             for (int ic = 0; ic < nic && ok && ntd > 0; ++ic) {
                 for (int cb = a8; cb < (b >> 3) && ok;) {
-                    const int u = cb / ncbE, uend = (u + 1) * ncbE;
-                    const int cend = min(min(b >> 3, uend), (cb / MCB + 1) * MCB);
+                    const int u = cb / ncbE;
+                    const int cend = dn_run_end(cb, b >> 3, ncbE, gcb, MCB);
                     const int lcb = cb - u * ncbE, ncb = cend - cb;
                     const int lg0 = lcb / gcb, lg1 = (lcb + ncb - 1) / gcb;
                     const uint8_t *blkp = p.table + (size_t)(rs.ulist[u] - p.e0) * tl.block;
@@ -745,55 +805,65 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         }
         if (tid == 0) trace_event(p.trace, 0, 17);
         named_sync(1, kConsumerThreads);  // every gate/up item of this CTA is done
+        // Activations of this CTA's rows, in three short passes: (1) one thread
+        // per (row, token) sums the column slices in order and applies SwiGLU
+        // where items left partial sums; (2) one per (8-row column block,
+        // token): the block's max |a| and sum; (3) one per (block, token): the
+        // group's (gs rows) max from its blocks, the block as int16 pairs in the
+        // dp2a layout (4 words, as for x), and per group the scale and exact sum.
+        const int ncb_cta = (b - a) >> 3, arows = p.act_cb * 8;
         if (nslg > 1) {
-            // sum the column slices in order, SwiGLU
-            if (!ctl.abort) {
-                for (int i = tid; i < (b - a) / 2 * NT; i += kConsumerThreads) {
-                    const int slot = i / NT, k = i % NT;
-                    const int lr = 8 * (slot >> 2) + (slot & 3);  // row R - a; R+4 is lr + 4
-                    const int Ru = a + lr, u = Ru / I;
-                    const int e = rs.ulist[u];
-                    if (!((rs.tmask[e] >> k) & 1u)) continue;
-                    float gv[2] = {0.f, 0.f}, uv[2] = {0.f, 0.f};
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh)
-                        for (int jj = 0; jj < nslg; ++jj) {
-                            const float *gp = gup + ((size_t)(lr + 4 * hh) * nslg + jj) * (2 * NT) + 2 * k;
-                            gv[hh] += gp[0];
-                            uv[hh] += gp[1];
-                        }
-                    put_act(actf, p.act_cb * 8, a, k, Ru, swiglu(gv[0], uv[0]), swiglu(gv[1], uv[1]));
+            for (int i = tid; i < (b - a) * NT; i += kConsumerThreads) {
+                const int lr = i / NT, k = i % NT;
+                const int e = rs.ulist[(a + lr) / I];
+                if (ctl.abort || !((rs.tmask[e] >> k) & 1u)) continue;
+                float gv = 0.f, uv = 0.f;
+                const float *gp = gup + (size_t)lr * nslg * (2 * NT) + 2 * k;
+                for (int jj = 0; jj < nslg; ++jj) {
+                    gv += gp[jj * 2 * NT];
+                    uv += gp[jj * 2 * NT + 1];
                 }
+                actf[(size_t)k * arows + lr] = swiglu(gv, uv);
             }
             named_sync(1, kConsumerThreads);
         }
-        // quantise the activations per (group of this CTA's range, token):
-        // int16 pairs in the dp2a layout of one column block (4 words per 8
-        // rows, as for x), the group's scale and its exact sum
-        const int nseg = b > a ? (b - 1) / p.gs - ag + 1 : 0;
-        for (int i = tid; i < nseg * NT; i += kConsumerThreads) {
-            const int sg = i / NT, k = i % NT;
-            const int c_lo = max((ag + sg) * gcb, a8), c_hi = min((ag + sg + 1) * gcb, b >> 3);
-            const float *f = actf + (size_t)k * p.act_cb * 8 + (c_lo - a8) * 8;
-            const int n = (c_hi - c_lo) * 8;
+        for (int i = tid; i < ncb_cta * NT; i += kConsumerThreads) {
+            const int cb = i / NT, k = i % NT;
+            const float *f = actf + (size_t)k * arows + 8 * cb;
             float m = 0.f, s0 = 0.f, s1 = 0.f;
-            for (int j = 0; j < n; j += 2) {
-                m = fmaxf(m, fmaxf(fabsf(f[j]), fabsf(f[j + 1])));
-                s0 += f[j];
-                s1 += f[j + 1];
+#pragma unroll
+            for (int jr = 0; jr < 8; jr += 2) {
+                m = fmaxf(m, fmaxf(fabsf(f[jr]), fabsf(f[jr + 1])));
+                s0 += f[jr];
+                s1 += f[jr + 1];
             }
+            bst[2 * i] = m;
+            bst[2 * i + 1] = s0 + s1;
+        }
+        named_sync(1, kConsumerThreads);
+        for (int i = tid; i < ncb_cta * NT; i += kConsumerThreads) {
+            const int cb = i / NT, k = i % NT;
+            const int R0 = a + 8 * cb, e = rs.ulist[R0 / I];
+            if (ctl.abort || !((rs.tmask[e] >> k) & 1u)) continue;
+            const int gg = (a8 + cb) / gcb;
+            const int c_lo = max(gg * gcb, a8) - a8, c_hi = min((gg + 1) * gcb, b >> 3) - a8;
+            float m = 0.f;
+            for (int c = c_lo; c < c_hi; ++c) m = fmaxf(m, bst[2 * (c * NT + k)]);
             const float inv = m > 0.f ? 32767.0f / m : 0.f;
-            uint32_t *o = act + (((size_t)k * p.act_cb + (c_lo - a8)) << 2);
-            for (int c = 0; c < c_hi - c_lo; ++c) {
-                const float *x = f + 8 * c;
-                auto qz = [&](float v) { return (uint32_t)(__float2int_rn(v * inv) & 0xFFFF); };
-                o[4 * c + 0] = qz(x[0]) | (qz(x[2]) << 16);
-                o[4 * c + 1] = qz(x[4]) | (qz(x[6]) << 16);
-                o[4 * c + 2] = qz(x[1]) | (qz(x[3]) << 16);
-                o[4 * c + 3] = qz(x[5]) | (qz(x[7]) << 16);
+            const float *x = actf + (size_t)k * arows + 8 * cb;
+            auto qz = [&](float v) { return (uint32_t)(__float2int_rn(v * inv) & 0xFFFF); };
+            uint32_t *o = act + (((size_t)k * p.act_cb + cb) << 2);
+            o[0] = qz(x[0]) | (qz(x[2]) << 16);
+            o[1] = qz(x[4]) | (qz(x[6]) << 16);
+            o[2] = qz(x[1]) | (qz(x[3]) << 16);
+            o[3] = qz(x[5]) | (qz(x[7]) << 16);
+            if (cb == c_lo) {  // the group's first block of this range: scale and sum
+                float sum = 0.f;
+                for (int c = c_lo; c < c_hi; ++c) sum += bst[2 * (c * NT + k) + 1];
+                float *xg = xseg + ((size_t)(gg - ag) * NT + k) * 2;
+                xg[0] = sum;
+                xg[1] = m * (1.0f / 32767.0f);
             }
-            xseg[2 * i] = s0 + s1;
-            xseg[2 * i + 1] = m * (1.0f / 32767.0f);
         }
         named_sync(1, kConsumerThreads);
         if (tid == 0) trace_event(p.trace, 0, 6);
@@ -807,6 +877,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         const int nsub = nic ? ntd / nic : 0;  // down tiles per row chunk
         const int nd_items = (ctl.abort || ntd == 0) ? 0 : nic * ipt_d;
         float *dst = p.out_bf16 ? p.acc : reinterpret_cast<float *>(p.out);
+        bool seen = false;  // epochs_seen observed (acquire) by this warp
         for (;;) {
             const int q = grab(&ctl.next_dn);
             if (q >= nd_items) break;
@@ -875,6 +946,20 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 release_item(empty, ctl, s, ipt_d);
             }
             if (!ok) break;
+            if (!seen) {
+                if (lane == 0) {
+                    for (uint32_t it = 0; it < kWaitLimit && !seen; ++it) {
+                        seen = ld_acquire_cta_shared(&ctl.epochs_seen) != 0;
+                        if (!seen) {
+                            if (*vabort) break;
+                            __nanosleep(64);
+                        }
+                    }
+                    if (!seen && !*vabort) set_abort(ctl, p.err);
+                }
+                seen = __shfl_sync(0xffffffffu, seen, 0);
+                if (!seen) break;
+            }
             const int i = ic * RC + ri;
 #pragma unroll
             for (int t = 0; t < NT; ++t)

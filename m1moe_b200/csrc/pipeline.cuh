@@ -111,6 +111,13 @@ __device__ __forceinline__ void trace_event(unsigned long long *trace, int kerne
     }
 }
 
+// A value (not a time) into trace slot `slot` of this CTA's row.
+__device__ __forceinline__ void trace_value(unsigned long long *trace, int kernel, int slot,
+                                            unsigned long long v) {
+    if (trace == nullptr || blockIdx.x >= kTraceCtas) return;
+    trace[((size_t)kernel * kTraceCtas + blockIdx.x) * kTraceSlots + slot] = v;
+}
+
 // Named barrier over the first `nthreads` threads (a multiple of 32).
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -151,6 +151,7 @@ cudaError_t launch_matvec_nt(const m1::MatvecParams &p, int num_sms, cudaStream_
 }
 
 constexpr size_t kStageTarget = 40 * 1024;  // bulk copies this large run at HBM speed
+static_assert(m1::kLayerSlots <= m1::kMaxStages, "slot arrays are kMaxStages long");
 constexpr size_t kStagingBytes = 256u << 20;  // device staging for cold-start repacking
 
 }  // namespace
@@ -286,7 +287,16 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     p.gu_tile_rows = divisor_tile(p.I, 8, std::max<long long>(8, stage_target / tl.pr));
     p.stage_bytes = (int)m1::round_up_ll(std::max<long long>(p.gu_tile_rows * tl.pr, dn_bytes), 128);
     p.gu_nslices = nt <= 2 ? (nch + 31) / 32 : 1;
-    (void)pg;
+    p.nic = p.h / tl.rc;
+    p.fd_G = m1::make_fastdiv(grid);
+    p.fd_GT = m1::make_fastdiv(p.gu_tile_rows);
+    p.fd_I = m1::make_fastdiv(p.I);
+    p.fd_ncbE = m1::make_fastdiv(p.I / 8);
+    p.fd_gcb = m1::make_fastdiv(gcb);
+    p.fd_gs = m1::make_fastdiv(p.gs);
+    p.fd_iptg = m1::make_fastdiv((p.gu_tile_rows / 2 / pg) * p.gu_nslices);
+    p.fd_nslg = m1::make_fastdiv(p.gu_nslices);
+    p.fd_iptd = m1::make_fastdiv(tl.rc / 32);
     const long long units = (long long)maxU * (p.I / 8);
     p.gu_rows_max = (int)((units + grid - 1) / grid) * 8;
     p.act_cb = p.gu_rows_max / 8;
@@ -310,11 +320,14 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     const size_t rlog = take((size_t)nt * p.E * 4);
     const size_t lpart = take(8 * m1::kMaxTok * 4);
     const size_t fixed = off;
-    const size_t per_stage = (size_t)p.stage_bytes + 2 * sizeof(uint64_t);
-    if (fixed + 2 * per_stage + 16 > kMaxDynSmem) return 0;
-    p.nstages = (int)std::min<size_t>(m1::kMaxStages, (kMaxDynSmem - fixed - 16) / per_stage);
-    const size_t bars = (size_t)p.nstages * p.stage_bytes;
-    const size_t base = align16(bars + 2 * sizeof(uint64_t) * p.nstages);
+    // the tile ring: everything else, tiles packed back to back, at most
+    // kLayerSlots of them in flight (each slot has a full and an empty barrier)
+    const size_t bar_bytes = 2 * sizeof(uint64_t) * (size_t)m1::kLayerSlots;
+    if (fixed + bar_bytes + 32 > kMaxDynSmem) return 0;
+    p.ring_bytes = (int)((kMaxDynSmem - fixed - bar_bytes - 16) / 128 * 128);
+    if (p.ring_bytes < 2 * p.stage_bytes) return 0;
+    const size_t bars = (size_t)p.ring_bytes;
+    const size_t base = align16(bars + bar_bytes);
     p.off_bars = (int)bars;
     p.off_ctl = (int)(base + ctl);
     p.off_xs = (int)(base + xs);

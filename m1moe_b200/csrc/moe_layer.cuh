@@ -65,6 +65,7 @@ constexpr int kConsumerWarps = 24;
 constexpr int kLayerThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kMaxStages = 32;
+constexpr int kLayerSlots = 32;  // tiles in flight per CTA at most (a power of two)
 constexpr int kMaxCtas = 1024;
 constexpr int kEpochStride = 32;  // words between two CTAs' epoch words (own 128-byte line)
 
@@ -114,39 +115,56 @@ struct LayerParams {
     int *err;         // device error word
     unsigned long long *trace;  // optional phase timestamps
     // geometry (host-planned)
-    int stage_bytes, nstages;
+    int stage_bytes;       // largest tile (bytes)
+    int ring_bytes;        // bytes of the tile ring
     int gu_tile_rows, gu_nslices, gu_rows_max;  // pair-rows per tile (multiple of 8, divides I)
     int dn_max_cb;    // column blocks per down tile (a multiple of gs/8)
     int act_cb;       // activation capacity, column blocks per token (gu_rows_max / 8)
     int xseg_max;     // activation groups per token (scale and sum)
     int route_only;   // stop after routing (m1moe_cuda_router_topk)
+    int nic;          // row chunks of the down matrices (h / tl.rc)
+    // divisors known on the host: grid, gate/up tile rows, I, column blocks
+    // per expert and per group, group size, items per gate/up tile, column
+    // slices, items per down tile
+    FastDiv fd_G, fd_GT, fd_I, fd_ncbE, fd_gcb, fd_gs, fd_iptg, fd_nslg, fd_iptd;
     // shared-memory offsets (bytes, 16-aligned)
     int off_bars, off_ctl, off_xs, off_xsum, off_gup, off_actf, off_act, off_xseg, off_blk, off_keys,
         off_rlog,
         off_lpart;
 };
 
-// The tile in a ring stage.  Gate/up: distinct expert u, first pair-row r0 of
+// The tile in a ring slot.  Gate/up: distinct expert u, first pair-row r0 of
 // the expert, row count nr (ic = -1).  Down: distinct expert u, first column
 // block cb0 (in the concatenated row space, 8 rows per block), ncb blocks,
-// row chunk ic.
+// row chunk ic.  off: its first byte in the ring.
 struct StageGeo {
-    int u, r0, nr, ic;
+    int u, r0, nr, ic, off;
+};
+
+// A tile's bulk copies: b0 bytes from src0, then b1 bytes from src1.
+struct TileCopy {
+    const uint8_t *src0, *src1;
+    uint32_t b0, b1;
+    StageGeo g;
 };
 
 struct Ctl {
     RouteInfo route;
     unsigned tag;       // this call's tag (epoch + 1, never 0)
     int abort;
+    int route_ok;       // warps 0..7 routed this call (written before barrier 3)
     int next_gu, next_dn;  // work-item counters
     int issued;            // tiles issued by the producer
     int a, b;              // this CTA's gate/up rows [a, b) of the distinct-expert row space
     int ntg, ntd;          // gate/up and down tiles of this CTA
+    int nsub;              // down tiles per row chunk (ntd = nsub * nic)
     int last;              // this CTA finished last (bf16 output)
     int epochs_seen;       // every CTA's output rows are initialised (1)
-    int stage_tile[kMaxStages];  // tile whose copy was last issued into each stage
-    int stage_done[kMaxStages];  // work items finished on each stage's current tile
+    int stage_tile[kMaxStages];  // tile whose copy was last issued into each slot
+    int stage_done[kMaxStages];  // work items finished on each slot's current tile
+    int vstart[kMaxStages];      // producer: running byte position of each slot's tile
     StageGeo geo[kMaxStages];
+    TileCopy copy[32];           // producer: the next (up to) 32 tiles' copies
 };
 
 __device__ __forceinline__ bool is_local(const LayerParams &p, int e) {
@@ -362,7 +380,7 @@ __device__ void route_weights(const LayerParams &p, RouteInfo &rs, const float *
 
 // ------------------------------------------------------------ pipeline ----
 // ------------------------------------------------------------ pipeline ----
-// Wait until tile n occupies stage s and its bytes have landed (warp-uniform).
+// Wait until tile n occupies slot s and its bytes have landed (warp-uniform).
 // The stage_tile check comes first because mbarrier.try_wait.parity(P) also
 // succeeds while the barrier is still in the phase BEFORE the awaited one.
 // Once stage_tile[s] == n, the previous phase of full[s] has completed (its
@@ -410,9 +428,173 @@ __device__ __forceinline__ int grab(int *counter) {
 // be split between two tiles), and spans at most mcb blocks from the start
 // of cb's group, so it touches at most mcb/gcb groups (the stage holds mcb
 // weight blocks and mcb/gcb scale/bias rows).
-__device__ __forceinline__ int dn_run_end(int cb, int b8, int ncbE, int gcb, int mcb) {
-    const int uend = (cb / ncbE + 1) * ncbE;
-    return min(min(b8, uend), (cb / gcb) * gcb + mcb);
+__device__ __forceinline__ int dn_run_end(const LayerParams &p, int cb, int b8) {
+    const int ncbE = p.I >> 3, gcb = p.gs >> 3;
+    const int uend = (fdiv(cb, p.fd_ncbE) + 1) * ncbE;
+    return min(min(b8, uend), fdiv(cb, p.fd_gcb) * gcb + p.dn_max_cb);
+}
+
+// ------------------------------------------------------------ producer ----
+// One warp, right after routing: the distinct local experts (ascending, from
+// the expert bit mask) and this CTA's share of the work.  Gate/up rows [a, b)
+// of the distinct-expert row space (expert u's rows are u*I .. u*I+I-1), cut
+// in units of 8 rows so that row pairs (R, R+4) stay together; ntg gate/up
+// tiles (cut at multiples of GT, so a tile never crosses experts) and ntd =
+// nsub * nic down tiles (column-block runs, dn_run_end, per row chunk).
+__device__ void route_geometry(const LayerParams &p, Ctl &ctl, int blk) {
+    RouteInfo &rs = ctl.route;
+    const int lane = threadIdx.x & 31;
+    unsigned m = lane < kMaxExperts / 32 ? rs.emask[lane] : 0u;
+    const int c = __popc(m);
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    int pos = incl - c;
+    while (m) {
+        rs.ulist[pos++] = lane * 32 + __ffs(m) - 1;
+        m &= m - 1;
+    }
+    const int nU = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+        rs.nU = nU;
+        const int units = nU * (p.I >> 3);  // units * G < 2^31 (kMaxPairs, I, kMaxCtas)
+        const int a = fdiv(units * blk, p.fd_G) * 8, b = fdiv(units * (blk + 1), p.fd_G) * 8;
+        ctl.a = a;
+        ctl.b = b;
+        ctl.ntg = (b > a) ? fdiv(b - 1, p.fd_GT) - fdiv(a, p.fd_GT) + 1 : 0;
+        int nsub = 0;
+        for (int cb = a >> 3; cb < (b >> 3); cb = dn_run_end(p, cb, b >> 3)) ++nsub;
+        ctl.nsub = nsub;
+        ctl.ntd = nsub * p.nic;
+    }
+    __syncwarp();
+}
+
+// Producer state; lane 0 of the producer warp holds the authoritative copy
+// (batch is kept by every lane).
+struct Producer {
+    int n = 0;        // next tile to issue
+    int tail = 0;     // oldest tile whose release has not been seen
+    int head = 0;     // running byte position of the next tile
+    int pos = 0;      // head within the ring
+    int batch = -1;   // tiles 32*batch .. +31 are described in ctl.copy
+    bool ok = true;
+};
+
+// Lane l describes tile 32*batch + l into ctl.copy[l] (closed forms, so the
+// lanes work in parallel).  Tile order: gate/up tiles, then the down tiles
+// row chunk by row chunk, runs within a chunk in column order.
+__device__ void describe_tiles(const LayerParams &p, Ctl &ctl, int batch) {
+    const int lane = threadIdx.x & 31;
+    const TiledLayout &tl = p.tl;
+    const RouteInfo &rs = ctl.route;
+    const int a = ctl.a, b = ctl.b, ntg = ctl.ntg, ntd = ctl.ntd, nsub = ctl.nsub;
+    const int GT = p.gu_tile_rows, RC = tl.rc, ncbE = p.I >> 3, gcb = p.gs >> 3;
+    const int k = batch * 32 + lane;
+    TileCopy &c = ctl.copy[lane];
+    if (k < ntg) {
+        const int g0 = fdiv(a, p.fd_GT) + k;
+        const int R = k == 0 ? a : g0 * GT, hi = min((g0 + 1) * GT, b);
+        const int u = fdiv(R, p.fd_I), r0 = R - u * p.I;
+        c.src0 = p.table + (size_t)(rs.ulist[u] - p.e0) * tl.block + (size_t)r0 * tl.pr;
+        c.b0 = (uint32_t)((hi - R) * tl.pr);
+        c.src1 = nullptr;
+        c.b1 = 0;
+        c.g = StageGeo{u, r0, hi - R, -1, 0};
+    } else if (k < ntg + ntd) {
+        int j = k - ntg, ic = 0;
+        while (j >= nsub) {
+            j -= nsub;
+            ++ic;
+        }
+        int cb = a >> 3;
+        for (int q = 0; q < j; ++q) cb = dn_run_end(p, cb, b >> 3);
+        const int cend = dn_run_end(p, cb, b >> 3);
+        const int u = fdiv(cb, p.fd_ncbE), lcb = cb - u * ncbE, ncb = cend - cb;
+        const int lg0 = fdiv(lcb, p.fd_gcb), lg1 = fdiv(lcb + ncb - 1, p.fd_gcb);
+        (void)gcb;
+        const uint8_t *blkp = p.table + (size_t)(rs.ulist[u] - p.e0) * tl.block;
+        c.src0 = blkp + tl.dn_w + ((size_t)ic * tl.ncbI + lcb) * RC * 4;
+        c.b0 = (uint32_t)(ncb * RC * 4);
+        c.src1 = blkp + tl.dn_sb + ((size_t)ic * tl.ngI + lg0) * RC * 4;
+        c.b1 = (uint32_t)((lg1 - lg0 + 1) * RC * 4);
+        c.g = StageGeo{u, cb, ncb, ic, 0};
+    }
+}
+
+// Lane 0: issue the described tiles of the current batch in order.  Tile n
+// takes slot n % kLayerSlots and the next bytes of the ring (tiles back to
+// back; one that would run past the end starts at 0).  Slots and bytes come
+// free in tile order, so this waits, oldest tile first, for as many releases
+// as the new tile needs -- unless may_wait is false (the consumers have not
+// started yet): then it stops before such a tile and returns false.
+__device__ bool issue_batch(const LayerParams &p, Ctl &ctl, uint8_t *ring, uint64_t *full,
+                            uint64_t *empty, Producer &ps, bool may_wait, uint64_t pol,
+                            int ntiles) {
+    constexpr int NSL = kLayerSlots;
+    const int RB = p.ring_bytes, end = min(ntiles, (ps.batch + 1) * 32);
+    while (ps.ok && ps.n < end) {
+        const TileCopy c = ctl.copy[ps.n & 31];
+        const int len = (int)((c.b0 + c.b1 + 127u) & ~127u);
+        if (ps.pos + len > RB) {
+            ps.head += RB - ps.pos;
+            ps.pos = 0;
+        }
+        const bool slot_busy = ps.tail <= ps.n - NSL;
+        const bool bytes_busy = ps.tail < ps.n && ps.head + len - ctl.vstart[ps.tail % NSL] > RB;
+        if (!may_wait && (slot_busy || bytes_busy)) return false;
+        while (ps.ok && ps.tail <= ps.n - NSL) {
+            ps.ok = mbar_wait(&empty[ps.tail % NSL], (ps.tail / NSL) & 1, &ctl.abort, p.err);
+            ps.tail += ps.ok;
+        }
+        while (ps.ok && ps.tail < ps.n && ps.head + len - ctl.vstart[ps.tail % NSL] > RB) {
+            ps.ok = mbar_wait(&empty[ps.tail % NSL], (ps.tail / NSL) & 1, &ctl.abort, p.err);
+            ps.tail += ps.ok;
+        }
+        if (!ps.ok) break;
+        const int s = ps.n % NSL;
+        ctl.vstart[s] = ps.head;
+        StageGeo g = c.g;
+        g.off = ps.pos;
+        ctl.geo[s] = g;
+        __threadfence_block();
+        mbar_arrive_expect_tx(&full[s], c.b0 + c.b1);
+        bulk_g2s(ring + ps.pos, c.src0, c.b0, &full[s], pol);
+        if (c.b1) bulk_g2s(ring + ps.pos + c.b0, c.src1, c.b1, &full[s], pol);
+        *reinterpret_cast<volatile int *>(&ctl.stage_tile[s]) = ps.n;
+        if (ps.n == 0) trace_event(p.trace, 0, 11);
+        ++ps.n;
+        ps.head += len;
+        ps.pos += len;
+    }
+    return true;
+}
+
+// The producer warp: describe and issue tiles until `limit` tiles (or all)
+// are issued, an error stops it, or (may_wait false) a tile would have to
+// wait.
+__device__ void produce(const LayerParams &p, Ctl &ctl, uint8_t *ring, uint64_t *full,
+                        uint64_t *empty, Producer &ps, bool may_wait, uint64_t pol, int limit) {
+    const int lane = threadIdx.x & 31;
+    const int ntiles = min(ctl.ntg + ctl.ntd, limit);
+    for (;;) {
+        const int n = __shfl_sync(0xffffffffu, ps.n, 0);
+        const bool ok = __shfl_sync(0xffffffffu, ps.ok, 0);
+        if (!ok || n >= ntiles) break;
+        if ((n >> 5) != ps.batch) {
+            ps.batch = n >> 5;
+            describe_tiles(p, ctl, ps.batch);
+            __syncwarp();
+        }
+        bool more = true;
+        if (lane == 0) more = issue_batch(p, ctl, ring, full, empty, ps, may_wait, pol, ntiles);
+        more = __shfl_sync(0xffffffffu, more, 0);
+        __syncwarp();  // ctl.copy may be rewritten next round
+        if (!more) break;
+    }
 }
 
 __device__ __forceinline__ float swiglu(float g, float u) {
@@ -435,10 +617,10 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     constexpr int RG = ItemRows<NT>::gu, PG = ItemRows<NT>::pairs, NPASS = ItemRows<NT>::passes;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = (int)gridDim.x, blk = (int)blockIdx.x;
-    const int NST = p.nstages, STG = p.stage_bytes;
+    constexpr int NSL = kLayerSlots;
     uint8_t *ring = smem;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.off_bars);
-    uint64_t *empty = full + NST;
+    uint64_t *empty = full + NSL;
     Ctl &ctl = *reinterpret_cast<Ctl *>(smem + p.off_ctl);
     RouteInfo &rs = ctl.route;
     uint32_t *xq = reinterpret_cast<uint32_t *>(smem + p.off_xs);       // [ntok][h/2] int16 pairs
@@ -460,6 +642,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     if (tid == 0) {
         trace_event(p.trace, 0, 0);
         ctl.abort = 0;
+        ctl.route_ok = 0;
         ctl.epochs_seen = 0;
         const unsigned t1 = ld_relaxed_u32(my_epoch) + 1u;
         ctl.tag = t1 ? t1 : 1u;
@@ -467,6 +650,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     __syncthreads();
     const unsigned tag = ctl.tag;
     // this CTA's rows of h (output initialisation)
+    Producer ps;       // the producer warp's state (warp 24)
+    uint64_t pol = 0;  // its L2 policy for the streamed weights
     const int i0 = (int)((long long)h * blk / G), i1 = (int)((long long)h * (blk + 1) / G);
     const int nrows = i1 - i0;
     if (warp < 8) {
@@ -541,53 +726,16 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         // ---- phase 3: route (warps 0..7 of every CTA) ----
         const bool ok = route_cta(p, rs, rlog, keys, tag, vabort);
         if (tid == 0) trace_event(p.trace, 0, 3);
-        if (!ok) {
-            if (tid == 0) set_abort(ctl, p.err);
-        } else if (warp == 0) {
-            // distinct local experts, ascending, from the expert bit mask
-            unsigned m = lane < kMaxExperts / 32 ? rs.emask[lane] : 0u;
-            const int c = __popc(m);
-            int incl = c;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            int pos = incl - c;
-            while (m) {
-                rs.ulist[pos++] = lane * 32 + __ffs(m) - 1;
-                m &= m - 1;
-            }
-            const int nU = __shfl_sync(0xffffffffu, incl, 31);
-            if (lane == 0) {
-                rs.nU = nU;
-                // gate/up rows [a, b) of the distinct-expert row space
-                // (expert u's rows are u*I .. u*I+I-1), cut in units of 8
-                // rows so that row pairs (R, R+4) stay together.
-                const int units = nU * (I / 8);  // units * G < 2^31 (kMaxPairs, I, kMaxCtas)
-                const int a = units * blk / G * 8;
-                const int b = units * (blk + 1) / G * 8;
-                const int GT = p.gu_tile_rows, MCB = p.dn_max_cb, nic = h / tl.rc;
-                ctl.a = a;
-                ctl.b = b;
-                ctl.ntg = (b > a) ? (b - 1) / GT - a / GT + 1 : 0;
-                // down tiles: per expert segment of [a, b), column-block runs
-                // (dn_run_end), times the row chunks
-                const int gcb = p.gs / 8;
-                int ntd = 0;
-                for (int cb = a >> 3; cb < (b >> 3);) {
-                    const int cend = dn_run_end(cb, b >> 3, I / 8, gcb, MCB);
-                    ntd += nic;
-                    cb = cend;
-                }
-                ctl.ntd = ntd;
-            }
+        if (tid == 0) {
+            if (ok) ctl.route_ok = 1;
+            else set_abort(ctl, p.err);
         }
+        named_arrive(3, 256 + 32);  // routing (or its failure) is in shared memory
     } else {
         // ---- phase 1 (warps 8..24): pipeline set-up, x staging, output rows ----
         const int st = tid - 256, nst = kLayerThreads - 256;
         if (tid == kConsumerThreads) {
-            for (int i = 0; i < NST; ++i) {
+            for (int i = 0; i < NSL; ++i) {
                 mbar_init(&full[i], 1);
                 mbar_init(&empty[i], 1);
                 ctl.stage_tile[i] = -1;
@@ -619,8 +767,23 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             load_x32_any(p.x, p.x_bf16, (size_t)t * h + (size_t)c * kChunkCols, v);
             xsc[q] = quant_chunk_i16(v, xq + (size_t)t * (h / 2), nch, c, &xsum[q]);
         }
+        if (warp == kConsumerWarps) {
+            // the producer starts as soon as warps 0..7 have routed: the
+            // geometry and the first tile, then it lets the others go
+            // (barrier 5, without waiting) and keeps issuing
+            pol = l2_evict_first_policy();
+            named_sync(3, 256 + 32);
+            if (lane == 0) trace_event(p.trace, 0, 19);
+            if (!p.route_only && ctl.route_ok) {
+                route_geometry(p, ctl, blk);
+                if (lane == 0) trace_event(p.trace, 0, 16);
+                produce(p, ctl, ring, full, empty, ps, false, pol, 1);
+            }
+            named_arrive(5, kLayerThreads);
+        }
     }
-    __syncthreads();
+    if (warp != kConsumerWarps) named_sync(5, kLayerThreads);
+    const bool go = !p.route_only && ctl.route_ok;  // uniform: fixed before barrier 5
     if (tid == 0) {
         trace_event(p.trace, 0, 4);
         trace_value(p.trace, 0, 14, (unsigned)ctl.a | ((unsigned long long)(unsigned)ctl.b << 32));
@@ -628,9 +791,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     }
     // the routing weights: needed only by the caller's outputs and the final
     // atomics, so warps 1..7 compute them while the first copies are in flight
-    if (warp >= 1 && warp < 8 && !ctl.abort)
+    if (warp >= 1 && warp < 8 && ctl.route_ok)
         for (int t = warp - 1; t < p.ntok; t += 7) route_weights(p, rs, rlog, t);
-    if (p.route_only || ctl.abort) {
+    if (!go) {
         if (p.route_only) __syncthreads();  // user outputs complete before the epoch advances
         return;  // uniform; no copies were issued
     }
@@ -647,72 +810,19 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     }
 
     // ---- phase 4 geometry ----
-    const int GT = p.gu_tile_rows, MCB = p.dn_max_cb, RC = tl.rc, nic = h / RC;
-    const int ncbE = I / 8;  // column blocks per expert
-    const int a = ctl.a, b = ctl.b, ntg = ctl.ntg, ntd = ctl.ntd, nU = rs.nU;
-    const int a8 = a >> 3, ag = a / p.gs, gcb = p.gs / 8;
+    const int GT = p.gu_tile_rows, RC = tl.rc, nic = p.nic;
+    const int a = ctl.a, b = ctl.b, ntg = ctl.ntg, ntd = ctl.ntd;
+    const int a8 = a >> 3, ag = fdiv(a, p.fd_gs), gcb = p.gs >> 3;
     const int nslg = p.gu_nslices;
     const int ipt_g = (GT / 2 / PG) * nslg;  // work items per gate/up tile
     const int ipt_d = RC / 32;               // work items per down tile (32 rows each)
-    (void)nU;
 
     if (warp == kConsumerWarps) {
-        // ================= producer =================
+        // ================= producer (warp 24) =================
+        // the rest of the tiles, waiting for releases as needed
+        produce(p, ctl, ring, full, empty, ps, true, pol, 1 << 30);
         if (lane == 0) {
-            trace_event(p.trace, 0, 19);
-            const uint64_t pol = l2_evict_first_policy();
-            int n = 0, s = 0, wrap = 0;
-            bool ok = true;
-            // Wait for stage s to be free, record its tile, copy (one or two runs).
-            auto issue = [&](StageGeo g, const uint8_t *src0, uint32_t b0, const uint8_t *src1,
-                             uint32_t b1) {
-                if (n >= NST && !mbar_wait(&empty[s], (wrap - 1) & 1, &ctl.abort, p.err)) return false;
-                ctl.geo[s] = g;
-                __threadfence_block();
-                mbar_arrive_expect_tx(&full[s], b0 + b1);
-                bulk_g2s(ring + (size_t)s * STG, src0, b0, &full[s], pol);
-                if (b1) bulk_g2s(ring + (size_t)s * STG + b0, src1, b1, &full[s], pol);
-                *reinterpret_cast<volatile int *>(&ctl.stage_tile[s]) = n;
-                if (n == 0) trace_event(p.trace, 0, 11);
-                ++n;
-                if (++s == NST) {
-                    s = 0;
-                    ++wrap;
-                }
-                return true;
-            };
-            // gate/up tiles: [a, b) cut at multiples of GT (GT | I, so a tile
-            // never crosses experts)
-            {
-                int R = a, u = ntg ? a / I : 0, bound = (a / GT + 1) * GT;
-                for (int k = 0; k < ntg && ok; ++k) {
-                    const int hi = min(bound, b), r0 = R - u * I;
-                    ok = issue(StageGeo{u, r0, hi - R, -1},
-                               p.table + (size_t)(rs.ulist[u] - p.e0) * tl.block + (size_t)r0 * tl.pr,
-                               (uint32_t)((hi - R) * tl.pr), nullptr, 0);
-                    R = hi;
-                    bound += GT;
-                    if (R == (u + 1) * I) ++u;
-                }
-            }
-            // down tiles: the same rows as columns of the down matrices, in
-            // runs (dn_run_end); row chunk by row chunk
-            for (int ic = 0; ic < nic && ok && ntd > 0; ++ic) {
-                for (int cb = a8; cb < (b >> 3) && ok;) {
-                    const int u = cb / ncbE;
-                    const int cend = dn_run_end(cb, b >> 3, ncbE, gcb, MCB);
-                    const int lcb = cb - u * ncbE, ncb = cend - cb;
-                    const int lg0 = lcb / gcb, lg1 = (lcb + ncb - 1) / gcb;
-                    const uint8_t *blkp = p.table + (size_t)(rs.ulist[u] - p.e0) * tl.block;
-                    ok = issue(StageGeo{u, cb, ncb, ic},
-                               blkp + tl.dn_w + ((size_t)ic * tl.ncbI + lcb) * RC * 4,
-                               (uint32_t)(ncb * RC * 4),
-                               blkp + tl.dn_sb + ((size_t)ic * tl.ngI + lg0) * RC * 4,
-                               (uint32_t)((lg1 - lg0 + 1) * RC * 4));
-                    cb = cend;
-                }
-            }
-            ctl.issued = n;
+            ctl.issued = ps.n;
             trace_event(p.trace, 0, 9);
         }
     } else {
@@ -723,13 +833,14 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         for (;;) {
             const int q = grab(&ctl.next_gu);
             if (q >= ng_items) break;
-            const int n = q / ipt_g, rem = q - n * ipt_g, pg = rem / nslg, j = rem - pg * nslg;
-            const int s = n % NST;
-            if (!wait_tile(full, ctl, s, n, NST, p.err)) break;
+            const int n = fdiv(q, p.fd_iptg), rem = q - n * ipt_g, pg = fdiv(rem, p.fd_nslg),
+                      j = rem - pg * nslg;
+            const int s = n % NSL;
+            if (!wait_tile(full, ctl, s, n, NSL, p.err)) break;
             if (q == 0 && lane == 0) trace_event(p.trace, 0, 5);
             const StageGeo g = ctl.geo[s];
             if (pg * PG < g.nr / 2) {
-                const uint8_t *st = ring + (size_t)s * STG;
+                const uint8_t *st = ring + g.off;
                 const int e = rs.ulist[g.u];
                 const unsigned mask = rs.tmask[e];
                 float act_prev = 0.f;
@@ -747,7 +858,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
 #pragma unroll
                     for (int i = 0; i < kNg; ++i) accg[i] = 0.f;
                     for (int ch = j * 32 + lane; ch < nch; ch += 32 * nslg) {
-                        const int gi = (ch * kChunkCols) / p.gs;
+                        const int gi = fdiv(ch * kChunkCols, p.fd_gs);
 #pragma unroll
                         for (int k = 0; k < NT; ++k) {
                             if (!((mask >> k) & 1u)) continue;
@@ -815,7 +926,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         if (nslg > 1) {
             for (int i = tid; i < (b - a) * NT; i += kConsumerThreads) {
                 const int lr = i / NT, k = i % NT;
-                const int e = rs.ulist[(a + lr) / I];
+                const int e = rs.ulist[fdiv(a + lr, p.fd_I)];
                 if (ctl.abort || !((rs.tmask[e] >> k) & 1u)) continue;
                 float gv = 0.f, uv = 0.f;
                 const float *gp = gup + (size_t)lr * nslg * (2 * NT) + 2 * k;
@@ -843,9 +954,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         named_sync(1, kConsumerThreads);
         for (int i = tid; i < ncb_cta * NT; i += kConsumerThreads) {
             const int cb = i / NT, k = i % NT;
-            const int R0 = a + 8 * cb, e = rs.ulist[R0 / I];
+            const int R0 = a + 8 * cb, e = rs.ulist[fdiv(R0, p.fd_I)];
             if (ctl.abort || !((rs.tmask[e] >> k) & 1u)) continue;
-            const int gg = (a8 + cb) / gcb;
+            const int gg = fdiv(a8 + cb, p.fd_gcb);
             const int c_lo = max(gg * gcb, a8) - a8, c_hi = min((gg + 1) * gcb, b >> 3) - a8;
             float m = 0.f;
             for (int c = c_lo; c < c_hi; ++c) m = fmaxf(m, bst[2 * (c * NT + k)]);
@@ -874,14 +985,14 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         // weight word, four nibble pairs shared by the tokens; per group:
         // y += s*A + (b - 128 s)*X; per tile (one expert): total += w_k * y.
         // One atomic per row and token at the end.
-        const int nsub = nic ? ntd / nic : 0;  // down tiles per row chunk
+        const int nsub = ctl.nsub;  // down tiles per row chunk
         const int nd_items = (ctl.abort || ntd == 0) ? 0 : nic * ipt_d;
         float *dst = p.out_bf16 ? p.acc : reinterpret_cast<float *>(p.out);
         bool seen = false;  // epochs_seen observed (acquire) by this warp
         for (;;) {
             const int q = grab(&ctl.next_dn);
             if (q >= nd_items) break;
-            const int ic = q / ipt_d, w32 = q - ic * ipt_d;
+            const int ic = fdiv(q, p.fd_iptd), w32 = q - ic * ipt_d;
             const int ri = w32 * 32 + lane;
             if (q == 0 && lane == 0) trace_event(p.trace, 0, 18);
             float tot[NT];
@@ -890,17 +1001,17 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             unsigned any = 0u;
             bool ok = true;
             for (int jt = 0; jt < nsub; ++jt) {
-                const int n = ntg + ic * nsub + jt, s = n % NST;
-                if (!wait_tile(full, ctl, s, n, NST, p.err)) {
+                const int n = ntg + ic * nsub + jt, s = n % NSL;
+                if (!wait_tile(full, ctl, s, n, NSL, p.err)) {
                     ok = false;
                     break;
                 }
                 const StageGeo g = ctl.geo[s];
                 const int e = rs.ulist[g.u];
                 const unsigned mask = rs.tmask[e];
-                const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + (size_t)s * STG) + ri;
+                const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + g.off) + ri;
                 const uint32_t *SBt = Wt + (size_t)g.nr * RC;
-                const int gfirst = g.r0 / gcb;  // first group (concatenated space)
+                const int gfirst = fdiv(g.r0, p.fd_gcb);  // first group (concatenated space)
                 float y[NT];
                 int Q[NT];
 #pragma unroll
@@ -987,10 +1098,10 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     if (tid == 0) trace_event(p.trace, 0, 10);
     if (ctl.abort && tid == 0) {
         // wait (bounded) for copies still in flight into this CTA's shared memory
-        for (int n = ctl.issued - NST; n < ctl.issued; ++n) {
+        for (int n = ctl.issued - NSL; n < ctl.issued; ++n) {
             if (n < 0) continue;
             for (uint32_t i = 0; i < kWaitLimit; ++i)
-                if (mbar_try_wait(&full[n % NST], (n / NST) & 1)) break;
+                if (mbar_try_wait(&full[n % NSL], (n / NSL) & 1)) break;
         }
     }
 }

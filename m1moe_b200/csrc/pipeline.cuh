@@ -118,9 +118,38 @@ __device__ __forceinline__ void trace_value(unsigned long long *trace, int kerne
     trace[((size_t)kernel * kTraceCtas + blockIdx.x) * kTraceSlots + slot] = v;
 }
 
-// Named barrier over the first `nthreads` threads (a multiple of 32).
+// Named barrier `id` for `nthreads` threads (a multiple of 32), whichever
+// warps they are.
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Arrive at named barrier `id` without waiting (the waiting side calls
+// named_sync with the same thread count).
+__device__ __forceinline__ void named_arrive(int id, int nthreads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// floor(n / d) for 0 <= n < 2^31 and a divisor d >= 1 known on the host:
+// n * m >> k with m = ceil(2^k / d), k = 31 + ceil(log2 d) (the round-up
+// multiplier of Granlund and Montgomery, "Division by invariant integers
+// using multiplication", PLDI 1994: the error m*n/2^k - n/d < 1/d never
+// reaches the next integer).  A runtime integer division is a long
+// dependent instruction chain; this is one wide multiply.
+struct FastDiv {
+    unsigned long long m;
+    int k;
+};
+
+__device__ __forceinline__ int fdiv(int n, const FastDiv &f) {
+    return (int)(((unsigned long long)(unsigned)n * f.m) >> f.k);
+}
+
+inline FastDiv make_fastdiv(int d) {
+    int l = 0;
+    while ((1LL << l) < d) ++l;
+    const int k = 31 + l;
+    return FastDiv{((1ULL << k) + (unsigned long long)d - 1) / (unsigned long long)d, k};
 }
 
 // Named barrier that also ANDs a predicate over the participating threads.

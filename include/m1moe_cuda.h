@@ -62,7 +62,8 @@ typedef enum m1moe_dtype {
 
 /* Dimensions of one MoE model; field meanings follow ModelSpec.swift
  * (hiddenDim, MoESpec.intermediateDim/numExperts/topK/normTopkProb,
- * QuantSpec.groupSize, numLayers). */
+ * QuantSpec.groupSize, numLayers).  hidden_dim is a multiple of 128,
+ * intermediate_dim of 64, group_size a multiple of 32 dividing both. */
 typedef struct m1moe_cuda_cfg {
     int32_t hidden_dim;
     int32_t intermediate_dim;
@@ -208,16 +209,17 @@ M1MOE_API int64_t m1moe_cuda_launch_count(void);
 /* Phase tracing (the reference only has wall-clock timing, bench/main.swift
  * :51-54).  With a non-NULL device buffer of 160 x 24 uint64, every MoE call
  * made afterwards records, per CTA (first 160), the SM cycle counter at each
- * phase event in slots 0-19 and the global nanosecond timer at events 0 and 10
- * in slots 20 and 21; NULL turns tracing off (the default).  Events: 0 start,
- * 1 x staged and output rows initialised, 2 this CTA's logits published,
- * 3 top-K ranked, 4 routing done in the whole CTA, 5 first gate/up tile
- * landed, 6 activations quantised, 7 every CTA's output rows seen
- * initialised, 8 down items done, 9 producer issued every tile, 10 end,
- * 11 producer issued its first tile, 12 every logit seen, 13 ranks counted,
- * 17 gate/up items done, 18 first down item started, 19 producer started;
- * slots 14 and 15 hold values, not times: the CTA's gate/up row range
- * (first | end << 32) and its tile counts (gate/up | down << 32); 16 unused. */
+ * phase event (slots 0-13, 16-19, 22, 23) and the global nanosecond timer at
+ * events 0 and 10 (slots 20 and 21); NULL turns tracing off (the default).
+ * Events: 0 start, 1 output rows initialised, 2 this CTA's logits published,
+ * 3 top-K ranked, 4 consumers released (routing and geometry known),
+ * 5 first gate/up tile landed, 6 activations quantised, 7 every CTA's output
+ * rows seen initialised, 8 down items done, 9 producer issued every tile,
+ * 10 end, 11 producer issued its first tile, 12 every logit seen, 13 ranks
+ * counted, 16 producer's geometry done, 17 gate/up items done, 18 first down
+ * item started, 19 producer saw the routing, 22 first and 23 last down tile
+ * seen landed.  Slots 14 and 15 hold values, not times: the CTA's gate/up
+ * row range (first | end << 32) and its tile counts (gate/up | down << 32). */
 M1MOE_API m1moe_status m1moe_cuda_set_trace(m1moe_cuda_ctx *ctx, uint64_t *d_trace);
 
 #ifdef __cplusplus

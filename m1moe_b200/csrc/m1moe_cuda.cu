@@ -296,7 +296,8 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     p.fd_gs = m1::make_fastdiv(p.gs);
     p.fd_iptg = m1::make_fastdiv((p.gu_tile_rows / 2 / pg) * p.gu_nslices);
     p.fd_nslg = m1::make_fastdiv(p.gu_nslices);
-    p.fd_iptd = m1::make_fastdiv(tl.rc / 32);
+    if (tl.rc % (32 * m1::dn_lane_rows(nt))) return 0;
+    p.fd_iptd = m1::make_fastdiv(tl.rc / (32 * m1::dn_lane_rows(nt)));
     const long long units = (long long)maxU * (p.I / 8);
     p.gu_rows_max = (int)((units + grid - 1) / grid) * 8;
     p.act_cb = p.gu_rows_max / 8;
@@ -493,8 +494,9 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     const m1moe_cuda_cfg g = *cfg;
     if (g.hidden_dim <= 0 || g.intermediate_dim <= 0 || g.num_layers <= 0)
         return fail(M1MOE_ERR_INVALID_ARG, "dims must be positive");
-    if (g.hidden_dim % 64 || g.intermediate_dim % 64)
-        return fail(M1MOE_ERR_INVALID_ARG, "hidden_dim and intermediate_dim must be multiples of 64");
+    if (g.hidden_dim % 128 || g.intermediate_dim % 64)
+        return fail(M1MOE_ERR_INVALID_ARG,
+                    "hidden_dim must be a multiple of 128 and intermediate_dim of 64");
     if (g.group_size <= 0 || g.group_size % 32 || g.hidden_dim % g.group_size ||
         g.intermediate_dim % g.group_size)
         return fail(M1MOE_ERR_UNSUPPORTED,
@@ -837,6 +839,8 @@ m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *
     p.res_bf16 = res_dtype == M1MOE_DTYPE_BF16;
     p.out = d_out;
     p.out_bf16 = out_dtype == M1MOE_DTYPE_BF16;
+    // the down items add four adjacent fp32 rows with one 16-byte atomic
+    p.out_acc = p.out_bf16 || (reinterpret_cast<uintptr_t>(d_out) & 15) != 0;
     p.user_idx = d_idx;
     p.user_w = d_w;
     return dispatch_layer(c, p, as_stream(stream));

@@ -104,6 +104,7 @@ struct LayerParams {
     int res_bf16;
     void *out;        // must not overlap x
     int out_bf16;
+    int out_acc;      // sums go to acc, the last CTA writes out (bf16, or f32 not 16-byte aligned)
     float *acc;       // [ntok][h] fp32 sums for bf16 output
     int *done;        // CTAs finished with their atomics (bf16 output)
     unsigned long long *xlog;  // [nbox][box_words] tagged logits {tag, f32}, box = [ntok][E]
@@ -434,6 +435,44 @@ __device__ __forceinline__ int dn_run_end(const LayerParams &p, int cb, int b8) 
     return min(min(b8, uend), fdiv(cb, p.fd_gcb) * gcb + p.dn_max_cb);
 }
 
+// Rows of h per lane in a down item: several adjacent rows give one vector
+// load per column block and one vector atomic per token, and independent
+// dot-product chains; fewer for larger batches (registers: LR*NT of each of
+// Q, y and the totals).
+__host__ __device__ constexpr int dn_lane_rows(int nt) { return nt <= 2 ? 4 : (nt == 4 ? 2 : 1); }
+
+template <int NT>
+struct DnRows {
+    static constexpr int lane = dn_lane_rows(NT);
+};
+
+// LR consecutive 32-bit words from shared memory (4*LR-byte aligned).
+template <int LR>
+__device__ __forceinline__ void load_words(const uint32_t *p, uint32_t (&w)[LR]) {
+    if constexpr (LR == 4) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(p);
+        w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+    } else if constexpr (LR == 2) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(p);
+        w[0] = v.x, w[1] = v.y;
+    } else {
+        w[0] = *p;
+    }
+}
+
+// Add token t's LR row totals to LR consecutive floats of global memory
+// (4*LR-byte aligned) with one vector atomic.
+template <int LR, int NT>
+__device__ __forceinline__ void add_words(float *dst, const float (&tot)[LR][NT], int t) {
+    if constexpr (LR == 4) {
+        atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(tot[0][t], tot[1][t], tot[2][t], tot[3][t]));
+    } else if constexpr (LR == 2) {
+        atomicAdd(reinterpret_cast<float2 *>(dst), make_float2(tot[0][t], tot[1][t]));
+    } else {
+        atomicAdd(dst, tot[0][t]);
+    }
+}
+
 // ------------------------------------------------------------ producer ----
 // One warp, right after routing: the distinct local experts (ascending, from
 // the expert bit mask) and this CTA's share of the work.  Gate/up rows [a, b)
@@ -748,7 +787,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         // this CTA's output rows start as the residual (moeCombine adds it
         // first, Shaders.metal:368) or zero
         if (!p.route_only) {
-            float *dst = p.out_bf16 ? p.acc : reinterpret_cast<float *>(p.out);
+            float *dst = p.out_acc ? p.acc : reinterpret_cast<float *>(p.out);
             for (int q = st; q < p.ntok * nrows; q += nst) {
                 const int t = q / nrows, i = i0 + q % nrows;
                 dst[(size_t)t * h + i] = p.res ? load_act(p.res, p.res_bf16, (size_t)t * h + i) : 0.f;
@@ -815,7 +854,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     const int a8 = a >> 3, ag = fdiv(a, p.fd_gs), gcb = p.gs >> 3;
     const int nslg = p.gu_nslices;
     const int ipt_g = (GT / 2 / PG) * nslg;  // work items per gate/up tile
-    const int ipt_d = RC / 32;               // work items per down tile (32 rows each)
+    const int ipt_d = RC / (32 * DnRows<NT>::lane);  // work items per down tile
 
     if (warp == kConsumerWarps) {
         // ================= producer (warp 24) =================
@@ -980,24 +1019,28 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         if (tid == 0) trace_event(p.trace, 0, 6);
 
         // ================= consumers: down (split-K) =================
-        // Item = 32 rows of one row chunk (lane = row of h), over all of this
-        // CTA's down tiles of that chunk in ring order.  Per column block: one
-        // weight word, four nibble pairs shared by the tokens; per group:
-        // y += s*A + (b - 128 s)*X; per tile (one expert): total += w_k * y.
-        // One atomic per row and token at the end.
+        // Item = 32*LR consecutive rows of one row chunk (lane: LR adjacent
+        // rows of h), over all of this CTA's down tiles of that chunk in ring
+        // order.  Per column block: LR weight words (one vector load), the
+        // nibble pairs of each shared by the tokens; per group:
+        // y += s*sa*Q + b*X; per tile (one expert): total += w_k * y.  One
+        // LR-wide atomic per lane and token at the end.
+        constexpr int LR = DnRows<NT>::lane;
         const int nsub = ctl.nsub;  // down tiles per row chunk
         const int nd_items = (ctl.abort || ntd == 0) ? 0 : nic * ipt_d;
-        float *dst = p.out_bf16 ? p.acc : reinterpret_cast<float *>(p.out);
+        float *dst = p.out_acc ? p.acc : reinterpret_cast<float *>(p.out);
         bool seen = false;  // epochs_seen observed (acquire) by this warp
         for (;;) {
             const int q = grab(&ctl.next_dn);
             if (q >= nd_items) break;
-            const int ic = fdiv(q, p.fd_iptd), w32 = q - ic * ipt_d;
-            const int ri = w32 * 32 + lane;
+            const int ic = fdiv(q, p.fd_iptd), wi = q - ic * ipt_d;
+            const int ri = (wi * 32 + lane) * LR;  // first row (in the chunk) of this lane
             if (q == 0 && lane == 0) trace_event(p.trace, 0, 18);
-            float tot[NT];
+            float tot[LR][NT];
 #pragma unroll
-            for (int t = 0; t < NT; ++t) tot[t] = 0.f;
+            for (int r = 0; r < LR; ++r)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) tot[r][t] = 0.f;
             unsigned any = 0u;
             bool ok = true;
             for (int jt = 0; jt < nsub; ++jt) {
@@ -1006,41 +1049,55 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                     ok = false;
                     break;
                 }
+                if (lane == 0 && wi == 0 && n == ntg) trace_event(p.trace, 0, 22);
+                if (lane == 0 && wi == 0 && n == ntg + ntd - 1) trace_event(p.trace, 0, 23);
                 const StageGeo g = ctl.geo[s];
                 const int e = rs.ulist[g.u];
                 const unsigned mask = rs.tmask[e];
                 const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + g.off) + ri;
                 const uint32_t *SBt = Wt + (size_t)g.nr * RC;
                 const int gfirst = fdiv(g.r0, p.fd_gcb);  // first group (concatenated space)
-                float y[NT];
-                int Q[NT];
+                float y[LR][NT];
+                int Q[LR][NT];
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    y[t] = 0.f;
-                    Q[t] = 0;
-                }
-                int gcur = gfirst, left = gcb - (g.r0 - gfirst * gcb);  // blocks left in gcur
-                auto flush = [&](int gg) {
-                    const uint32_t sb = SBt[(size_t)(gg - gfirst) * RC];
-                    const float sc = bf16_bits(sb & 0xFFFFu), bi = bf16_bits(sb >> 16);
-                    const float *xg = xseg + (size_t)(gg - ag) * NT * 2;
+                for (int r = 0; r < LR; ++r)
 #pragma unroll
                     for (int t = 0; t < NT; ++t) {
-                        // s * sa * Q + b * X over the group's columns in this range
-                        if ((mask >> t) & 1u)
-                            y[t] = fmaf(sc * xg[2 * t + 1], (float)Q[t], fmaf(bi, xg[2 * t], y[t]));
-                        Q[t] = 0;
+                        y[r][t] = 0.f;
+                        Q[r][t] = 0;
+                    }
+                int gcur = gfirst, left = gcb - (g.r0 - gfirst * gcb);  // blocks left in gcur
+                auto flush = [&](int gg) {
+                    uint32_t sb[LR];
+                    load_words<LR>(SBt + (size_t)(gg - gfirst) * RC, sb);
+                    const float *xg = xseg + (size_t)(gg - ag) * NT * 2;
+#pragma unroll
+                    for (int r = 0; r < LR; ++r) {
+                        const float sc = bf16_bits(sb[r] & 0xFFFFu), bi = bf16_bits(sb[r] >> 16);
+#pragma unroll
+                        for (int t = 0; t < NT; ++t) {
+                            // s * sa * Q + b * X over the group's columns in this range
+                            if ((mask >> t) & 1u)
+                                y[r][t] = fmaf(sc * xg[2 * t + 1], (float)Q[r][t],
+                                               fmaf(bi, xg[2 * t], y[r][t]));
+                            Q[r][t] = 0;
+                        }
                     }
                 };
                 for (int c = 0; c < g.nr; ++c) {
-                    const uint32_t wd = Wt[(size_t)c * RC];
-                    const uint32_t lo = wd & 0x0F0F0F0Fu, hi = (wd >> 4) & 0x0F0F0F0Fu;
+                    uint32_t wd[LR];
+                    load_words<LR>(Wt + (size_t)c * RC, wd);
                     const uint4 *av = reinterpret_cast<const uint4 *>(act) + (g.r0 + c - a8);
 #pragma unroll
                     for (int t = 0; t < NT; ++t) {
                         if ((mask >> t) & 1u) {
                             const uint4 v = av[(size_t)t * p.act_cb];
-                            Q[t] = dp2a_hi(v.w, hi, dp2a_lo(v.z, hi, dp2a_hi(v.y, lo, dp2a_lo(v.x, lo, Q[t]))));
+#pragma unroll
+                            for (int r = 0; r < LR; ++r) {
+                                const uint32_t lo = wd[r] & 0x0F0F0F0Fu, hi = (wd[r] >> 4) & 0x0F0F0F0Fu;
+                                Q[r][t] = dp2a_hi(v.w, hi, dp2a_lo(v.z, hi, dp2a_hi(v.y, lo,
+                                                                                  dp2a_lo(v.x, lo, Q[r][t]))));
+                            }
                         }
                     }
                     if (--left == 0) {
@@ -1052,7 +1109,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 if (left != gcb) flush(gcur);
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
-                    if ((mask >> t) & 1u) tot[t] = fmaf(rs.w[t][rs.kof[e][t]], y[t], tot[t]);
+                    if ((mask >> t) & 1u) {
+                        const float wk = rs.w[t][rs.kof[e][t]];
+#pragma unroll
+                        for (int r = 0; r < LR; ++r) tot[r][t] = fmaf(wk, y[r][t], tot[r][t]);
+                    }
                 any |= mask;
                 release_item(empty, ctl, s, ipt_d);
             }
@@ -1074,11 +1135,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             const int i = ic * RC + ri;
 #pragma unroll
             for (int t = 0; t < NT; ++t)
-                if ((any >> t) & 1u) atomicAdd(dst + (size_t)t * h + i, tot[t]);
+                if ((any >> t) & 1u) add_words<LR>(dst + (size_t)t * h + i, tot, t);
         }
         if (tid == 0) trace_event(p.trace, 0, 8);
-        if (p.out_bf16) {
-            // the last CTA to finish converts the fp32 sums
+        if (p.out_acc) {
+            // the last CTA to finish writes the fp32 sums out
             named_sync(1, kConsumerThreads);
             if (tid == 0) {
                 __threadfence();
@@ -1087,9 +1148,14 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             named_sync(1, kConsumerThreads);
             if (ctl.last) {
                 __threadfence();
-                __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(p.out);
-                for (int i = tid; i < p.ntok * h; i += kConsumerThreads)
-                    o[i] = __float2bfloat16_rn(__ldcg(p.acc + i));
+                if (p.out_bf16) {
+                    __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(p.out);
+                    for (int i = tid; i < p.ntok * h; i += kConsumerThreads)
+                        o[i] = __float2bfloat16_rn(__ldcg(p.acc + i));
+                } else {
+                    float *o = reinterpret_cast<float *>(p.out);
+                    for (int i = tid; i < p.ntok * h; i += kConsumerThreads) o[i] = __ldcg(p.acc + i);
+                }
                 if (tid == 0) *p.done = 0;
             }
         }

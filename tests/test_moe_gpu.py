@@ -114,6 +114,30 @@ def test_moe_layer_dtypes_and_no_residual(golden, oracle_lib, xdt, odt):
               norm=False, B=3, xdt=xdt, odt=odt, with_res=False, seed=3)
 
 
+def test_moe_layer_f32_output_not_16_byte_aligned(golden, oracle_lib):
+    """An fp32 output 4 bytes past a 16-byte boundary (the device path adds
+    four adjacent rows with one 16-byte atomic, so this one accumulates
+    elsewhere and is written at the end) matches the aligned output."""
+    from golden.make_golden import router_weights
+    g = golden("olmoe_tiny")
+    L, E, h, I, gs, seed = (int(v) for v in g["meta"])
+    router = router_weights(seed, L, E, h)[0]
+    blk = _block([g["layer_00"]], [router], h=h, I=I, E=E, K=2, norm=False)
+    B = 3
+    x = _bf16_dev(synth.hidden_states(41, B, h))
+    r = _bf16_dev(synth.hidden_states(42, B, h), torch.float32)
+    aligned = blk.forward(0, x, r).cpu().numpy()
+    buf = torch.full((B * h + 4,), float("nan"), dtype=torch.float32, device="cuda")
+    out = buf[1:1 + B * h].view(B, h)
+    assert out.data_ptr() % 16 == 4
+    blk.forward(0, x, r, out=out)
+    got = out.cpu().numpy()
+    blk.synchronize()
+    assert rel_max_err(got, aligned) < TOL
+    assert np.isnan(buf[0].item()) and np.isnan(buf[-3:].cpu().numpy()).all()  # nothing outside
+    blk.close()
+
+
 def test_forward_host_matches_device_path(golden):
     from golden.make_golden import router_weights
     g = golden("olmoe_tiny")

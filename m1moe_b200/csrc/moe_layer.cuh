@@ -308,8 +308,19 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
     }
     if (!named_sync_and(2, 256, ok)) return false;
     if (tid == 0) trace_event(p.trace, 0, 12);
-    // b. rank of every (token, expert): P threads per element, each counting
-    //    the keys above it in one slice of the token's E keys
+    // marks of token t's k-th expert: the caller's index output, and for a
+    // local expert its token mask, the token's k and the expert bit
+    auto mark = [&](int t, int k) {
+        const int e = rs.idx[t][k];
+        if (p.user_idx && blockIdx.x == 0) p.user_idx[t * K + k] = e;
+        if (is_local(p, e)) {
+            atomicOr(&rs.tmask[e], 1u << t);
+            rs.kof[e][t] = (unsigned char)k;
+            atomicOr(&rs.emask[e >> 5], 1u << (e & 31));
+        }
+    };
+    // b. rank of every (token, expert): P threads per element, each
+    //    counting the keys above it in one slice of the token's E keys
     int lp = 0;
     while (lp < 5 && (nel << (lp + 1)) <= 256) ++lp;
     const int P = 1 << lp;
@@ -337,13 +348,7 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
             k -= K;
             ++t;
         }
-        const int e = rs.idx[t][k];
-        if (p.user_idx && blockIdx.x == 0) p.user_idx[i] = e;
-        if (is_local(p, e)) {
-            atomicOr(&rs.tmask[e], 1u << t);
-            rs.kof[e][t] = (unsigned char)k;
-            atomicOr(&rs.emask[e >> 5], 1u << (e & 31));
-        }
+        mark(t, k);
     }
     named_sync(2, 256);
     return true;
@@ -523,18 +528,16 @@ struct Producer {
     bool ok = true;
 };
 
-// Lane l describes tile 32*batch + l into ctl.copy[l] (closed forms, so the
-// lanes work in parallel).  Tile order: gate/up tiles, then the down tiles
-// row chunk by row chunk, runs within a chunk in column order.
-__device__ void describe_tiles(const LayerParams &p, Ctl &ctl, int batch) {
-    const int lane = threadIdx.x & 31;
+// The copies of tile k.  Tile order: gate/up tiles, then the down tiles row
+// chunk by row chunk, runs within a chunk in column order.
+__device__ void describe_tile(const LayerParams &p, const Ctl &ctl, int k, TileCopy &c) {
     const TiledLayout &tl = p.tl;
     const RouteInfo &rs = ctl.route;
     const int a = ctl.a, b = ctl.b, ntg = ctl.ntg, ntd = ctl.ntd, nsub = ctl.nsub;
-    const int GT = p.gu_tile_rows, RC = tl.rc, ncbE = p.I >> 3, gcb = p.gs >> 3;
-    const int k = batch * 32 + lane;
-    TileCopy &c = ctl.copy[lane];
+    const int GT = p.gu_tile_rows, RC = tl.rc, ncbE = p.I >> 3;
     if (k < ntg) {
+        // gate/up: [a, b) cut at multiples of GT (GT | I, so a tile never
+        // crosses experts)
         const int g0 = fdiv(a, p.fd_GT) + k;
         const int R = k == 0 ? a : g0 * GT, hi = min((g0 + 1) * GT, b);
         const int u = fdiv(R, p.fd_I), r0 = R - u * p.I;
@@ -544,6 +547,8 @@ __device__ void describe_tiles(const LayerParams &p, Ctl &ctl, int batch) {
         c.b1 = 0;
         c.g = StageGeo{u, r0, hi - R, -1, 0};
     } else if (k < ntg + ntd) {
+        // down: the same rows as columns of the down matrices, in runs
+        // (dn_run_end)
         int j = k - ntg, ic = 0;
         while (j >= nsub) {
             j -= nsub;
@@ -554,7 +559,6 @@ __device__ void describe_tiles(const LayerParams &p, Ctl &ctl, int batch) {
         const int cend = dn_run_end(p, cb, b >> 3);
         const int u = fdiv(cb, p.fd_ncbE), lcb = cb - u * ncbE, ncb = cend - cb;
         const int lg0 = fdiv(lcb, p.fd_gcb), lg1 = fdiv(lcb + ncb - 1, p.fd_gcb);
-        (void)gcb;
         const uint8_t *blkp = p.table + (size_t)(rs.ulist[u] - p.e0) * tl.block;
         c.src0 = blkp + tl.dn_w + ((size_t)ic * tl.ncbI + lcb) * RC * 4;
         c.b0 = (uint32_t)(ncb * RC * 4);
@@ -562,6 +566,13 @@ __device__ void describe_tiles(const LayerParams &p, Ctl &ctl, int batch) {
         c.b1 = (uint32_t)((lg1 - lg0 + 1) * RC * 4);
         c.g = StageGeo{u, cb, ncb, ic, 0};
     }
+}
+
+// Lane l describes tile 32*batch + l into ctl.copy[l] (the lanes work in
+// parallel).
+__device__ __forceinline__ void describe_tiles(const LayerParams &p, Ctl &ctl, int batch) {
+    const int lane = threadIdx.x & 31;
+    describe_tile(p, ctl, batch * 32 + lane, ctl.copy[lane]);
 }
 
 // Lane 0: issue the described tiles of the current batch in order.  Tile n
@@ -815,8 +826,17 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             if (lane == 0) trace_event(p.trace, 0, 19);
             if (!p.route_only && ctl.route_ok) {
                 route_geometry(p, ctl, blk);
-                if (lane == 0) trace_event(p.trace, 0, 16);
-                produce(p, ctl, ring, full, empty, ps, false, pol, 1);
+                if (lane == 0) {
+                    trace_event(p.trace, 0, 16);
+                    if (ctl.ntg + ctl.ntd > 0) {
+                        // the first tile, described by lane 0 alone; the
+                        // whole first batch is described again later
+                        describe_tile(p, ctl, 0, ctl.copy[0]);
+                        ps.batch = 0;
+                        issue_batch(p, ctl, ring, full, empty, ps, false, pol, 1);
+                        ps.batch = -1;
+                    }
+                }
             }
             named_arrive(5, kLayerThreads);
         }

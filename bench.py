@@ -22,6 +22,9 @@ N GPUs   = expert parallel: rank r holds experts [r*64/N, (r+1)*64/N) of every
            layer and owns one decode token; per layer the tokens are
            all-gathered, each rank applies its experts to every token routed to
            them, and a reduce-scatter returns each token's sum (weak scaling).
+prefill  = (1 GPU) config 3's prefill mode beside the decode line: one
+           Mixtral-shaped layer over 512 tokens through m1moe_cuda_moe_prefill
+           (tensor-core grouped GEMMs), TFLOP/s against the measured bf16 peak.
 --impl reference  times the CPU oracle (a C restatement of the reference's
            Metal/Swift arithmetic; the reference itself is Swift+Metal and cannot
            run on this box) on a bounded sample, on all host cores.
@@ -63,6 +66,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the tensor-core prefill measurement (config 3, 512 tokens)")
     return ap.parse_args()
 
 
@@ -133,6 +138,16 @@ def traffic_per_launch(wl: dict, world: int):
         return d.get(f"{wl['name']}/ep{world}")
     except Exception:
         return None
+
+
+def tensor_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s: the measured cuBLAS burst figure, else the fallback."""
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        v = json.loads(path.read_text()).get("bf16_tflops")
+        if v:
+            return float(v), "measured"
+    return 1590.0, "fallback"
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -234,6 +249,54 @@ def run_reference(args, wl) -> None:
 
 
 # -------------------------------------------------------------- GPU arm ----
+PREFILL = dict(name="mixtral_moe_prefill_512", h=4096, I=14336, E=8, K=2, gs=64, tokens=512)
+
+
+def prefill_measure(dev, steps: int, warmup: int) -> dict:
+    """Config 3's prefill mode: one Mixtral-shaped MoE layer over 512 tokens as
+    grouped int4 x bf16 GEMMs on the tensor cores (m1moe_cuda_moe_prefill).
+    Algorithmic work: tokens x K x 3 matrices x 2*h*I flops (360.8 GFLOP)."""
+    import torch
+
+    from m1moe_b200 import MoEBlock, synth
+
+    c = PREFILL
+    h, I, E, K, T = c["h"], c["I"], c["E"], c["K"], c["tokens"]
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, group_size=c["gs"],
+                   num_layers=1, norm_topk_prob=True, max_batch=8, device=dev.index)
+    img = synth.layer_image_device(E, h, I, c["gs"], seed=SEED + 77, device=dev)
+    blk.load_expert_layer(0, img)
+    del img
+    blk.load_router(0, synth.router_weights(SEED + 78, E, h))
+    x = torch.from_numpy(synth.hidden_states(SEED + 79, T, h).view(np.int16)).to(dev).view(torch.bfloat16)
+    out = torch.empty((T, h), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, warmup)):
+            blk.prefill(0, x, x, out=out, stream=stream)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(3, min(steps, 50))
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(n):
+            blk.prefill(0, x, x, out=out, stream=stream)
+        b.record(stream)
+    torch.cuda.synchronize()
+    blk.synchronize()
+    ms = a.elapsed_time(b) / n
+    blk.close()
+    flops = T * K * 3 * 2.0 * h * I
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak = tensor_peak()
+    return {"workload": c["name"], "tokens": T, "value": tflops, "unit": "TFLOP/s", "ms": ms,
+            "calls": n, "flops_per_call": flops,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak[0], "unit": "TFLOP/s",
+                         "frac": tflops / peak[0], "peak_source": peak[1],
+                         "kernel": "m1moe_cuda_moe_prefill (k_prefill_gemm gate/up + down)"},
+            "dtype": "bf16 operands (int4 weights dequantised), fp32 accumulation"}
+
+
 def run_gpu(args, wl) -> None:
     import torch
     import torch.distributed as dist
@@ -319,9 +382,14 @@ def run_gpu(args, wl) -> None:
             one_step()
     torch.cuda.synchronize()
 
-    ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(L + 1)]
+    # the timed graph holds only the layer launches; a second graph with an
+    # event between layers gives the per-layer durations
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
+        one_step()
+    ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(L + 1)]
+    graph_ev = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_ev, stream=stream):
         one_step(ev)
     torch.cuda.synchronize()
 
@@ -348,7 +416,14 @@ def run_gpu(args, wl) -> None:
         dist.barrier()
     torch.cuda.synchronize()
     ms = t_start.elapsed_time(t_end)
-    # per-layer launch-sequence durations of the last replay
+    # per-layer durations: the event graph, replayed after the timed region
+    # (its event nodes add a little time between layers)
+    with torch.cuda.stream(stream):
+        for _ in range(5):
+            graph_ev.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     layer_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(L)]
 
     # Distinct local experts per layer from the last step's routing.
@@ -424,6 +499,10 @@ def run_gpu(args, wl) -> None:
                "h2d_bytes_per_step": b * h * 4, "d2h_bytes_per_step": b * h * 4,
                "api": "pinned H2D + captured EP step + D2H per step"}
 
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        prefill = prefill_measure(dev, args.steps, args.warmup)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host = host_layers_for_cpu(wl, 2, device=dev)
@@ -450,11 +529,12 @@ def run_gpu(args, wl) -> None:
                          "algorithmic_bytes_per_launch": per_layer_bytes},
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "prefill": prefill,
             "gpu_launches": launches_per_step * (args.steps + 0),
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
-    del graph
+    del graph, graph_ev
     blk.close()
     if world > 1:
         dist.barrier()

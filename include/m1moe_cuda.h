@@ -191,6 +191,23 @@ M1MOE_API m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *ctx, int32_t layer, 
                                   void *d_out, int32_t out_dtype, int32_t batch,
                                   int32_t *d_topk_idx, float *d_topk_w, void *stream);
 
+/* The same MoE block for `tokens` tokens at once (prefill, large batches) as
+ * grouped int4 x bf16 GEMMs on the tensor cores (stream-ordered, device
+ * pointers, the argument meanings of m1moe_cuda_moe_layer).  The reference
+ * has no batched path: it runs runLayer token by token during prefill
+ * (bench/main.swift:139-141, InferenceEngine.swift:240-266).  Weights,
+ * tokens and SwiGLU activations enter the tensor cores as fp16 (fp32
+ * accumulation), so results agree with m1moe_cuda_moe_layer within the FFN
+ * tolerance, not bitwise; a value beyond the fp16 range (|v| > 65504) makes
+ * the next m1moe_cuda_synchronize report M1MOE_ERR_DEVICE.  Needs group_size
+ * 64 and intermediate_dim a multiple of 128.
+ * Scratch for `tokens` is allocated on the first call that needs more
+ * (synchronously, outside stream capture); out may alias x. */
+M1MOE_API m1moe_status m1moe_cuda_moe_prefill(m1moe_cuda_ctx *ctx, int32_t layer, const void *d_x,
+                                    int32_t x_dtype, const void *d_residual, int32_t res_dtype,
+                                    void *d_out, int32_t out_dtype, int32_t tokens,
+                                    int32_t *d_topk_idx, float *d_topk_w, void *stream);
+
 /* Synchronous host-buffer form of m1moe_cuda_moe_layer with the reference's
  * f32 buffers (buf_h_mid, buf_residual -> buf_moe_out, MetalContext.swift
  * :134-152): copies in, runs, copies out and waits.  h_topk_* may be NULL. */

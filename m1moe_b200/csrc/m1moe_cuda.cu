@@ -5,6 +5,7 @@
 // duration of a call, as in the reference where MetalContext owns the expert
 // slots (MetalContext.swift:154-178) and WeightStore owns the mmap
 // (WeightStore.swift:78-81).
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -21,6 +22,7 @@
 #include "matvec4.cuh"
 #include "moe_layer.cuh"
 #include "pipeline.cuh"
+#include "prefill.cuh"
 #include "tiled_layout.cuh"
 
 namespace {
@@ -182,6 +184,15 @@ struct m1moe_cuda_ctx {
     void *pinned[2] = {nullptr, nullptr};
     cudaEvent_t staged[2] = {nullptr, nullptr};
     int num_sms = 148;
+    // prefill (prefill.cuh): scratch for up to pf_cap tokens, grown on demand,
+    // and the tensor maps of the table (made on first use)
+    int pf_cap = 0, pf_nsplit = 0, pf_max_tiles = 0;
+    int *pf_idx = nullptr, *pf_tok_slot = nullptr, *pf_slot_tok = nullptr, *pf_ntiles = nullptr;
+    float *pf_w = nullptr, *pf_ypart = nullptr;
+    m1::PfTile *pf_tiles = nullptr;
+    uint8_t *pf_xg = nullptr, *pf_act = nullptr;
+    bool pf_maps = false;
+    CUtensorMap pf_map_gu{}, pf_map_dn{};
 };
 
 namespace {
@@ -213,6 +224,10 @@ void free_ctx(m1moe_cuda_ctx *c) {
     cudaFree(c->hout);
     cudaFree(c->hidx);
     cudaFree(c->hw);
+    for (void *q : {(void *)c->pf_idx, (void *)c->pf_tok_slot, (void *)c->pf_slot_tok,
+                    (void *)c->pf_ntiles, (void *)c->pf_w, (void *)c->pf_ypart, (void *)c->pf_tiles,
+                    (void *)c->pf_xg, (void *)c->pf_act})
+        cudaFree(q);
     for (int i = 0; i < 2; ++i) {
         if (c->pinned[i]) cudaFreeHost(c->pinned[i]);
         if (c->staged[i]) cudaEventDestroy(c->staged[i]);
@@ -461,6 +476,99 @@ m1moe_status repack_experts(m1moe_cuda_ctx *c, const uint8_t *d_src, uint8_t *d_
     m1::k_repack_tiled<<<grid, 128, 0, st>>>(d_src, (long long)c->expert_bytes, d_dst, c->tl, ro, n,
                                               c->cfg.hidden_dim, c->cfg.intermediate_dim,
                                               c->cfg.group_size);
+    M1_LAUNCHED();
+    return M1MOE_OK;
+}
+
+// ---------------------------------------------------------------- prefill ----
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The two tensor maps of the table: gate/up pair-rows as bytes [blocks][I][pr]
+// (box 32 bytes x 128 rows: one 64-column step of 128 rows), and the down
+// words [blocks][h/rc * I/8][rc] (box 128 rows x 8 column blocks).
+m1moe_status pf_make_maps(m1moe_cuda_ctx *c) {
+    if (c->pf_maps) return M1MOE_OK;
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    M1_CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (!fn || q != cudaDriverEntryPointSuccess)
+        return fail(M1MOE_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    auto encode = reinterpret_cast<EncodeTiledFn>(fn);
+    const m1::TiledLayout &tl = c->tl;
+    const cuuint64_t nblk = (cuuint64_t)c->cfg.num_layers * c->ne;
+    const cuuint32_t one[3] = {1, 1, 1};
+    {
+        const cuuint64_t dims[3] = {(cuuint64_t)tl.pr, (cuuint64_t)c->cfg.intermediate_dim, nblk};
+        const cuuint64_t strides[2] = {(cuuint64_t)tl.pr, (cuuint64_t)tl.block};
+        const cuuint32_t box[3] = {32, (cuuint32_t)m1::kPfRows, 1};
+        const CUresult r = encode(&c->pf_map_gu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, c->table, dims,
+                                  strides, box, one, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(M1MOE_ERR_CUDA, "gate/up tensor map: error %d", (int)r);
+    }
+    {
+        const cuuint64_t dims[3] = {(cuuint64_t)tl.rc,
+                                    (cuuint64_t)(c->cfg.hidden_dim / tl.rc) * tl.ncbI, nblk};
+        const cuuint64_t strides[2] = {(cuuint64_t)tl.rc * 4, (cuuint64_t)tl.block};
+        const cuuint32_t box[3] = {(cuuint32_t)m1::kPfRows, 8, 1};
+        const CUresult r = encode(&c->pf_map_dn, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3,
+                                  c->table + tl.dn_w, dims, strides, box, one,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(M1MOE_ERR_CUDA, "down tensor map: error %d", (int)r);
+    }
+    c->pf_maps = true;
+    return M1MOE_OK;
+}
+
+// Scratch for T tokens (grown, never shrunk; a synchronous reallocation).
+m1moe_status pf_reserve(m1moe_cuda_ctx *c, int T) {
+    if (T <= c->pf_cap) return M1MOE_OK;
+    const m1moe_cuda_cfg &g = c->cfg;
+    const long long pairs = (long long)T * g.top_k;
+    const int max_tiles = (int)std::min<long long>(c->ne, pairs) + (int)(pairs / m1::kPfTileTok) + 1;
+    const long long rows = pairs + 16LL * max_tiles;  // padded tile rows
+    // K splits of the down product: about four units per SM for one tile per
+    // used expert, each split at least 8 steps of 64 columns
+    const long long dn_units = (long long)std::min<long long>(c->ne, pairs) * (g.hidden_dim / m1::kPfRows);
+    int nsplit = (int)std::max<long long>(1, (4LL * c->num_sms + dn_units - 1) / dn_units);
+    nsplit = std::min(nsplit, std::max(1, g.intermediate_dim / 64 / 8));
+    M1_CK(cudaDeviceSynchronize());
+    for (void *q : {(void *)c->pf_idx, (void *)c->pf_tok_slot, (void *)c->pf_slot_tok,
+                    (void *)c->pf_ntiles, (void *)c->pf_w, (void *)c->pf_ypart, (void *)c->pf_tiles,
+                    (void *)c->pf_xg, (void *)c->pf_act})
+        cudaFree(q);
+    c->pf_idx = c->pf_tok_slot = c->pf_slot_tok = c->pf_ntiles = nullptr;
+    c->pf_w = c->pf_ypart = nullptr;
+    c->pf_tiles = nullptr;
+    c->pf_xg = c->pf_act = nullptr;
+    c->pf_cap = 0;
+    M1_CK(cudaMalloc((void **)&c->pf_idx, pairs * 4));
+    M1_CK(cudaMalloc((void **)&c->pf_tok_slot, pairs * 4));
+    M1_CK(cudaMalloc((void **)&c->pf_slot_tok, pairs * 4));
+    M1_CK(cudaMalloc((void **)&c->pf_ntiles, 4));
+    M1_CK(cudaMalloc((void **)&c->pf_w, pairs * 4));
+    M1_CK(cudaMalloc((void **)&c->pf_ypart, (size_t)nsplit * pairs * g.hidden_dim * 4));
+    M1_CK(cudaMalloc((void **)&c->pf_tiles, (size_t)max_tiles * sizeof(m1::PfTile)));
+    M1_CK(cudaMalloc((void **)&c->pf_xg, (size_t)rows * g.hidden_dim * 2));
+    M1_CK(cudaMalloc((void **)&c->pf_act, (size_t)rows * g.intermediate_dim * 2));
+    c->pf_cap = T;
+    c->pf_nsplit = nsplit;
+    c->pf_max_tiles = max_tiles;
+    return M1MOE_OK;
+}
+
+template <int KIND>
+m1moe_status pf_gemm(m1moe_cuda_ctx *c, const m1::PrefillParams &p, const CUtensorMap &map,
+                     cudaStream_t st) {
+    const int smem = m1::PfStage<KIND>::smem;
+    M1_CK(cudaFuncSetAttribute(m1::k_prefill_gemm<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem));
+    m1::k_prefill_gemm<KIND><<<c->num_sms, m1::kPfThreads, smem, st>>>(p, map);
     M1_LAUNCHED();
     return M1MOE_OK;
 }
@@ -844,6 +952,78 @@ m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *
     p.user_idx = d_idx;
     p.user_w = d_w;
     return dispatch_layer(c, p, as_stream(stream));
+}
+
+m1moe_status m1moe_cuda_moe_prefill(m1moe_cuda_ctx *c, int32_t layer, const void *d_x,
+                                    int32_t x_dtype, const void *d_res, int32_t res_dtype,
+                                    void *d_out, int32_t out_dtype, int32_t T, int32_t *d_idx,
+                                    float *d_w, void *stream) {
+    if (m1moe_status st = check_layer(c, layer)) return st;
+    if (!d_x || !d_out) return fail(M1MOE_ERR_INVALID_ARG, "x/out is NULL");
+    if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype) || (d_res && !valid_dtype(res_dtype)))
+        return fail(M1MOE_ERR_INVALID_ARG, "dtype must be F32 (0) or BF16 (1)");
+    if (T < 1) return fail(M1MOE_ERR_INVALID_ARG, "tokens %d < 1", T);
+    const m1moe_cuda_cfg &g = c->cfg;
+    if (g.group_size != 64 || g.intermediate_dim % m1::kPfRows)
+        return fail(M1MOE_ERR_UNSUPPORTED,
+                    "prefill needs group_size 64 and intermediate_dim a multiple of 128");
+    if ((long long)T * g.top_k > (1LL << 24))
+        return fail(M1MOE_ERR_INVALID_ARG, "tokens %d: at most %d (token, expert) pairs", T, 1 << 24);
+    if (!c->router_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "router of layer %d not loaded", layer);
+    if (!c->layer_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "experts of layer %d not loaded", layer);
+    DeviceGuard dg(g.device);
+    if (m1moe_status st = pf_make_maps(c)) return st;
+    if (m1moe_status st = pf_reserve(c, T)) return st;
+    m1::PrefillParams p{};
+    p.table = c->table + (size_t)layer * c->ne * c->tl.block;
+    p.tl = c->tl;
+    p.router = c->router + (size_t)layer * g.num_experts * g.hidden_dim;
+    p.E = g.num_experts;
+    p.K = g.top_k;
+    p.h = g.hidden_dim;
+    p.I = g.intermediate_dim;
+    p.gs = g.group_size;
+    p.norm = g.norm_topk_prob;
+    p.e0 = c->e0;
+    p.ne = c->ne;
+    p.zblock = layer * c->ne;
+    p.T = T;
+    p.x = d_x;
+    p.x_bf16 = x_dtype == M1MOE_DTYPE_BF16;
+    p.res = d_res;
+    p.res_bf16 = res_dtype == M1MOE_DTYPE_BF16;
+    p.out = d_out;
+    p.out_bf16 = out_dtype == M1MOE_DTYPE_BF16;
+    p.user_idx = d_idx;
+    p.user_w = d_w;
+    p.idx = c->pf_idx;
+    p.w = c->pf_w;
+    p.tok_slot = c->pf_tok_slot;
+    p.slot_tok = c->pf_slot_tok;
+    p.tiles = c->pf_tiles;
+    p.ntiles = c->pf_ntiles;
+    p.max_tiles = c->pf_max_tiles;
+    p.xg = c->pf_xg;
+    p.act = c->pf_act;
+    p.ypart = c->pf_ypart;
+    p.nsplit = c->pf_nsplit;
+    p.err = c->err;
+    cudaStream_t st = as_stream(stream);
+    const size_t rsmem = (size_t)g.hidden_dim * 4;
+    if (rsmem > 48 * 1024)
+        M1_CK(cudaFuncSetAttribute(m1::k_prefill_route, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)rsmem));
+    m1::k_prefill_route<<<T, 256, rsmem, st>>>(p);
+    M1_LAUNCHED();
+    m1::k_prefill_plan<<<1, 1024, 0, st>>>(p);
+    M1_LAUNCHED();
+    m1::k_prefill_gather<<<dim3(p.max_tiles, m1::kPfTileTok / 8), 256, 0, st>>>(p);
+    M1_LAUNCHED();
+    if (m1moe_status s2 = pf_gemm<m1::kGateUp>(c, p, c->pf_map_gu, st)) return s2;
+    if (m1moe_status s2 = pf_gemm<m1::kDown>(c, p, c->pf_map_dn, st)) return s2;
+    m1::k_prefill_combine<<<dim3(T, (g.hidden_dim + 255) / 256), 256, 0, st>>>(p);
+    M1_LAUNCHED();
+    return M1MOE_OK;
 }
 
 m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *c, int32_t layer, const float *h_x,

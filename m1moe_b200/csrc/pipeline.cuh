@@ -14,6 +14,7 @@ namespace m1 {
 // Device error word bits (m1moe_cuda_synchronize reports them as M1MOE_ERR_DEVICE).
 constexpr int kErrWaitTimeout = 1;   // an mbarrier wait exceeded its iteration limit
 constexpr int kErrBadExpert = 2;     // a routed expert index was out of range
+constexpr int kErrRange = 4;         // a value left the fp16 range of the tensor-core operands
 
 // A wait gives up after this many try_wait polls (each poll may suspend the
 // thread for a hardware-defined interval), i.e. far longer than any copy.

@@ -126,6 +126,32 @@ class MoEBlock:
         out_v = out.squeeze(0) if x.dim() == 1 else out
         return (out_v, idx, w) if return_topk else out_v
 
+    def prefill(self, layer: int, x: torch.Tensor, residual: torch.Tensor | None = None, *,
+                out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float32,
+                return_topk: bool = False, stream=None):
+        """forward() for many tokens x [T][h] at once: grouped GEMMs on the tensor
+        cores (m1moe_cuda_moe_prefill); the same result within the FFN tolerance."""
+        x2 = x.unsqueeze(0) if x.dim() == 1 else x
+        T = x2.shape[0]
+        if out is None:
+            out = torch.empty((T, self.hidden_dim), dtype=out_dtype, device=x.device)
+        _check_cuda(x2, out)
+        res_ptr, res_dt = 0, 0
+        if residual is not None:
+            r2 = residual.unsqueeze(0) if residual.dim() == 1 else residual
+            _check_cuda(r2)
+            res_ptr, res_dt = r2.data_ptr(), dtype_code(r2.dtype)
+        idx = w = None
+        if return_topk:
+            idx = torch.empty((T, self.top_k), dtype=torch.int32, device=x.device)
+            w = torch.empty((T, self.top_k), dtype=torch.float32, device=x.device)
+        _lib.call("m1moe_cuda_moe_prefill", self._ctx, layer, x2.data_ptr(), dtype_code(x2.dtype),
+                  res_ptr, res_dt, out.data_ptr(), dtype_code(out.dtype), T,
+                  idx.data_ptr() if idx is not None else 0,
+                  w.data_ptr() if w is not None else 0, _stream(stream))
+        out_v = out.squeeze(0) if x.dim() == 1 else out
+        return (out_v, idx, w) if return_topk else out_v
+
     def forward_host(self, layer: int, x: np.ndarray, residual: np.ndarray | None = None):
         """Synchronous host-buffer call with the reference's f32 buffers.
         Returns (out f32[B][h], idx int32[B][K], w f32[B][K])."""

@@ -3,6 +3,7 @@
     python -m m1moe_b200.profile_cases layer olmoe 1     # k_moe_layer, OLMoE shapes, batch 1
     python -m m1moe_b200.profile_cases layer mixtral 1   # k_moe_layer, Mixtral shapes
     python -m m1moe_b200.profile_cases matvec 1          # k_matvec4_ring over 2048 matrices
+    python -m m1moe_b200.profile_cases prefill mixtral 512  # k_prefill_gemm, 512 tokens
 
 Each case builds synthetic weights (m1moe_b200.synth), runs the kernel a few
 times and exits 0; the device footprint stays at a few GB so that a profiler
@@ -65,9 +66,39 @@ def matvec_case(batch: int) -> None:
     print("ok")
 
 
+def prefill_case(workload: str, tokens: int) -> None:
+    import torch
+
+    from m1moe_b200 import MoEBlock, synth
+
+    if workload == "olmoe":
+        h, inter, e, k, norm = 2048, 1024, 64, 8, False
+    elif workload == "mixtral":
+        h, inter, e, k, norm = 4096, 14336, 8, 2, True
+    else:
+        raise SystemExit(f"unknown workload {workload!r}")
+    torch.cuda.set_device(0)
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=inter, num_experts=e, top_k=k, num_layers=1,
+                   max_batch=8, norm_topk_prob=norm)
+    img = synth.layer_image_device(e, h, inter, 64, seed=0, device="cuda")
+    blk.load_expert_layer(0, img)
+    del img
+    blk.load_router(0, synth.router_weights(100, e, h))
+    x = torch.randn(tokens, h, device="cuda").to(torch.bfloat16)
+    out = torch.empty(tokens, h, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):
+        blk.prefill(0, x, None, out=out)
+    torch.cuda.synchronize()
+    blk.synchronize()
+    blk.close()
+    print("ok")
+
+
 def main(argv: list[str]) -> None:
     if len(argv) >= 1 and argv[0] == "layer":
         layer_case(argv[1] if len(argv) > 1 else "olmoe", int(argv[2]) if len(argv) > 2 else 1)
+    elif len(argv) >= 1 and argv[0] == "prefill":
+        prefill_case(argv[1] if len(argv) > 1 else "mixtral", int(argv[2]) if len(argv) > 2 else 512)
     elif len(argv) >= 1 and argv[0] == "matvec":
         matvec_case(int(argv[1]) if len(argv) > 1 else 1)
     else:

@@ -294,7 +294,7 @@ def prefill_measure(dev, steps: int, warmup: int) -> dict:
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak[0], "unit": "TFLOP/s",
                          "frac": tflops / peak[0], "peak_source": peak[1],
                          "kernel": "m1moe_cuda_moe_prefill (k_prefill_gemm gate/up + down)"},
-            "dtype": "bf16 operands (int4 weights dequantised), fp32 accumulation"}
+            "dtype": "fp16 operands (int4 weights dequantised), fp32 accumulation"}
 
 
 def run_gpu(args, wl) -> None:

@@ -351,27 +351,19 @@ def run_gpu(args, wl) -> None:
             if events is not None:
                 events[L].record()
     else:
-        # Expert parallel (m1moe_b200.expert_parallel): gather every rank's
-        # token, apply the local experts to all of them, reduce-scatter the
-        # partial sums back to the owners.
-        from m1moe_b200.expert_parallel import EPStep
-        cur = {"layer": 0}
-
-        def local(x_all, res_all, out_all):
-            layer = cur["layer"]
-            _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, x_all.data_ptr(), 0,
-                      res_all.data_ptr(), 0, out_all.data_ptr(), 0, B, idx_log[layer].data_ptr(),
-                      w_log[layer].data_ptr(), stream.cuda_stream)
-
-        ep = EPStep(local, b, h, device=dev)
-        nxt = ep.out
+        # Expert parallel in the kernel over NVLink peer memory
+        # (m1moe_b200.expert_parallel.EPFused): per layer one launch per GPU
+        # gathers every rank's token, applies the local experts and returns each
+        # rank its own token's sum; no collective library call per layer.
+        from m1moe_b200.expert_parallel import EPFused
+        ep = EPFused(blk, b)
+        nxt = torch.zeros((b, h), dtype=torch.float32, device=dev)
 
         def one_step(events=None):
             for layer in range(L):
                 if events is not None:
                     events[layer].record()
-                cur["layer"] = layer
-                ep(own)
+                ep(layer, own, own, out=nxt, idx=idx_log[layer], w=w_log[layer], stream=stream)
             if events is not None:
                 events[L].record()
 

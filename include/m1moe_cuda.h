@@ -208,6 +208,38 @@ M1MOE_API m1moe_status m1moe_cuda_moe_prefill(m1moe_cuda_ctx *ctx, int32_t layer
                                     void *d_out, int32_t out_dtype, int32_t tokens,
                                     int32_t *d_topk_idx, float *d_topk_w, void *stream);
 
+/* Expert parallelism over NVLink peer memory (one process per GPU, all on one
+ * node), the expert-parallel decode step: every rank owns tokens_per_rank
+ * tokens and the experts of its shard (expert_begin/expert_count); one call
+ * per layer gathers all ranks' tokens, applies the local experts and returns
+ * each rank its own tokens' full MoE output, with no collective library in
+ * between.  The reference runs on one GPU and has no counterpart; it is the
+ * multi-GPU mode of runLayer's MoE part (InferenceEngine.swift:240-266).
+ *
+ * Setup, on every rank: m1moe_cuda_ep_region(ctx, world, tokens_per_rank,
+ * handle) allocates this rank's exchange region and writes its 64-byte CUDA
+ * IPC handle to `handle`; the caller gathers the handles of all ranks (any
+ * host transport) into world x 64 bytes in rank order and calls
+ * m1moe_cuda_ep_connect(ctx, rank, handles).  world * tokens_per_rank must
+ * not exceed the context's max_batch; world is 2..8. */
+M1MOE_API m1moe_status m1moe_cuda_ep_region(m1moe_cuda_ctx *ctx, int32_t world,
+                                  int32_t tokens_per_rank, void *h_handle_out);
+M1MOE_API m1moe_status m1moe_cuda_ep_connect(m1moe_cuda_ctx *ctx, int32_t rank,
+                                   const void *h_handles);
+
+/* One expert-parallel MoE step for this rank's tokens (stream-ordered):
+ * d_x, d_residual and d_out hold this rank's tokens_per_rank tokens; out =
+ * residual + sum over ALL ranks' experts.  Every rank must make the same
+ * sequence of calls (a call waits, bounded, for the other ranks' inputs and
+ * partial sums; a rank that stops calling makes the others time out with
+ * M1MOE_ERR_DEVICE on m1moe_cuda_synchronize).  d_topk_idx/d_topk_w, if not
+ * NULL, receive [world*tokens_per_rank][top_k] for all ranks' tokens in rank
+ * order.  After an error the contexts of all ranks must be recreated. */
+M1MOE_API m1moe_status m1moe_cuda_moe_layer_ep(m1moe_cuda_ctx *ctx, int32_t layer, const void *d_x,
+                                     int32_t x_dtype, const void *d_residual,
+                                     int32_t res_dtype, void *d_out, int32_t out_dtype,
+                                     int32_t *d_topk_idx, float *d_topk_w, void *stream);
+
 /* Synchronous host-buffer form of m1moe_cuda_moe_layer with the reference's
  * f32 buffers (buf_h_mid, buf_residual -> buf_moe_out, MetalContext.swift
  * :134-152): copies in, runs, copies out and waits.  h_topk_* may be NULL. */

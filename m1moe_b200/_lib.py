@@ -59,6 +59,10 @@ _SIGS = [
      [_vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp]),
     ("m1moe_cuda_moe_prefill", ctypes.c_int,
      [_vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp]),
+    ("m1moe_cuda_ep_region", ctypes.c_int, [_vp, _i32, _i32, _vp]),
+    ("m1moe_cuda_ep_connect", ctypes.c_int, [_vp, _i32, _vp]),
+    ("m1moe_cuda_moe_layer_ep", ctypes.c_int,
+     [_vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp, _vp]),
     ("m1moe_cuda_moe_layer_host", ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp]),
     ("m1moe_cuda_synchronize", ctypes.c_int, [_vp]),
     ("m1moe_cuda_launch_count", ctypes.c_int64, []),

@@ -358,7 +358,7 @@ __device__ __forceinline__ void load_x32_any(const void *x, int is_bf16, size_t 
         const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + at);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const float4 r = __ldg(p + i);
+            const float4 r = __ldcg(p + i);  // coherent: x may come from peers during the launch
             v[4 * i] = r.x;
             v[4 * i + 1] = r.y;
             v[4 * i + 2] = r.z;

@@ -193,6 +193,11 @@ struct m1moe_cuda_ctx {
     uint8_t *pf_xg = nullptr, *pf_act = nullptr;
     bool pf_maps = false;
     CUtensorMap pf_map_gu{}, pf_map_dn{};
+    // expert parallelism over peer memory (moe_layer.cuh EpLayout)
+    int ep_world = 1, ep_rank = 0, ep_b = 0;
+    uint8_t *ep_region = nullptr;              // this rank's exchange region
+    uint8_t *ep_peer[m1::kMaxRanks] = {};      // every rank's region as mapped here
+    bool ep_ready = false;                     // every peer mapped
 };
 
 namespace {
@@ -228,6 +233,9 @@ void free_ctx(m1moe_cuda_ctx *c) {
                     (void *)c->pf_ntiles, (void *)c->pf_w, (void *)c->pf_ypart, (void *)c->pf_tiles,
                     (void *)c->pf_xg, (void *)c->pf_act})
         cudaFree(q);
+    for (int r = 0; r < m1::kMaxRanks; ++r)
+        if (c->ep_peer[r] && c->ep_peer[r] != c->ep_region) cudaIpcCloseMemHandle(c->ep_peer[r]);
+    cudaFree(c->ep_region);
     for (int i = 0; i < 2; ++i) {
         if (c->pinned[i]) cudaFreeHost(c->pinned[i]);
         if (c->staged[i]) cudaEventDestroy(c->staged[i]);
@@ -1024,6 +1032,80 @@ m1moe_status m1moe_cuda_moe_prefill(m1moe_cuda_ctx *c, int32_t layer, const void
     m1::k_prefill_combine<<<dim3(T, (g.hidden_dim + 255) / 256), 256, 0, st>>>(p);
     M1_LAUNCHED();
     return M1MOE_OK;
+}
+
+m1moe_status m1moe_cuda_ep_region(m1moe_cuda_ctx *c, int32_t world, int32_t tokens_per_rank,
+                                 void *h_handle) {
+    if (!c || !h_handle) return fail(M1MOE_ERR_INVALID_ARG, "ctx/handle is NULL");
+    if (world < 2 || world > m1::kMaxRanks)
+        return fail(M1MOE_ERR_INVALID_ARG, "world %d outside [2,%d]", world, m1::kMaxRanks);
+    if (tokens_per_rank < 1 || (long long)world * tokens_per_rank > c->cfg.max_batch)
+        return fail(M1MOE_ERR_INVALID_ARG, "world %d x tokens %d exceeds max_batch %d", world,
+                    tokens_per_rank, c->cfg.max_batch);
+    if (c->ep_region) return fail(M1MOE_ERR_INVALID_ARG, "exchange region already made");
+    DeviceGuard dg(c->cfg.device);
+    const m1::EpLayout el = m1::ep_layout(world, tokens_per_rank, c->cfg.hidden_dim);
+    M1_CK(cudaMalloc((void **)&c->ep_region, (size_t)el.bytes));
+    M1_CK(cudaMemset(c->ep_region, 0, (size_t)el.bytes));
+    cudaIpcMemHandle_t hnd;
+    M1_CK(cudaIpcGetMemHandle(&hnd, c->ep_region));
+    std::memcpy(h_handle, &hnd, sizeof(hnd));
+    c->ep_world = world;
+    c->ep_b = tokens_per_rank;
+    return M1MOE_OK;
+}
+
+m1moe_status m1moe_cuda_ep_connect(m1moe_cuda_ctx *c, int32_t rank, const void *h_handles) {
+    if (!c || !h_handles) return fail(M1MOE_ERR_INVALID_ARG, "ctx/handles is NULL");
+    if (!c->ep_region) return fail(M1MOE_ERR_INVALID_ARG, "no exchange region (m1moe_cuda_ep_region)");
+    if (rank < 0 || rank >= c->ep_world)
+        return fail(M1MOE_ERR_INVALID_ARG, "rank %d outside [0,%d)", rank, c->ep_world);
+    DeviceGuard dg(c->cfg.device);
+    const uint8_t *hb = static_cast<const uint8_t *>(h_handles);
+    for (int o = 0; o < c->ep_world; ++o) {
+        if (o == rank) {
+            c->ep_peer[o] = c->ep_region;
+            continue;
+        }
+        cudaIpcMemHandle_t hnd;
+        std::memcpy(&hnd, hb + (size_t)o * sizeof(hnd), sizeof(hnd));
+        void *ptr = nullptr;
+        M1_CK(cudaIpcOpenMemHandle(&ptr, hnd, cudaIpcMemLazyEnablePeerAccess));
+        c->ep_peer[o] = static_cast<uint8_t *>(ptr);
+    }
+    c->ep_rank = rank;
+    c->ep_ready = true;
+    return M1MOE_OK;
+}
+
+m1moe_status m1moe_cuda_moe_layer_ep(m1moe_cuda_ctx *c, int32_t layer, const void *d_x,
+                                     int32_t x_dtype, const void *d_res, int32_t res_dtype,
+                                     void *d_out, int32_t out_dtype, int32_t *d_idx, float *d_w,
+                                     void *stream) {
+    if (m1moe_status st = check_layer(c, layer)) return st;
+    if (!d_x || !d_out) return fail(M1MOE_ERR_INVALID_ARG, "x/out is NULL");
+    if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype) || (d_res && !valid_dtype(res_dtype)))
+        return fail(M1MOE_ERR_INVALID_ARG, "dtype must be F32 (0) or BF16 (1)");
+    if (!c->ep_ready) return fail(M1MOE_ERR_INVALID_ARG, "not connected (m1moe_cuda_ep_connect)");
+    if (!c->router_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "router of layer %d not loaded", layer);
+    if (!c->layer_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "experts of layer %d not loaded", layer);
+    DeviceGuard dg(c->cfg.device);
+    const int B = c->ep_world * c->ep_b;
+    m1::LayerParams p = layer_params(c, layer, B);
+    p.x = d_x;
+    p.x_bf16 = x_dtype == M1MOE_DTYPE_BF16;
+    p.res = d_res;
+    p.res_bf16 = res_dtype == M1MOE_DTYPE_BF16;
+    p.out = d_out;
+    p.out_bf16 = out_dtype == M1MOE_DTYPE_BF16;
+    p.out_acc = 1;  // sums in the accumulator; the last CTA exchanges and writes out
+    p.user_idx = d_idx;
+    p.user_w = d_w;
+    p.ep_world = c->ep_world;
+    p.ep_rank = c->ep_rank;
+    p.ep_b = c->ep_b;
+    for (int o = 0; o < c->ep_world; ++o) p.ep_base[o] = c->ep_peer[o];
+    return dispatch_layer(c, p, as_stream(stream));
 }
 
 m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *c, int32_t layer, const float *h_x,

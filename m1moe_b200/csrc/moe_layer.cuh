@@ -68,6 +68,27 @@ constexpr int kMaxStages = 32;
 constexpr int kLayerSlots = 32;  // tiles in flight per CTA at most (a power of two)
 constexpr int kMaxCtas = 1024;
 constexpr int kEpochStride = 32;  // words between two CTAs' epoch words (own 128-byte line)
+constexpr int kMaxRanks = 8;      // expert-parallel ranks joined over peer memory
+
+// Expert parallelism over NVLink peer memory: every rank owns one exchange
+// region (its own device memory, mapped into the other ranks' address space)
+// laid out the same way on all ranks, for `world` ranks of `b` tokens:
+//   [0]                   x-ready flags, one 128-byte line per source rank
+//   [world*128]           done flags, one 128-byte line per source rank
+//   [2*world*128]         the call counter (one line)
+//   [xs_off]              gathered x, f32 [2][world*b][h] (by call parity)
+//   [recv_off]            partial sums received, f32 [2][world][b][h]
+struct EpLayout {
+    long long xs_off, recv_off, bytes;
+};
+
+__host__ __device__ inline EpLayout ep_layout(int world, int b, int h) {
+    EpLayout l;
+    l.xs_off = (2LL * world + 1) * 128;
+    l.recv_off = l.xs_off + 2LL * world * b * h * 4;
+    l.bytes = l.recv_off + 2LL * world * b * h * 4;
+    return l;
+}
 
 // Gate/up work items for NT tokens: an item covers PG "row pairs" (rows R and
 // R+4 of an expert, R % 8 < 4: the two rows whose activations share one
@@ -115,6 +136,11 @@ struct LayerParams {
     float *user_scores;  // optional [ntok][E]
     int *err;         // device error word
     unsigned long long *trace;  // optional phase timestamps
+    // expert parallelism (ep_world > 1): tokens [ep_rank*ep_b, +ep_b) of the
+    // ntok = ep_world*ep_b are this rank's (x, residual and out point at them);
+    // ep_base[r] is rank r's exchange region as mapped here
+    int ep_world, ep_rank, ep_b;
+    uint8_t *ep_base[kMaxRanks];
     // geometry (host-planned)
     int stage_bytes;       // largest tile (bytes)
     int ring_bytes;        // bytes of the tile ring
@@ -191,6 +217,16 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
 
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys_u32(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long tagged(unsigned tag, uint32_t payload) {
@@ -703,6 +739,55 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     Producer ps;       // the producer warp's state (warp 24)
     uint64_t pol = 0;  // its L2 policy for the streamed weights
     const int i0 = (int)((long long)h * blk / G), i1 = (int)((long long)h * (blk + 1) / G);
+    // ---- expert parallelism: gather x from every rank over peer memory ----
+    const bool ep = p.ep_world > 1;
+    const void *X = p.x;
+    int Xbf16 = p.x_bf16;
+    unsigned ep_tag = 0;
+    int ep_par = 0;
+    if (ep) {
+        const EpLayout el = ep_layout(p.ep_world, p.ep_b, h);
+        uint8_t *mine = p.ep_base[p.ep_rank];
+        // every rank makes the same sequence of EP calls: the call counter
+        // (advanced by the last CTA at the end of a call) names the call
+        ep_tag = ld_acquire_sys_u32(reinterpret_cast<const unsigned *>(mine + 2LL * p.ep_world * 128)) + 1u;
+        ep_par = ep_tag & 1;
+        // CTA 0 writes this rank's tokens into every rank's gathered-x slot
+        // for this call's parity, then raises one tagged flag per rank (148
+        // CTAs adding to one counter over NVLink serialise for ~10 us)
+        const int nb = p.ep_b;
+        if (blk == 0) {
+            for (int q = tid; q < p.ep_world * nb * h; q += kLayerThreads) {
+                const int o = q / (nb * h), rem = q - o * nb * h;
+                float *xs = reinterpret_cast<float *>(p.ep_base[o] + el.xs_off) +
+                            ((size_t)ep_par * p.ep_world + p.ep_rank) * nb * h;
+                xs[rem] = load_act(p.x, p.x_bf16, rem);
+            }
+            // the barrier orders every thread's stores before the release
+            // stores of the flags (release is cumulative): one system-scope
+            // release per rank instead of a system fence in every thread
+            __syncthreads();
+            if (tid < p.ep_world)
+                st_release_sys_u32(reinterpret_cast<unsigned *>(p.ep_base[tid]) + p.ep_rank * 32, ep_tag);
+        }
+        // every rank's tokens have arrived
+        if (tid < p.ep_world) {
+            const unsigned *fl = reinterpret_cast<const unsigned *>(mine) + tid * 32;
+            bool ok = false;
+            for (uint32_t it = 0, nap = 32; it < kWaitLimit; ++it) {
+                if (ld_acquire_sys_u32(fl) == ep_tag) {
+                    ok = true;
+                    break;
+                }
+                __nanosleep(nap);
+                nap = min(nap * 2, 256u);
+            }
+            if (!ok) set_abort(ctl, p.err);
+        }
+        __syncthreads();
+        X = reinterpret_cast<const float *>(mine + el.xs_off) + (size_t)ep_par * p.ep_world * nb * h;
+        Xbf16 = 0;
+    }
     const int nrows = i1 - i0;
     if (warp < 8) {
         // ---- phase 2: logits of this CTA's experts, straight from global memory ----
@@ -728,9 +813,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 for (int t = 0; t < NT; ++t) {
                     if (t < p.ntok) {
                         float xv[8];
-                        if (p.x_bf16) {
-                            const uint4 r = __ldg(reinterpret_cast<const uint4 *>(
-                                reinterpret_cast<const uint16_t *>(p.x) + (size_t)t * h) + g8);
+                        if (Xbf16) {
+                            const uint4 r = *(reinterpret_cast<const uint4 *>(
+                                reinterpret_cast<const uint16_t *>(X) + (size_t)t * h) + g8);
                             const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
@@ -739,8 +824,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                             }
                         } else {
                             const float4 *xf = reinterpret_cast<const float4 *>(
-                                reinterpret_cast<const float *>(p.x) + (size_t)t * h) + 2 * g8;
-                            const float4 a0 = __ldg(xf), a1 = __ldg(xf + 1);
+                                reinterpret_cast<const float *>(X) + (size_t)t * h) + 2 * g8;
+                            const float4 a0 = __ldcg(xf), a1 = __ldcg(xf + 1);
                             xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
                             xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
                         }
@@ -801,7 +886,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             float *dst = p.out_acc ? p.acc : reinterpret_cast<float *>(p.out);
             for (int q = st; q < p.ntok * nrows; q += nst) {
                 const int t = q / nrows, i = i0 + q % nrows;
-                dst[(size_t)t * h + i] = p.res ? load_act(p.res, p.res_bf16, (size_t)t * h + i) : 0.f;
+                // (expert parallel: the residual is added once, by the owner, at the end)
+                dst[(size_t)t * h + i] = (p.res && !ep) ? load_act(p.res, p.res_bf16, (size_t)t * h + i) : 0.f;
             }
         }
         named_sync(4, nst);
@@ -814,7 +900,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         for (int q = st; q < p.ntok * nch; q += nst) {
             const int t = q / nch, c = q - t * nch;
             float v[32];
-            load_x32_any(p.x, p.x_bf16, (size_t)t * h + (size_t)c * kChunkCols, v);
+            load_x32_any(X, Xbf16, (size_t)t * h + (size_t)c * kChunkCols, v);
             xsc[q] = quant_chunk_i16(v, xq + (size_t)t * (h / 2), nch, c, &xsum[q]);
         }
         if (warp == kConsumerWarps) {
@@ -1166,7 +1252,53 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 ctl.last = atomicAdd(p.done, 1) == G - 1;
             }
             named_sync(1, kConsumerThreads);
-            if (ctl.last) {
+            if (ctl.last && ep) {
+                __threadfence();
+                // expert parallel: send each rank the partial sums of its tokens,
+                // then add those received to this rank's own, in rank order
+                const EpLayout el = ep_layout(p.ep_world, p.ep_b, h);
+                const int W = p.ep_world, nb = p.ep_b, me = p.ep_rank;
+                uint8_t *mine = p.ep_base[me];
+                for (int q = tid; q < W * nb * h; q += kConsumerThreads) {
+                    const int o = q / (nb * h);
+                    if (o == me) continue;
+                    const int rem = q - o * nb * h;
+                    float *rv = reinterpret_cast<float *>(p.ep_base[o] + el.recv_off) +
+                                ((size_t)ep_par * W + me) * nb * h;
+                    rv[rem] = __ldcg(p.acc + (size_t)o * nb * h + rem);
+                }
+                named_sync(1, kConsumerThreads);  // then the release stores below
+                if (tid < W && tid != me)
+                    st_release_sys_u32(reinterpret_cast<unsigned *>(p.ep_base[tid] + (size_t)W * 128) + me * 32,
+                                       ep_tag);
+                if (tid < W && tid != me && !ctl.abort) {
+                    const unsigned *fl = reinterpret_cast<const unsigned *>(mine + (size_t)W * 128) + tid * 32;
+                    bool ok = false;
+                    for (uint32_t it = 0, nap = 32; it < kWaitLimit; ++it) {
+                        if (ld_acquire_sys_u32(fl) == ep_tag) {
+                            ok = true;
+                            break;
+                        }
+                        __nanosleep(nap);
+                        nap = min(nap * 2, 256u);
+                    }
+                    if (!ok) set_abort(ctl, p.err);
+                }
+                named_sync(1, kConsumerThreads);
+                const float *rv = reinterpret_cast<const float *>(mine + el.recv_off) + (size_t)ep_par * W * nb * h;
+                for (int q = tid; q < nb * h; q += kConsumerThreads) {
+                    float v = p.res ? load_act(p.res, p.res_bf16, q) : 0.f;
+                    for (int o = 0; o < W; ++o)
+                        v += o == me ? __ldcg(p.acc + (size_t)me * nb * h + q) : __ldcg(rv + (size_t)o * nb * h + q);
+                    if (p.out_bf16)
+                        reinterpret_cast<__nv_bfloat16 *>(p.out)[q] = __float2bfloat16_rn(v);
+                    else
+                        reinterpret_cast<float *>(p.out)[q] = v;
+                }
+                // the call is complete on this rank: advance its call counter
+                if (tid == 0) st_release_sys_u32(reinterpret_cast<unsigned *>(mine + 2LL * W * 128), ep_tag);
+                if (tid == 0) *p.done = 0;
+            } else if (ctl.last) {
                 __threadfence();
                 if (p.out_bf16) {
                     __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(p.out);

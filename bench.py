@@ -312,7 +312,10 @@ def run_gpu(args, wl) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        # host-side plumbing only (barriers, the timing reductions, the IPC
+        # handle exchange): the expert-parallel data path is peer memory
+        # inside the kernel, so no collective library sits on it
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     E, h, I, K, L = wl["E"], wl["h"], wl["I"], wl["K"], wl["layers"]
     from m1moe_b200.expert_parallel import shard
     b = args.tokens_per_rank
@@ -425,7 +428,7 @@ def run_gpu(args, wl) -> None:
         len({e for e in idx_last[layer].ravel().tolist() if e0 <= e < e0 + ne}) * eb
         + router_bytes(wl) for layer in range(L))
 
-    t = torch.tensor([ms, float(step_bytes_local)], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms, float(step_bytes_local)], dtype=torch.float64)
     if world > 1:
         tmax = t[:1].clone()
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
@@ -485,7 +488,7 @@ def run_gpu(args, wl) -> None:
                 hout.copy_(nxt, non_blocking=True)
             s1.record(stream)
         torch.cuda.synchronize()
-        te = torch.tensor([s0.elapsed_time(s1)], dtype=torch.float64, device=dev)
+        te = torch.tensor([s0.elapsed_time(s1)], dtype=torch.float64)
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e = {"value": job_step_bytes * args.steps / (te.item() * 1e-3) / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": b * h * 4, "d2h_bytes_per_step": b * h * 4,

@@ -380,12 +380,17 @@ m1moe_status launch_layer(m1moe_cuda_ctx *c, m1::LayerParams p, cudaStream_t st)
     cfg.blockDim = dim3(m1::kLayerThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    // Cooperative: every CTA is resident at once, which the grid barriers need.
-    cudaLaunchAttribute attr[1];
+    // Cooperative: every CTA is resident at once, which the waits on other
+    // CTAs need.  Programmatic stream serialisation: the launch may be
+    // scheduled while the previous kernel in the stream finishes (the kernel
+    // waits for that grid before touching memory), hiding the launch gap.
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, m1::k_moe_layer<NT>, p);
     if (e != cudaSuccess) return cuda_fail(e, "k_moe_layer launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);

@@ -725,6 +725,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     const TiledLayout &tl = p.tl;
     unsigned *my_epoch = p.epochs + (size_t)blk * kEpochStride;
 
+    // programmatic dependent launch: let the next launch in the stream be
+    // scheduled now, and touch nothing until the previous grid has completed
+    // and its memory is visible (no-ops without a dependent launch)
+    pdl_trigger();
+    pdl_wait();
     if (tid == 0) {
         trace_event(p.trace, 0, 0);
         ctl.abort = 0;

@@ -370,7 +370,14 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
             }
             const unsigned long long *kt = keys + (size_t)t * E;
             const unsigned long long ki = kt[e];
-            for (int f = part; f < E; f += P) cnt += kt[f] > ki ? 1 : 0;
+            // four independent loads in flight per round (a plain loop waits
+            // out each shared-memory load in turn)
+            int f = part;
+            for (; f + 3 * P < E; f += 4 * P) {
+                const unsigned long long k0 = kt[f], k1 = kt[f + P], k2 = kt[f + 2 * P], k3 = kt[f + 3 * P];
+                cnt += (k0 > ki ? 1 : 0) + (k1 > ki ? 1 : 0) + (k2 > ki ? 1 : 0) + (k3 > ki ? 1 : 0);
+            }
+            for (; f < E; f += P) cnt += kt[f] > ki ? 1 : 0;
         }
         for (int o = 1; o < P; o <<= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
         if (i < nel && part == 0 && cnt < K) rs.idx[t][cnt] = e;
@@ -1066,40 +1073,51 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         }
         if (tid == 0) trace_event(p.trace, 0, 17);
         named_sync(1, kConsumerThreads);  // every gate/up item of this CTA is done
-        // Activations of this CTA's rows, in three short passes: (1) one thread
+        // Activations of this CTA's rows, in two short passes: (1) one thread
         // per (row, token) sums the column slices in order and applies SwiGLU
-        // where items left partial sums; (2) one per (8-row column block,
-        // token): the block's max |a| and sum; (3) one per (block, token): the
-        // group's (gs rows) max from its blocks, the block as int16 pairs in the
-        // dp2a layout (4 words, as for x), and per group the scale and exact sum.
+        // where items left partial sums, and the 8 lanes of a column block
+        // reduce its max |a| and sum; (2) one per (block, token): the group's
+        // (gs rows) max from its blocks, the block as int16 pairs in the dp2a
+        // layout (4 words, as for x), and per group the scale and fp32 sum.
         const int ncb_cta = (b - a) >> 3, arows = p.act_cb * 8;
-        if (nslg > 1) {
-            for (int i = tid; i < (b - a) * NT; i += kConsumerThreads) {
-                const int lr = i / NT, k = i % NT;
-                const int e = rs.ulist[fdiv(a + lr, p.fd_I)];
-                if (ctl.abort || !((rs.tmask[e] >> k) & 1u)) continue;
-                float gv = 0.f, uv = 0.f;
-                const float *gp = gup + (size_t)lr * nslg * (2 * NT) + 2 * k;
-                for (int jj = 0; jj < nslg; ++jj) {
-                    gv += gp[jj * 2 * NT];
-                    uv += gp[jj * 2 * NT + 1];
+        {
+            // passes 1 and 2 together: thread (token k, row lr), rows inner, so
+            // the 8 rows of a column block are 8 consecutive lanes and the
+            // block's max |a| and sum come from shuffles
+            const int nrows = b - a, total = nrows * NT;
+            for (int base = warp * 32; base < total; base += kConsumerThreads) {
+                const int i = base + lane, k = i / max(nrows, 1), lr = i - k * nrows;
+                float v = 0.f;
+                if (i < total) {
+                    float *af = actf + (size_t)k * arows + lr;
+                    if (nslg > 1) {
+                        const int e = rs.ulist[fdiv(a + lr, p.fd_I)];
+                        if (!ctl.abort && ((rs.tmask[e] >> k) & 1u)) {
+                            float gv = 0.f, uv = 0.f;
+                            const float *gp = gup + (size_t)lr * nslg * (2 * NT) + 2 * k;
+                            for (int jj = 0; jj < nslg; ++jj) {
+                                gv += gp[jj * 2 * NT];
+                                uv += gp[jj * 2 * NT + 1];
+                            }
+                            v = swiglu(gv, uv);
+                            *af = v;
+                        }
+                    } else {
+                        v = *af;
+                    }
                 }
-                actf[(size_t)k * arows + lr] = swiglu(gv, uv);
-            }
-            named_sync(1, kConsumerThreads);
-        }
-        for (int i = tid; i < ncb_cta * NT; i += kConsumerThreads) {
-            const int cb = i / NT, k = i % NT;
-            const float *f = actf + (size_t)k * arows + 8 * cb;
-            float m = 0.f, s0 = 0.f, s1 = 0.f;
+                float m = fabsf(v), sm = v;
 #pragma unroll
-            for (int jr = 0; jr < 8; jr += 2) {
-                m = fmaxf(m, fmaxf(fabsf(f[jr]), fabsf(f[jr + 1])));
-                s0 += f[jr];
-                s1 += f[jr + 1];
+                for (int o = 1; o < 8; o <<= 1) {
+                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                }
+                if (i < total && (lane & 7) == 0) {
+                    const int bi = (lr >> 3) * NT + k;
+                    bst[2 * bi] = m;
+                    bst[2 * bi + 1] = sm;
+                }
             }
-            bst[2 * i] = m;
-            bst[2 * i + 1] = s0 + s1;
         }
         named_sync(1, kConsumerThreads);
         for (int i = tid; i < ncb_cta * NT; i += kConsumerThreads) {

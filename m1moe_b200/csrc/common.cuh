@@ -314,6 +314,34 @@ __device__ __forceinline__ int dot_chunk_i16(const uint4 w, const uint32_t (&xq)
     return a0 + a1;
 }
 
+// The chunk's nibble planes, for reuse by several token vectors: lo[i] holds
+// nibbles 0,2,4,6 of word i as bytes; hi[i] nibbles 1,3,5,7 left in the high
+// half of each byte (16*q: one AND instead of a shift and an AND).
+__device__ __forceinline__ void split_nibbles(const uint4 w, uint32_t (&lo)[4], uint32_t (&hi)[4]) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        lo[i] = ws[i] & 0x0F0F0F0Fu;
+        hi[i] = ws[i] & 0xF0F0F0F0u;
+    }
+}
+
+// dot_chunk_i16 on split planes: the low nibbles and the high ones (times
+// 16) in two chains; Q = lo + hi/16, exact (hi is a multiple of 16 and
+// |hi| <= 16 * 16 * 15 * 32767 < 2^31).
+__device__ __forceinline__ int dot_split_i16(const uint32_t (&lo)[4], const uint32_t (&hi)[4],
+                                             const uint32_t (&xq)[16]) {
+    int a0 = 0, a1 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        a0 = dp2a_lo(xq[4 * i + 0], lo[i], a0);
+        a0 = dp2a_hi(xq[4 * i + 1], lo[i], a0);
+        a1 = dp2a_lo(xq[4 * i + 2], hi[i], a1);
+        a1 = dp2a_hi(xq[4 * i + 3], hi[i], a1);
+    }
+    return a0 + (a1 >> 4);
+}
+
 // Quantise one 32-value chunk (v) into its 16 words (strided by nch*4 words
 // per i), returning the scale; *sum receives the exact fp32 sum.
 __device__ __forceinline__ float quant_chunk_i16(const float (&v)[32], uint32_t *xq, int nch, int c,

@@ -153,6 +153,11 @@ cudaError_t launch_matvec_nt(const m1::MatvecParams &p, int num_sms, cudaStream_
 }
 
 constexpr size_t kStageTarget = 40 * 1024;  // bulk copies this large run at HBM speed
+#ifndef M1_SLOT_TILE_BYTES
+#define M1_SLOT_TILE_BYTES (40 * 1024)
+#endif
+// gate/up tiles of the slot path: smaller tiles keep more of them in flight
+constexpr long long kSlotTileBytes = M1_SLOT_TILE_BYTES;
 static_assert(m1::kLayerSlots <= m1::kMaxStages, "slot arrays are kMaxStages long");
 constexpr size_t kStagingBytes = 256u << 20;  // device staging for cold-start repacking
 
@@ -167,8 +172,9 @@ struct m1moe_cuda_ctx {
     uint8_t *table = nullptr;     // [layers][ne] tiled blocks
     uint16_t *router = nullptr;   // [layers][E][h]
     std::vector<uint8_t> layer_loaded, router_loaded;
-    unsigned long long *xlog = nullptr;  // [nbox][max_batch][E] tagged logits, a box per CTA
+    unsigned long long *xlog = nullptr;  // [nbox][box_words] tagged partial logits, a box per CTA
     int nbox = 0;                        // = the layer kernel's grid
+    int box_words = 0;                   // logit_box_words(nbox, E, h)
     float *acc = nullptr;                // [max_batch][h] fp32 sums for bf16 output
     int *done = nullptr;                 // CTAs finished with their atomics (bf16 output)
     unsigned *epochs = nullptr;          // per-CTA call counters (moe_layer.cuh)
@@ -246,13 +252,31 @@ void free_ctx(m1moe_cuda_ctx *c) {
 
 constexpr size_t kEpochBytes = (size_t)m1::kMaxCtas * m1::kEpochStride * sizeof(unsigned);
 
+// Partial sums per router logit: h is cut into `parts` column ranges, each
+// summed by its own CTA, so that up to E*parts CTAs share the router product
+// instead of E.  At least 256 (token, 8-column block) pairs per part, at most
+// 16 parts, and the box (ntok*E*parts tagged words) within
+// kMaxTok*kMaxExperts words.
+int logit_parts(int grid, int E, int ntok, int h) {
+    int P = std::min(std::max(1, grid / E), 16);
+    P = std::min(P, std::max(1, ntok * h / 2048));
+    while (P > 1 && ntok * E * P > m1::kMaxTok * m1::kMaxExperts) --P;
+    return P;
+}
+
+// Words of one logit box: the largest ntok*E*parts of any batch.
+int logit_box_words(int grid, int E, int h) {
+    int w = 0;
+    for (int b = 1; b <= m1::kMaxTok; ++b) w = std::max(w, b * E * logit_parts(grid, E, b, h));
+    return w;
+}
+
 // Zero the epoch words and the tagged logits (tag 0 is never a call's tag,
 // so no stale word can match after this).
 cudaError_t clear_exchange(m1moe_cuda_ctx *c) {
-    const m1moe_cuda_cfg &g = c->cfg;
     cudaError_t e = cudaMemset(c->epochs, 0, kEpochBytes);
     if (e == cudaSuccess) e = cudaMemset(c->done, 0, 4);
-    if (e == cudaSuccess) e = cudaMemset(c->xlog, 0, (size_t)c->nbox * g.max_batch * g.num_experts * 8);
+    if (e == cudaSuccess) e = cudaMemset(c->xlog, 0, (size_t)c->nbox * c->box_words * 8);
     return e;
 }
 
@@ -273,7 +297,8 @@ m1::LayerParams layer_params(m1moe_cuda_ctx *c, int layer, int B) {
     p.ntok = B;
     p.xlog = c->xlog;
     p.nbox = c->nbox;
-    p.box_words = g.max_batch * g.num_experts;
+    p.box_words = c->box_words;
+    p.lparts = logit_parts(c->nbox, g.num_experts, B, g.hidden_dim);
     p.acc = c->acc;
     p.done = c->done;
     p.epochs = c->epochs;
@@ -293,7 +318,7 @@ int divisor_tile(int n, int m, long long cap) {
 
 // Plan tiles, stages and the shared-memory map of k_moe_layer<nt>.  Returns
 // the dynamic shared memory size, or 0 if the shape does not fit an SM.
-size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
+size_t plan_layer(m1::LayerParams &p, int grid, int nt) {
     const m1::TiledLayout &tl = p.tl;
     const int nch = p.h / m1::kChunkCols;
     const int maxU = std::min(p.ntok * p.K, p.ne);
@@ -307,7 +332,10 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     // gate/up tile: GT pair-rows, GT | I and 8 | GT (row pairs R, R+4 stay in
     // one tile), filling the stage the down tiles need (at least kStageTarget/2)
     const long long stage_target = std::max<long long>(dn_bytes, kStageTarget / 2);
-    p.gu_tile_rows = divisor_tile(p.I, 8, std::max<long long>(8, stage_target / tl.pr));
+    // (the slot path has no row pairs: any multiple of 4 rows)
+    const int gmul = m1::slot_path(nt) ? 4 : 8;
+    const long long gu_target = m1::slot_path(nt) ? std::min<long long>(stage_target, kSlotTileBytes) : stage_target;
+    p.gu_tile_rows = divisor_tile(p.I, gmul, std::max<long long>(gmul, gu_target / tl.pr));
     p.stage_bytes = (int)m1::round_up_ll(std::max<long long>(p.gu_tile_rows * tl.pr, dn_bytes), 128);
     p.gu_nslices = nt <= 2 ? (nch + 31) / 32 : 1;
     p.nic = p.h / tl.rc;
@@ -317,12 +345,25 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     p.fd_ncbE = m1::make_fastdiv(p.I / 8);
     p.fd_gcb = m1::make_fastdiv(gcb);
     p.fd_gs = m1::make_fastdiv(p.gs);
-    p.fd_iptg = m1::make_fastdiv((p.gu_tile_rows / 2 / pg) * p.gu_nslices);
+    p.fd_iptg = m1::make_fastdiv(m1::gu_items_per_tile(nt, p.gu_tile_rows, p.gu_nslices));
     p.fd_nslg = m1::make_fastdiv(p.gu_nslices);
     if (tl.rc % (32 * m1::dn_lane_rows(nt))) return 0;
     p.fd_iptd = m1::make_fastdiv(tl.rc / (32 * m1::dn_lane_rows(nt)));
-    const long long units = (long long)maxU * (p.I / 8);
-    p.gu_rows_max = (int)((units + grid - 1) / grid) * 8;
+    // rows per CTA: an even split, or the cost-weighted one (route_geometry):
+    // a CTA's cost share is at most ceil(total / grid) and a unit costs at
+    // least beta + 1, so it gets at most share / (beta + 1) + 1 units
+    const long long n8 = p.I / 8;
+    p.bal_beta = p.ntok > 1 ? m1::kBalBeta : 0;
+    if (p.bal_beta == 0) {
+        const long long units = (long long)maxU * n8;
+        p.gu_rows_max = (int)((units + grid - 1) / grid) * 8;
+    } else {
+        const long long pairs = (long long)p.ntok * std::min(p.K, p.ne);
+        const long long total = n8 * (p.bal_beta * (long long)maxU + pairs);
+        if (total * grid >= (1LL << 31)) return 0;  // route_geometry's int costs
+        const long long share = (total + grid - 1) / grid;
+        p.gu_rows_max = (int)std::min<long long>(share / (p.bal_beta + 1) + 2, maxU * n8) * 8;
+    }
     p.act_cb = p.gu_rows_max / 8;
     p.xseg_max = p.gu_rows_max / p.gs + 2;
     // fixed part of the shared-memory map (after the ring and its barriers)
@@ -337,9 +378,13 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
     const size_t xsum = take((size_t)nt * nch * 8);
     const size_t gup = take(p.gu_nslices > 1 ? (size_t)p.gu_rows_max * p.gu_nslices * 2 * nt * 4 : 16);
     const size_t actf = take((size_t)nt * p.act_cb * 8 * 4);
-    const size_t act = take((size_t)nt * p.act_cb * 16);
+    // the int16 activations and block statistics are written once gate/up is
+    // done; the slot path places them over the staged x, which is dead then
+    const size_t act_bytes = align16((size_t)nt * p.act_cb * 16), blk_bytes = (size_t)nt * p.act_cb * 8;
+    const bool alias_x = m1::slot_path(nt) && act_bytes + blk_bytes <= (size_t)nt * p.h * 2;
+    const size_t act = alias_x ? xs : take(act_bytes);
     const size_t xseg = take((size_t)nt * p.xseg_max * 8);
-    const size_t blk = take((size_t)nt * p.act_cb * 8);
+    const size_t blk = alias_x ? xs + act_bytes : take(blk_bytes);
     const size_t keys = take((size_t)nt * p.E * 8);
     const size_t rlog = take((size_t)nt * p.E * 4);
     const size_t lpart = take(8 * m1::kMaxTok * 4);
@@ -370,7 +415,7 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, int pg) {
 template <int NT>
 m1moe_status launch_layer(m1moe_cuda_ctx *c, m1::LayerParams p, cudaStream_t st) {
     const int grid = c->nbox;  // one CTA per SM, each with its own logit box
-    const size_t smem = plan_layer(p, grid, NT, m1::ItemRows<NT>::pairs);
+    const size_t smem = plan_layer(p, grid, NT);
     if (smem == 0 || smem > kMaxDynSmem)
         return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
     M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -451,7 +496,7 @@ m1moe_status noalloc_setup(int dev, NoAllocDevice *&out) {
 
 template <int NT>
 m1moe_status launch_route_noalloc(m1::LayerParams p, int grid, cudaStream_t st) {
-    const size_t smem = plan_layer(p, grid, NT, m1::ItemRows<NT>::pairs);
+    const size_t smem = plan_layer(p, grid, NT);
     if (smem == 0 || smem > kMaxDynSmem)
         return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
     M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -651,6 +696,7 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     c->router_loaded.assign(g.num_layers, 0);
     c->num_sms = sm_count();
     c->nbox = std::min(c->num_sms, m1::kMaxCtas);
+    c->box_words = logit_box_words(c->nbox, g.num_experts, g.hidden_dim);
     const size_t B = g.max_batch, E = g.num_experts, K = g.top_k;
     cudaError_t e;
 #define M1_ALLOC(ptr, bytes)                                        \
@@ -662,7 +708,7 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     }
     M1_ALLOC(c->table, (size_t)g.num_layers * ne * c->tl.block);
     M1_ALLOC(c->router, (size_t)g.num_layers * E * g.hidden_dim * 2);
-    M1_ALLOC(c->xlog, (size_t)c->nbox * B * E * 8);
+    M1_ALLOC(c->xlog, (size_t)c->nbox * c->box_words * 8);
     M1_ALLOC(c->acc, B * g.hidden_dim * 4);
     M1_ALLOC(c->done, 4);
     M1_ALLOC(c->epochs, kEpochBytes);
@@ -921,6 +967,7 @@ m1moe_status m1moe_cuda_router_topk_noalloc(const uint16_t *d_router, int32_t nu
     p.xlog = reinterpret_cast<unsigned long long *>(nd->scratch);
     p.nbox = 1;  // one shared box: the fixed scratch has no room for a box per CTA
     p.box_words = 0;
+    p.lparts = logit_parts(std::min(nd->num_sms, kNoAllocMaxCtas), E, B, h);
     p.epochs = reinterpret_cast<unsigned *>(nd->scratch + kNoAllocXlog);
     p.err = d_status ? d_status : reinterpret_cast<int *>(nd->scratch + kNoAllocXlog + kNoAllocEpochs);
     p.route_only = 1;

@@ -100,6 +100,28 @@ struct ItemRows {
     static constexpr int passes = gu >= 2 ? 1 : 2;              // NPASS
 };
 
+// Batches of 4 and 8 work in token SLOTS: slot j of distinct expert u is the
+// j-th token (ascending) routed to it, and the inner loops are instantiated
+// for the expert's token count, so no lane tests token bits or multiplies
+// for a token the expert does not see.  A gate/up item is then ONE row of a
+// tile for all of the expert's tokens; smaller batches keep the row-group
+// items above (with column slices for 1 and 2 tokens).
+__host__ __device__ constexpr bool slot_path(int nt) { return nt >= 4; }
+
+__host__ __device__ constexpr int gu_items_per_tile(int nt, int gt, int nslices) {
+    return slot_path(nt) ? gt
+                         : (gt / 2 / (nt == 1 ? 2 : 1)) * nslices;  // row groups x slices
+}
+
+// Relative cost of a unit of 8 gate/up rows of an expert with t tokens
+// (the same rows of the down matrices included): beta + t.  beta weighs the
+// bytes, which do not depend on t, against the per-token arithmetic; the
+// rows are split so that every CTA gets the same total cost.
+#ifndef M1_BAL_BETA
+#define M1_BAL_BETA 2
+#endif
+constexpr int kBalBeta = M1_BAL_BETA;
+
 // The routing decision of one call.
 struct RouteInfo {
     int idx[kMaxTok][kMaxTopK];    // top-K experts per token, descending
@@ -128,8 +150,9 @@ struct LayerParams {
     int out_acc;      // sums go to acc, the last CTA writes out (bf16, or f32 not 16-byte aligned)
     float *acc;       // [ntok][h] fp32 sums for bf16 output
     int *done;        // CTAs finished with their atomics (bf16 output)
-    unsigned long long *xlog;  // [nbox][box_words] tagged logits {tag, f32}, box = [ntok][E]
+    unsigned long long *xlog;  // [nbox][box_words] tagged logits {tag, f32}, box = [ntok][E][lparts]
     int nbox, box_words;       // logit boxes (CTA c reads box c % nbox) and their stride
+    int lparts;                // partial sums per logit (h cut into lparts column ranges)
     unsigned *epochs;          // [kMaxCtas * kEpochStride] per-CTA call counters
     int *user_idx;    // optional [ntok][K]
     float *user_w;    // optional [ntok][K]
@@ -149,6 +172,7 @@ struct LayerParams {
     int act_cb;       // activation capacity, column blocks per token (gu_rows_max / 8)
     int xseg_max;     // activation groups per token (scale and sum)
     int route_only;   // stop after routing (m1moe_cuda_router_topk)
+    int bal_beta;     // 0: rows split evenly; else cost-weighted split (kBalBeta)
     int nic;          // row chunks of the down matrices (h / tl.rc)
     // divisors known on the host: grid, gate/up tile rows, I, column blocks
     // per expert and per group, group size, items per gate/up tile, column
@@ -192,6 +216,8 @@ struct Ctl {
     int vstart[kMaxStages];      // producer: running byte position of each slot's tile
     StageGeo geo[kMaxStages];
     TileCopy copy[32];           // producer: the next (up to) 32 tiles' copies
+    unsigned char ute[kMaxPairs];            // tokens of distinct expert u
+    unsigned char utok[kMaxPairs][kMaxTok];  // its token slots: j-th token, ascending
 };
 
 __device__ __forceinline__ bool is_local(const LayerParams &p, int e) {
@@ -302,10 +328,11 @@ __device__ __forceinline__ unsigned long long logit_key(float v, int e) {
 }
 
 __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
-                          unsigned long long *keys, unsigned tag, const volatile int *abort) {
+                          unsigned long long *keys, float *parts, unsigned tag, const volatile int *abort) {
     const int tid = threadIdx.x;
-    const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E;
-    // a. collect the tagged logits (all of this thread's loads in flight at once)
+    const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E, LP = p.lparts, nw = nel * LP;
+    // a. collect the tagged partial logits (all of this thread's loads in
+    //    flight at once; nw <= kMaxTok * kMaxExperts)
     constexpr int kPer = kMaxTok * kMaxExperts / 256;
     const unsigned long long *box = p.xlog + (size_t)(blockIdx.x % p.nbox) * p.box_words;
     bool ok = false;
@@ -315,11 +342,11 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
             const int i = tid + 256 * j;
-            if (i < nel) w[j] = ld_relaxed_u64(box + i);
+            if (i < nw) w[j] = ld_relaxed_u64(box + i);
         }
 #pragma unroll
         for (int j = 0; j < kPer; ++j)
-            if (tid + 256 * j < nel) all = all && (unsigned)(w[j] >> 32) == tag;
+            if (tid + 256 * j < nw) all = all && (unsigned)(w[j] >> 32) == tag;
         if (all) {
             ok = true;
             break;
@@ -328,18 +355,26 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
         __nanosleep(nap);
         nap = min(nap * 2, 256u);
     }
+    // b. the logit of (token, expert) element i: its parts summed in order
+    auto put = [&](int i, float v) {
+        int e = i;
+        while (e >= E) e -= E;
+        rlog[i] = v;
+        keys[i] = logit_key(v, e);
+    };
+    if (LP == 1) {
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-        const int i = tid + 256 * j;
-        if (i < nel) {
-            int t = 0, e = i;
-            while (e >= E) {
-                e -= E;
-                ++t;
-            }
-            const float v = __uint_as_float((uint32_t)w[j]);
-            rlog[i] = v;
-            keys[i] = logit_key(v, e);
+        for (int j = 0; j < kPer; ++j)
+            if (tid + 256 * j < nel) put(tid + 256 * j, __uint_as_float((uint32_t)w[j]));
+    } else {
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+            if (tid + 256 * j < nw) parts[tid + 256 * j] = __uint_as_float((uint32_t)w[j]);
+        named_sync(2, 256);
+        for (int i = tid; i < nel; i += 256) {
+            float v = 0.f;
+            for (int q = 0; q < LP; ++q) v += parts[i * LP + q];
+            put(i, v);
         }
     }
     if (!named_sync_and(2, 256, ok)) return false;
@@ -545,10 +580,70 @@ __device__ void route_geometry(const LayerParams &p, Ctl &ctl, int blk) {
         m &= m - 1;
     }
     const int nU = __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();  // ulist complete
+    // token slots of every distinct expert
+    for (int u = lane; u < nU; u += 32) {
+        unsigned tm = rs.tmask[rs.ulist[u]];
+        int j = 0;
+        while (tm) {
+            ctl.utok[u][j++] = (unsigned char)(__ffs(tm) - 1);
+            tm &= tm - 1;
+        }
+        ctl.ute[u] = (unsigned char)j;
+    }
+    const int n8 = p.I >> 3;  // units of 8 rows per expert
+    int ua = 0, ub = 0;       // this CTA's units [ua, ub)
+    if (p.bal_beta == 0) {
+        const int units = nU * n8;  // units * G < 2^31 (kMaxPairs, I, kMaxCtas)
+        ua = fdiv(units * blk, p.fd_G);
+        ub = fdiv(units * (blk + 1), p.fd_G);
+    } else {
+        // cost-weighted: unit i of expert u costs c_u = beta + t_u; lane l
+        // holds experts 4l..4l+3 (nU <= kMaxPairs = 128).  The boundary for a
+        // cost target T is the first unit whose preceding cost reaches T, so
+        // neighbouring CTAs agree on it.
+        int cu[4], cs = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int u = 4 * lane + i;
+            cu[i] = u < nU ? p.bal_beta + __popc(rs.tmask[rs.ulist[u]]) : 0;
+            cs += cu[i];
+        }
+        int ci = cs;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, ci, o);
+            if (lane >= o) ci += y;
+        }
+        // costs are ints: total * G < 2^31 (checked on the host)
+        const int pre = (ci - cs) * n8;  // cost before this lane's experts
+        const int total = __shfl_sync(0xffffffffu, ci, 31) * n8;
+        auto boundary = [&](int T) {
+            if (T >= total) return nU * n8;
+            const bool own = T >= pre && T < pre + cs * n8;
+            const unsigned who = __ballot_sync(0xffffffffu, own);
+            int unit = 0;
+            if (own) {
+                int c0 = pre;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int c1 = c0 + cu[i] * n8;
+                    if (T >= c0 && T < c1) unit = (4 * lane + i) * n8 + (T - c0 + cu[i] - 1) / cu[i];
+                    c0 = c1;
+                }
+            }
+            return __shfl_sync(0xffffffffu, unit, __ffs(who) - 1);
+        };
+        ua = boundary(fdiv(total * blk, p.fd_G));
+        ub = boundary(fdiv(total * (blk + 1), p.fd_G));
+    }
     if (lane == 0) {
         rs.nU = nU;
-        const int units = nU * (p.I >> 3);  // units * G < 2^31 (kMaxPairs, I, kMaxCtas)
-        const int a = fdiv(units * blk, p.fd_G) * 8, b = fdiv(units * (blk + 1), p.fd_G) * 8;
+        int a = ua * 8, b = ub * 8;
+        if (b - a > p.gu_rows_max) {  // cannot happen (host bound); never overrun the buffers
+            set_abort(ctl, p.err);
+            b = a;
+        }
         ctl.a = a;
         ctl.b = b;
         ctl.ntg = (b > a) ? fdiv(b - 1, p.fd_GT) - fdiv(a, p.fd_GT) + 1 : 0;
@@ -694,6 +789,168 @@ __device__ __forceinline__ float swiglu(float g, float u) {
     return (g / (1.0f + expf(-g))) * u;  // Shaders.metal:147-148: SiLU(gate) * up
 }
 
+// ------------------------------------------------------------ slot path ----
+// One gate/up row (pair-row pr in the ring) for the TE token slots of its
+// expert: lane = chunk of 32 columns; the chunk's weights are split into
+// nibble planes once and shared by the tokens; per chunk and token
+// acc += s*sx*Q + b*X for gate and up (common.cuh).  The SwiGLU activation
+// of slot j lands in actf[j][lr].
+template <int TE>
+__device__ __forceinline__ void gu_row_te(const LayerParams &p, const uint8_t *pr, const unsigned char *tk,
+                                          const uint32_t *xq, const float *xsc, const float *xsum,
+                                          float *actf, int arows, int lr) {
+    const int lane = threadIdx.x & 31, h = p.h, nch = h / kChunkCols;
+    const size_t wo_u = (size_t)h / 2 + 2 * p.tl.sbh;  // up part of the pair-row
+    const uint16_t *sgp = reinterpret_cast<const uint16_t *>(pr + h / 2);
+    const uint16_t *sup = reinterpret_cast<const uint16_t *>(pr + wo_u + h / 2);
+    const int bo = p.tl.sbh / 2;  // biases follow the scales
+    int tok[TE];
+#pragma unroll
+    for (int j = 0; j < TE; ++j) tok[j] = tk[j];
+    constexpr int NV = TE <= 1 ? 2 : (TE <= 2 ? 4 : (TE <= 4 ? 8 : 16));
+    float acc[NV];  // [2*slot + gate0/up1], zero-padded to a power of two
+#pragma unroll
+    for (int i = 0; i < NV; ++i) acc[i] = 0.f;
+    for (int ch = lane; ch < nch; ch += 32) {
+        const int gi = fdiv(ch * kChunkCols, p.fd_gs);
+        const uint4 wg = *reinterpret_cast<const uint4 *>(pr + ch * 16);
+        const uint4 wu = *reinterpret_cast<const uint4 *>(pr + wo_u + ch * 16);
+        const float sg = bf16_bits(sgp[gi]), bg = bf16_bits(sgp[bo + gi]);
+        const float su = bf16_bits(sup[gi]), bu = bf16_bits(sup[bo + gi]);
+        // up to 4 slots the split planes stay in registers across the slots;
+        // beyond, registers go to the accumulators and the planes are split
+        // again per slot
+        uint32_t glo[4], ghi[4], ulo[4], uhi[4];
+        if constexpr (TE <= 4) {
+            split_nibbles(wg, glo, ghi);
+            split_nibbles(wu, ulo, uhi);
+        }
+#pragma unroll
+        for (int j = 0; j < TE; ++j) {
+            uint32_t xp[16];
+            load_pairs_any(reinterpret_cast<const uint16_t *>(xq + (size_t)tok[j] * (h / 2)), nch, ch, xp);
+            const float X = xsum[tok[j] * nch + ch], sx = xsc[tok[j] * nch + ch];
+            int Qg, Qu;
+            if constexpr (TE <= 4) {
+                Qg = dot_split_i16(glo, ghi, xp);
+                Qu = dot_split_i16(ulo, uhi, xp);
+            } else {
+                Qg = dot_chunk_i16(wg, xp);
+                Qu = dot_chunk_i16(wu, xp);
+            }
+            acc[2 * j] = fmaf(sg * sx, (float)Qg, fmaf(bg, X, acc[2 * j]));
+            acc[2 * j + 1] = fmaf(su * sx, (float)Qu, fmaf(bu, X, acc[2 * j + 1]));
+        }
+    }
+    // lane l holds value l / kS; the up value sits kS lanes above its gate
+    const float tot = warp_reduce_multi(acc);
+    constexpr int kS = 32 / NV;
+    const float upv = __shfl_down_sync(0xffffffffu, tot, kS);
+    const int j = lane / (2 * kS);
+    if ((lane % (2 * kS)) == 0 && j < TE) actf[(size_t)j * arows + lr] = swiglu(tot, upv);
+}
+
+template <int NT>
+__device__ __forceinline__ void gu_row_slots(int te, const LayerParams &p, const uint8_t *pr,
+                                             const unsigned char *tk, const uint32_t *xq, const float *xsc,
+                                             const float *xsum, float *actf, int arows, int lr) {
+    switch (te) {
+    case 1: gu_row_te<1>(p, pr, tk, xq, xsc, xsum, actf, arows, lr); break;
+    case 2: gu_row_te<2>(p, pr, tk, xq, xsc, xsum, actf, arows, lr); break;
+    case 3: gu_row_te<3>(p, pr, tk, xq, xsc, xsum, actf, arows, lr); break;
+    case 4: gu_row_te<4>(p, pr, tk, xq, xsc, xsum, actf, arows, lr); break;
+    default:
+        if constexpr (NT > 4) {
+            switch (te) {
+            case 5: gu_row_te<5>(p, pr, tk, xq, xsc, xsum, actf, arows, lr); break;
+            case 6: gu_row_te<6>(p, pr, tk, xq, xsc, xsum, actf, arows, lr); break;
+            case 7: gu_row_te<7>(p, pr, tk, xq, xsc, xsum, actf, arows, lr); break;
+            default: gu_row_te<8>(p, pr, tk, xq, xsc, xsum, actf, arows, lr); break;
+            }
+        }
+    }
+}
+
+// One down tile (column blocks [r0, r0+nr) of one expert, this lane's LR rows
+// of the row chunk) for the TE slots: per column block the LR weight words
+// are split once and shared by the slots, whose activation blocks (int16
+// pairs, slot-major) feed two dp2a chains each; per group
+// y += s*sa*Q + b*X (common.cuh).
+template <int TE, int LR, int NT>
+__device__ __forceinline__ void dn_tile_te(const LayerParams &p, float (&y)[LR][NT], const uint32_t *Wt,
+                                           const uint32_t *SBt, const StageGeo &g, const uint32_t *act,
+                                           const float *xseg, int a8, int ag) {
+    const int RC = p.tl.rc, gcb = p.gs >> 3;
+    const int gfirst = fdiv(g.r0, p.fd_gcb);
+    const uint4 *av = reinterpret_cast<const uint4 *>(act) + (g.r0 - a8);
+    int Qa[LR][TE], Qb[LR][TE];
+#pragma unroll
+    for (int r = 0; r < LR; ++r)
+#pragma unroll
+        for (int j = 0; j < TE; ++j) Qa[r][j] = Qb[r][j] = 0;
+    int gcur = gfirst, c = 0;
+    int left = gcb - (g.r0 - gfirst * gcb);  // blocks of the first group in this tile
+    while (c < g.nr) {
+        const int cend = min(g.nr, c + left);
+#pragma unroll 2
+        for (; c < cend; ++c) {
+            uint32_t wd[LR];
+            load_words<LR>(Wt + (size_t)c * RC, wd);
+            uint32_t lo[LR], hi[LR];
+#pragma unroll
+            for (int r = 0; r < LR; ++r) {
+                lo[r] = wd[r] & 0x0F0F0F0Fu;
+                hi[r] = wd[r] & 0xF0F0F0F0u;  // 16 * q: Qb is 16 times its sum
+            }
+#pragma unroll
+            for (int j = 0; j < TE; ++j) {
+                const uint4 v = av[c + (size_t)j * p.act_cb];
+#pragma unroll
+                for (int r = 0; r < LR; ++r) {
+                    Qa[r][j] = dp2a_hi(v.y, lo[r], dp2a_lo(v.x, lo[r], Qa[r][j]));
+                    Qb[r][j] = dp2a_hi(v.w, hi[r], dp2a_lo(v.z, hi[r], Qb[r][j]));
+                }
+            }
+        }
+        // the group ends here (or the tile does): fold its scale and bias
+        uint32_t sb[LR];
+        load_words<LR>(SBt + (size_t)(gcur - gfirst) * RC, sb);
+        const float *xg = xseg + (size_t)(gcur - ag) * NT * 2;
+#pragma unroll
+        for (int r = 0; r < LR; ++r) {
+            const float sc = bf16_bits(sb[r] & 0xFFFFu), bi = bf16_bits(sb[r] >> 16);
+#pragma unroll
+            for (int j = 0; j < TE; ++j) {
+                y[r][j] = fmaf(sc * xg[2 * j + 1], (float)(Qa[r][j] + (Qb[r][j] >> 4)), fmaf(bi, xg[2 * j], y[r][j]));
+                Qa[r][j] = Qb[r][j] = 0;
+            }
+        }
+        ++gcur;
+        left = gcb;
+    }
+}
+
+template <int LR, int NT>
+__device__ __forceinline__ void dn_tile_slots(int te, const LayerParams &p, float (&y)[LR][NT],
+                                              const uint32_t *Wt, const uint32_t *SBt, const StageGeo &g,
+                                              const uint32_t *act, const float *xseg, int a8, int ag) {
+    switch (te) {
+    case 1: dn_tile_te<1, LR, NT>(p, y, Wt, SBt, g, act, xseg, a8, ag); break;
+    case 2: dn_tile_te<2, LR, NT>(p, y, Wt, SBt, g, act, xseg, a8, ag); break;
+    case 3: dn_tile_te<3, LR, NT>(p, y, Wt, SBt, g, act, xseg, a8, ag); break;
+    case 4: dn_tile_te<4, LR, NT>(p, y, Wt, SBt, g, act, xseg, a8, ag); break;
+    default:
+        if constexpr (NT > 4) {
+            switch (te) {
+            case 5: dn_tile_te<5, LR, NT>(p, y, Wt, SBt, g, act, xseg, a8, ag); break;
+            case 6: dn_tile_te<6, LR, NT>(p, y, Wt, SBt, g, act, xseg, a8, ag); break;
+            case 7: dn_tile_te<7, LR, NT>(p, y, Wt, SBt, g, act, xseg, a8, ag); break;
+            default: dn_tile_te<8, LR, NT>(p, y, Wt, SBt, g, act, xseg, a8, ag); break;
+            }
+        }
+    }
+}
+
 // Activations of token t for rows R and R+4 (concatenated row space), fp32,
 // at row - a of this CTA's range.
 __device__ __forceinline__ void put_act(float *actf, int act_rows, int a, int t, int R, float lo,
@@ -802,55 +1059,53 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     }
     const int nrows = i1 - i0;
     if (warp < 8) {
-        // ---- phase 2: logits of this CTA's experts, straight from global memory ----
+        // ---- phase 2: partial logits, straight from global memory ----
+        // Work item (e, part): W_r[e] . x[t] over the part's 8-column blocks
+        // [n8*part/P, n8*(part+1)/P) for every token; a thread takes token
+        // tid % NT of blocks tid / NT, +256/NT, ...  Fixed order throughout:
+        // lanes of one token by xor shuffles, then the 8 warps in order.
         for (int e = tid; e < p.E; e += 256) rs.tmask[e] = 0u;
         if (tid < kMaxExperts / 32) rs.emask[tid] = 0u;
-        const int nmine = (p.E > blk) ? (p.E - blk + G - 1) / G : 0;
+        const int P = p.lparts, nitems = p.E * P, n8 = h / 8;
+        constexpr int LT = NT == 1 ? 0 : (NT == 2 ? 1 : (NT == 4 ? 2 : 3));
+        const int tt = tid & (NT - 1);
+        const int nmine = (nitems > blk) ? (nitems - blk + G - 1) / G : 0;
         for (int m = 0; m < nmine; ++m) {
-            const int e = blk + m * G;
+            const int item = blk + m * G, e = item / P, part = item - e * P;
+            const int g0 = n8 * part / P, g1 = n8 * (part + 1) / P;
             const uint4 *row = reinterpret_cast<const uint4 *>(p.router + (size_t)e * h);
-            float acc[NT];
+            float acc = 0.f;
+            if (tt < p.ntok) {
+                for (int g8 = g0 + (tid >> LT); g8 < g1; g8 += 256 >> LT) {
+                    const uint4 wv = __ldg(row + g8);
+                    float xv[8];
+                    if (Xbf16) {
+                        const uint4 r = *(reinterpret_cast<const uint4 *>(
+                            reinterpret_cast<const uint16_t *>(X) + (size_t)tt * h) + g8);
+                        const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-            for (int t = 0; t < NT; ++t) acc[t] = 0.f;
-            for (int g8 = tid; g8 < h / 8; g8 += 256) {
-                const uint4 wv = __ldg(row + g8);
-                const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-                float wf[8];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    wf[2 * j] = __uint_as_float(ww[j] << 16);
-                    wf[2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
-                }
-#pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    if (t < p.ntok) {
-                        float xv[8];
-                        if (Xbf16) {
-                            const uint4 r = *(reinterpret_cast<const uint4 *>(
-                                reinterpret_cast<const uint16_t *>(X) + (size_t)t * h) + g8);
-                            const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                xv[2 * j] = __uint_as_float(rr[j] << 16);
-                                xv[2 * j + 1] = __uint_as_float(rr[j] & 0xFFFF0000u);
-                            }
-                        } else {
-                            const float4 *xf = reinterpret_cast<const float4 *>(
-                                reinterpret_cast<const float *>(X) + (size_t)t * h) + 2 * g8;
-                            const float4 a0 = __ldcg(xf), a1 = __ldcg(xf + 1);
-                            xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
-                            xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
+                        for (int j = 0; j < 4; ++j) {
+                            xv[2 * j] = __uint_as_float(rr[j] << 16);
+                            xv[2 * j + 1] = __uint_as_float(rr[j] & 0xFFFF0000u);
                         }
+                    } else {
+                        const float4 *xf = reinterpret_cast<const float4 *>(
+                            reinterpret_cast<const float *>(X) + (size_t)tt * h) + 2 * g8;
+                        const float4 a0 = __ldcg(xf), a1 = __ldcg(xf + 1);
+                        xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
+                        xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
+                    }
+                    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) acc[t] = fmaf(wf[j], xv[j], acc[t]);
+                    for (int j = 0; j < 4; ++j) {
+                        acc = fmaf(__uint_as_float(ww[j] << 16), xv[2 * j], acc);
+                        acc = fmaf(__uint_as_float(ww[j] & 0xFFFF0000u), xv[2 * j + 1], acc);
                     }
                 }
             }
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                const float v = warp_sum(acc[t]);
-                if (lane == 0) lpart[warp * kMaxTok + t] = v;
-            }
+            for (int o = NT; o < 32; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane < NT) lpart[warp * kMaxTok + lane] = acc;
             named_sync(2, 256);
             // publish into every CTA's box (each box is polled by its CTAs only)
             uint32_t sv[NT];
@@ -862,16 +1117,17 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 sv[t] = __float_as_uint(s);
             }
             for (int bx = tid; bx < p.nbox; bx += 256) {
-                unsigned long long *box = p.xlog + (size_t)bx * p.box_words + e;
+                unsigned long long *box = p.xlog + (size_t)bx * p.box_words + (size_t)e * P + part;
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
-                    if (t < p.ntok) st_relaxed_u64(box + (size_t)t * p.E, tagged(tag, sv[t]));
+                    if (t < p.ntok) st_relaxed_u64(box + (size_t)t * p.E * P, tagged(tag, sv[t]));
             }
             named_sync(2, 256);
         }
         if (tid == 0) trace_event(p.trace, 0, 2);
         // ---- phase 3: route (warps 0..7 of every CTA) ----
-        const bool ok = route_cta(p, rs, rlog, keys, tag, vabort);
+        // partial logits are summed in the tile ring, idle until routing is done
+        const bool ok = route_cta(p, rs, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
         if (tid == 0) trace_event(p.trace, 0, 3);
         if (tid == 0) {
             if (ok) ctl.route_ok = 1;
@@ -971,7 +1227,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     const int a = ctl.a, b = ctl.b, ntg = ctl.ntg, ntd = ctl.ntd;
     const int a8 = a >> 3, ag = fdiv(a, p.fd_gs), gcb = p.gs >> 3;
     const int nslg = p.gu_nslices;
-    const int ipt_g = (GT / 2 / PG) * nslg;  // work items per gate/up tile
+    const int ipt_g = gu_items_per_tile(NT, GT, nslg);  // work items per gate/up tile
     const int ipt_d = RC / (32 * DnRows<NT>::lane);  // work items per down tile
 
     if (warp == kConsumerWarps) {
@@ -984,92 +1240,109 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         }
     } else {
         // ================= consumers: gate/up =================
-        constexpr int kNg = 2 * RG * NT, kSg = 32 / kNg;
-        const size_t wo_u = (size_t)h / 2 + 2 * tl.sbh;  // up part offset in a pair-row
         const int ng_items = ntg * ipt_g;
-        for (;;) {
-            const int q = grab(&ctl.next_gu);
-            if (q >= ng_items) break;
-            const int n = fdiv(q, p.fd_iptg), rem = q - n * ipt_g, pg = fdiv(rem, p.fd_nslg),
-                      j = rem - pg * nslg;
-            const int s = n % NSL;
-            if (!wait_tile(full, ctl, s, n, NSL, p.err)) break;
-            if (q == 0 && lane == 0) trace_event(p.trace, 0, 5);
-            const StageGeo g = ctl.geo[s];
-            if (pg * PG < g.nr / 2) {
-                const uint8_t *st = ring + g.off;
-                const int e = rs.ulist[g.u];
-                const unsigned mask = rs.tmask[e];
-                float act_prev = 0.f;
-#pragma unroll
-                for (int pass = 0; pass < NPASS; ++pass) {
-                    // tile-relative rows of this pass
-                    int trow[RG];
-#pragma unroll
-                    for (int r = 0; r < RG; ++r) {
-                        const int pu = NPASS == 1 ? pg * PG + (r >> 1) : pg;
-                        const int half = NPASS == 1 ? (r & 1) : pass;
-                        trow[r] = 8 * (pu >> 2) + (pu & 3) + 4 * half;
-                    }
-                    float accg[kNg];  // [(row * NT + token) * 2 + gate0/up1]
-#pragma unroll
-                    for (int i = 0; i < kNg; ++i) accg[i] = 0.f;
-                    for (int ch = j * 32 + lane; ch < nch; ch += 32 * nslg) {
-                        const int gi = fdiv(ch * kChunkCols, p.fd_gs);
-#pragma unroll
-                        for (int k = 0; k < NT; ++k) {
-                            if (!((mask >> k) & 1u)) continue;
-                            uint32_t xp[16];
-                            load_pairs_any(reinterpret_cast<const uint16_t *>(xq + (size_t)k * (h / 2)), nch, ch, xp);
-                            const float X = xsum[k * nch + ch], sx = xsc[k * nch + ch];
-#pragma unroll
-                            for (int r = 0; r < RG; ++r) {
-                                const uint8_t *pr = st + (size_t)trow[r] * tl.pr;
-                                const uint4 wg = *reinterpret_cast<const uint4 *>(pr + ch * 16);
-                                const uint4 wu = *reinterpret_cast<const uint4 *>(pr + wo_u + ch * 16);
-                                const uint16_t *sgp = reinterpret_cast<const uint16_t *>(pr + h / 2);
-                                const uint16_t *sup = reinterpret_cast<const uint16_t *>(pr + wo_u + h / 2);
-                                const float sg = bf16_bits(sgp[gi]);
-                                const float bg = bf16_bits(sgp[tl.sbh / 2 + gi]);
-                                const float su = bf16_bits(sup[gi]);
-                                const float bu = bf16_bits(sup[tl.sbh / 2 + gi]);
-                                float &ag = accg[(r * NT + k) * 2 + 0];
-                                float &au = accg[(r * NT + k) * 2 + 1];
-                                // s*sx*Q + b*X per chunk (Q exact, common.cuh)
-                                ag = fmaf(sg * sx, (float)dot_chunk_i16(wg, xp), fmaf(bg, X, ag));
-                                au = fmaf(su * sx, (float)dot_chunk_i16(wu, xp), fmaf(bu, X, au));
+        if constexpr (slot_path(NT)) {
+            // item = one row of a tile, for all of its expert's token slots
+            for (;;) {
+                const int q = grab(&ctl.next_gu);
+                if (q >= ng_items) break;
+                const int n = fdiv(q, p.fd_iptg), rr = q - n * ipt_g;
+                const int s = n % NSL;
+                if (!wait_tile(full, ctl, s, n, NSL, p.err)) break;
+                if (q == 0 && lane == 0) trace_event(p.trace, 0, 5);
+                const StageGeo g = ctl.geo[s];
+                if (rr < g.nr)
+                    gu_row_slots<NT>(ctl.ute[g.u], p, ring + g.off + (size_t)rr * tl.pr, ctl.utok[g.u], xq, xsc,
+                                     xsum, actf, p.act_cb * 8, g.u * I + g.r0 + rr - a);
+                release_item(empty, ctl, s, ipt_g);
+            }
+        } else {
+            constexpr int kNg = 2 * RG * NT, kSg = 32 / kNg;
+            const size_t wo_u = (size_t)h / 2 + 2 * tl.sbh;  // up part offset in a pair-row
+            for (;;) {
+                const int q = grab(&ctl.next_gu);
+                if (q >= ng_items) break;
+                const int n = fdiv(q, p.fd_iptg), rem = q - n * ipt_g, pg = fdiv(rem, p.fd_nslg),
+                          j = rem - pg * nslg;
+                const int s = n % NSL;
+                if (!wait_tile(full, ctl, s, n, NSL, p.err)) break;
+                if (q == 0 && lane == 0) trace_event(p.trace, 0, 5);
+                const StageGeo g = ctl.geo[s];
+                if (pg * PG < g.nr / 2) {
+                    const uint8_t *st = ring + g.off;
+                    const int e = rs.ulist[g.u];
+                    const unsigned mask = rs.tmask[e];
+                    float act_prev = 0.f;
+    #pragma unroll
+                    for (int pass = 0; pass < NPASS; ++pass) {
+                        // tile-relative rows of this pass
+                        int trow[RG];
+    #pragma unroll
+                        for (int r = 0; r < RG; ++r) {
+                            const int pu = NPASS == 1 ? pg * PG + (r >> 1) : pg;
+                            const int half = NPASS == 1 ? (r & 1) : pass;
+                            trow[r] = 8 * (pu >> 2) + (pu & 3) + 4 * half;
+                        }
+                        float accg[kNg];  // [(row * NT + token) * 2 + gate0/up1]
+    #pragma unroll
+                        for (int i = 0; i < kNg; ++i) accg[i] = 0.f;
+                        for (int ch = j * 32 + lane; ch < nch; ch += 32 * nslg) {
+                            const int gi = fdiv(ch * kChunkCols, p.fd_gs);
+    #pragma unroll
+                            for (int k = 0; k < NT; ++k) {
+                                if (!((mask >> k) & 1u)) continue;
+                                uint32_t xp[16];
+                                load_pairs_any(reinterpret_cast<const uint16_t *>(xq + (size_t)k * (h / 2)), nch, ch, xp);
+                                const float X = xsum[k * nch + ch], sx = xsc[k * nch + ch];
+    #pragma unroll
+                                for (int r = 0; r < RG; ++r) {
+                                    const uint8_t *pr = st + (size_t)trow[r] * tl.pr;
+                                    const uint4 wg = *reinterpret_cast<const uint4 *>(pr + ch * 16);
+                                    const uint4 wu = *reinterpret_cast<const uint4 *>(pr + wo_u + ch * 16);
+                                    const uint16_t *sgp = reinterpret_cast<const uint16_t *>(pr + h / 2);
+                                    const uint16_t *sup = reinterpret_cast<const uint16_t *>(pr + wo_u + h / 2);
+                                    const float sg = bf16_bits(sgp[gi]);
+                                    const float bg = bf16_bits(sgp[tl.sbh / 2 + gi]);
+                                    const float su = bf16_bits(sup[gi]);
+                                    const float bu = bf16_bits(sup[tl.sbh / 2 + gi]);
+                                    float &ag = accg[(r * NT + k) * 2 + 0];
+                                    float &au = accg[(r * NT + k) * 2 + 1];
+                                    // s*sx*Q + b*X per chunk (Q exact, common.cuh)
+                                    ag = fmaf(sg * sx, (float)dot_chunk_i16(wg, xp), fmaf(bg, X, ag));
+                                    au = fmaf(su * sx, (float)dot_chunk_i16(wu, xp), fmaf(bu, X, au));
+                                }
                             }
                         }
-                    }
-                    // lane holds value lane / kSg = (r*NT + k)*2 + m
-                    const float tot = warp_reduce_multi(accg);
-                    if (nslg == 1) {
-                        const float upv = __shfl_down_sync(0xffffffffu, tot, kSg);
-                        const float av = swiglu(tot, upv);  // meaningful where lane % (2kSg) == 0
-                        const int jj = lane / (2 * kSg), r = jj / NT, k = jj % NT;
-                        const bool lead = (lane % (2 * kSg)) == 0 && ((mask >> k) & 1u);
-                        if (NPASS == 1) {
-                            // slot r+1 (row R+4) is 2*kSg*NT lanes further on
-                            const float other = __shfl_down_sync(0xffffffffu, av, 2 * kSg * NT);
-                            if (lead && (r & 1) == 0) {
-                                const int pu = pg * PG + (r >> 1);
-                                put_act(actf, p.act_cb * 8, a, k, g.u * I + g.r0 + 8 * (pu >> 2) + (pu & 3),
-                                        av, other);
+                        // lane holds value lane / kSg = (r*NT + k)*2 + m
+                        const float tot = warp_reduce_multi(accg);
+                        if (nslg == 1) {
+                            const float upv = __shfl_down_sync(0xffffffffu, tot, kSg);
+                            const float av = swiglu(tot, upv);  // meaningful where lane % (2kSg) == 0
+                            const int jj = lane / (2 * kSg), r = jj / NT, k = jj % NT;
+                            const bool lead = (lane % (2 * kSg)) == 0 && ((mask >> k) & 1u);
+                            if (NPASS == 1) {
+                                // slot r+1 (row R+4) is 2*kSg*NT lanes further on
+                                const float other = __shfl_down_sync(0xffffffffu, av, 2 * kSg * NT);
+                                if (lead && (r & 1) == 0) {
+                                    const int pu = pg * PG + (r >> 1);
+                                    put_act(actf, p.act_cb * 8, a, k, g.u * I + g.r0 + 8 * (pu >> 2) + (pu & 3),
+                                            av, other);
+                                }
+                            } else if (pass == 0) {
+                                act_prev = av;
+                            } else if (lead) {
+                                put_act(actf, p.act_cb * 8, a, k, g.u * I + g.r0 + 8 * (pg >> 2) + (pg & 3),
+                                        act_prev, av);
                             }
-                        } else if (pass == 0) {
-                            act_prev = av;
-                        } else if (lead) {
-                            put_act(actf, p.act_cb * 8, a, k, g.u * I + g.r0 + 8 * (pg >> 2) + (pg & 3),
-                                    act_prev, av);
+                        } else if (lane % kSg == 0) {
+                            const int v = lane / kSg, r = v / (2 * NT), km = v % (2 * NT);
+                            const int lr = g.u * I + g.r0 + trow[r] - a;
+                            gup[((size_t)lr * nslg + j) * (2 * NT) + km] = tot;
                         }
-                    } else if (lane % kSg == 0) {
-                        const int v = lane / kSg, r = v / (2 * NT), km = v % (2 * NT);
-                        const int lr = g.u * I + g.r0 + trow[r] - a;
-                        gup[((size_t)lr * nslg + j) * (2 * NT) + km] = tot;
                     }
                 }
+                release_item(empty, ctl, s, ipt_g);
             }
-            release_item(empty, ctl, s, ipt_g);
         }
         if (tid == 0) trace_event(p.trace, 0, 17);
         named_sync(1, kConsumerThreads);  // every gate/up item of this CTA is done
@@ -1122,8 +1395,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         named_sync(1, kConsumerThreads);
         for (int i = tid; i < ncb_cta * NT; i += kConsumerThreads) {
             const int cb = i / NT, k = i % NT;
-            const int R0 = a + 8 * cb, e = rs.ulist[fdiv(R0, p.fd_I)];
-            if (ctl.abort || !((rs.tmask[e] >> k) & 1u)) continue;
+            const int R0 = a + 8 * cb, u = fdiv(R0, p.fd_I);
+            // k: a token (row groups) or a token slot of expert u (slot path)
+            if (ctl.abort || (slot_path(NT) ? k >= ctl.ute[u] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
             const int gg = fdiv(a8 + cb, p.fd_gcb);
             const int c_lo = max(gg * gcb, a8) - a8, c_hi = min((gg + 1) * gcb, b >> 3) - a8;
             float m = 0.f;
@@ -1159,94 +1433,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         const int nd_items = (ctl.abort || ntd == 0) ? 0 : nic * ipt_d;
         float *dst = p.out_acc ? p.acc : reinterpret_cast<float *>(p.out);
         bool seen = false;  // epochs_seen observed (acquire) by this warp
-        for (;;) {
-            const int q = grab(&ctl.next_dn);
-            if (q >= nd_items) break;
-            const int ic = fdiv(q, p.fd_iptd), wi = q - ic * ipt_d;
-            const int ri = (wi * 32 + lane) * LR;  // first row (in the chunk) of this lane
-            if (q == 0 && lane == 0) trace_event(p.trace, 0, 18);
-            float tot[LR][NT];
-#pragma unroll
-            for (int r = 0; r < LR; ++r)
-#pragma unroll
-                for (int t = 0; t < NT; ++t) tot[r][t] = 0.f;
-            unsigned any = 0u;
-            bool ok = true;
-            for (int jt = 0; jt < nsub; ++jt) {
-                const int n = ntg + ic * nsub + jt, s = n % NSL;
-                if (!wait_tile(full, ctl, s, n, NSL, p.err)) {
-                    ok = false;
-                    break;
-                }
-                if (lane == 0 && wi == 0 && n == ntg) trace_event(p.trace, 0, 22);
-                if (lane == 0 && wi == 0 && n == ntg + ntd - 1) trace_event(p.trace, 0, 23);
-                const StageGeo g = ctl.geo[s];
-                const int e = rs.ulist[g.u];
-                const unsigned mask = rs.tmask[e];
-                const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + g.off) + ri;
-                const uint32_t *SBt = Wt + (size_t)g.nr * RC;
-                const int gfirst = fdiv(g.r0, p.fd_gcb);  // first group (concatenated space)
-                float y[LR][NT];
-                int Q[LR][NT];
-#pragma unroll
-                for (int r = 0; r < LR; ++r)
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) {
-                        y[r][t] = 0.f;
-                        Q[r][t] = 0;
-                    }
-                int gcur = gfirst, left = gcb - (g.r0 - gfirst * gcb);  // blocks left in gcur
-                auto flush = [&](int gg) {
-                    uint32_t sb[LR];
-                    load_words<LR>(SBt + (size_t)(gg - gfirst) * RC, sb);
-                    const float *xg = xseg + (size_t)(gg - ag) * NT * 2;
-#pragma unroll
-                    for (int r = 0; r < LR; ++r) {
-                        const float sc = bf16_bits(sb[r] & 0xFFFFu), bi = bf16_bits(sb[r] >> 16);
-#pragma unroll
-                        for (int t = 0; t < NT; ++t) {
-                            // s * sa * Q + b * X over the group's columns in this range
-                            if ((mask >> t) & 1u)
-                                y[r][t] = fmaf(sc * xg[2 * t + 1], (float)Q[r][t],
-                                               fmaf(bi, xg[2 * t], y[r][t]));
-                            Q[r][t] = 0;
-                        }
-                    }
-                };
-                for (int c = 0; c < g.nr; ++c) {
-                    uint32_t wd[LR];
-                    load_words<LR>(Wt + (size_t)c * RC, wd);
-                    const uint4 *av = reinterpret_cast<const uint4 *>(act) + (g.r0 + c - a8);
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) {
-                        if ((mask >> t) & 1u) {
-                            const uint4 v = av[(size_t)t * p.act_cb];
-#pragma unroll
-                            for (int r = 0; r < LR; ++r) {
-                                const uint32_t lo = wd[r] & 0x0F0F0F0Fu, hi = (wd[r] >> 4) & 0x0F0F0F0Fu;
-                                Q[r][t] = dp2a_hi(v.w, hi, dp2a_lo(v.z, hi, dp2a_hi(v.y, lo,
-                                                                                  dp2a_lo(v.x, lo, Q[r][t]))));
-                            }
-                        }
-                    }
-                    if (--left == 0) {
-                        flush(gcur);
-                        ++gcur;
-                        left = gcb;
-                    }
-                }
-                if (left != gcb) flush(gcur);
-#pragma unroll
-                for (int t = 0; t < NT; ++t)
-                    if ((mask >> t) & 1u) {
-                        const float wk = rs.w[t][rs.kof[e][t]];
-#pragma unroll
-                        for (int r = 0; r < LR; ++r) tot[r][t] = fmaf(wk, y[r][t], tot[r][t]);
-                    }
-                any |= mask;
-                release_item(empty, ctl, s, ipt_d);
-            }
-            if (!ok) break;
+        // (acquire) every CTA's output rows are initialised: needed once per
+        // warp, before its first atomic
+        auto see_epochs = [&]() -> bool {
             if (!seen) {
                 if (lane == 0) {
                     for (uint32_t it = 0; it < kWaitLimit && !seen; ++it) {
@@ -1259,12 +1448,164 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                     if (!seen && !*vabort) set_abort(ctl, p.err);
                 }
                 seen = __shfl_sync(0xffffffffu, seen, 0);
-                if (!seen) break;
             }
-            const int i = ic * RC + ri;
+            return seen;
+        };
+        if constexpr (slot_path(NT)) {
+            // Item as above; the chunk's tiles come expert by expert (a tile
+            // never spans two), and each expert's run of tiles is summed per
+            // token slot and added to the output once, weighted by the
+            // slot's routing weight.
+            for (;;) {
+                const int q = grab(&ctl.next_dn);
+                if (q >= nd_items) break;
+                const int ic = fdiv(q, p.fd_iptd), wi = q - ic * ipt_d;
+                const int ri = (wi * 32 + lane) * LR;  // first row (in the chunk) of this lane
+                const int i = ic * RC + ri;
+                if (q == 0 && lane == 0) trace_event(p.trace, 0, 18);
+                float y[LR][NT];
 #pragma unroll
-            for (int t = 0; t < NT; ++t)
-                if ((any >> t) & 1u) add_words<LR>(dst + (size_t)t * h + i, tot, t);
+                for (int r = 0; r < LR; ++r)
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) y[r][t] = 0.f;
+                int cur = -1;  // distinct expert whose sums y holds
+                auto flush_expert = [&]() -> bool {
+                    if (!see_epochs()) return false;
+                    const int e = rs.ulist[cur], te = ctl.ute[cur];
+#pragma unroll
+                    for (int j = 0; j < NT; ++j) {
+                        if (j < te) {
+                            const int t = ctl.utok[cur][j];
+                            const float wk = rs.w[t][rs.kof[e][t]];
+                            float v[LR][1];
+#pragma unroll
+                            for (int r = 0; r < LR; ++r) v[r][0] = wk * y[r][j];
+                            add_words<LR>(dst + (size_t)t * h + i, v, 0);
+                        }
+#pragma unroll
+                        for (int r = 0; r < LR; ++r) y[r][j] = 0.f;
+                    }
+                    return true;
+                };
+                bool ok = true;
+                for (int jt = 0; jt < nsub; ++jt) {
+                    const int n = ntg + ic * nsub + jt, s = n % NSL;
+                    if (!wait_tile(full, ctl, s, n, NSL, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    if (lane == 0 && wi == 0 && n == ntg) trace_event(p.trace, 0, 22);
+                    if (lane == 0 && wi == 0 && n == ntg + ntd - 1) trace_event(p.trace, 0, 23);
+                    const StageGeo g = ctl.geo[s];
+                    if (g.u != cur) {
+                        if (cur >= 0 && !flush_expert()) {
+                            ok = false;
+                            break;
+                        }
+                        cur = g.u;
+                    }
+                    const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + g.off) + ri;
+                    dn_tile_slots<LR, NT>(ctl.ute[g.u], p, y, Wt, Wt + (size_t)g.nr * RC, g, act, xseg, a8, ag);
+                    release_item(empty, ctl, s, ipt_d);
+                }
+                if (ok && cur >= 0) ok = flush_expert();
+                if (!ok) break;
+            }
+        } else {
+            for (;;) {
+                const int q = grab(&ctl.next_dn);
+                if (q >= nd_items) break;
+                const int ic = fdiv(q, p.fd_iptd), wi = q - ic * ipt_d;
+                const int ri = (wi * 32 + lane) * LR;  // first row (in the chunk) of this lane
+                if (q == 0 && lane == 0) trace_event(p.trace, 0, 18);
+                float tot[LR][NT];
+    #pragma unroll
+                for (int r = 0; r < LR; ++r)
+    #pragma unroll
+                    for (int t = 0; t < NT; ++t) tot[r][t] = 0.f;
+                unsigned any = 0u;
+                bool ok = true;
+                for (int jt = 0; jt < nsub; ++jt) {
+                    const int n = ntg + ic * nsub + jt, s = n % NSL;
+                    if (!wait_tile(full, ctl, s, n, NSL, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    if (lane == 0 && wi == 0 && n == ntg) trace_event(p.trace, 0, 22);
+                    if (lane == 0 && wi == 0 && n == ntg + ntd - 1) trace_event(p.trace, 0, 23);
+                    const StageGeo g = ctl.geo[s];
+                    const int e = rs.ulist[g.u];
+                    const unsigned mask = rs.tmask[e];
+                    const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + g.off) + ri;
+                    const uint32_t *SBt = Wt + (size_t)g.nr * RC;
+                    const int gfirst = fdiv(g.r0, p.fd_gcb);  // first group (concatenated space)
+                    float y[LR][NT];
+                    int Q[LR][NT];
+    #pragma unroll
+                    for (int r = 0; r < LR; ++r)
+    #pragma unroll
+                        for (int t = 0; t < NT; ++t) {
+                            y[r][t] = 0.f;
+                            Q[r][t] = 0;
+                        }
+                    int gcur = gfirst, left = gcb - (g.r0 - gfirst * gcb);  // blocks left in gcur
+                    auto flush = [&](int gg) {
+                        uint32_t sb[LR];
+                        load_words<LR>(SBt + (size_t)(gg - gfirst) * RC, sb);
+                        const float *xg = xseg + (size_t)(gg - ag) * NT * 2;
+    #pragma unroll
+                        for (int r = 0; r < LR; ++r) {
+                            const float sc = bf16_bits(sb[r] & 0xFFFFu), bi = bf16_bits(sb[r] >> 16);
+    #pragma unroll
+                            for (int t = 0; t < NT; ++t) {
+                                // s * sa * Q + b * X over the group's columns in this range
+                                if ((mask >> t) & 1u)
+                                    y[r][t] = fmaf(sc * xg[2 * t + 1], (float)Q[r][t],
+                                                   fmaf(bi, xg[2 * t], y[r][t]));
+                                Q[r][t] = 0;
+                            }
+                        }
+                    };
+                    for (int c = 0; c < g.nr; ++c) {
+                        uint32_t wd[LR];
+                        load_words<LR>(Wt + (size_t)c * RC, wd);
+                        const uint4 *av = reinterpret_cast<const uint4 *>(act) + (g.r0 + c - a8);
+    #pragma unroll
+                        for (int t = 0; t < NT; ++t) {
+                            if ((mask >> t) & 1u) {
+                                const uint4 v = av[(size_t)t * p.act_cb];
+    #pragma unroll
+                                for (int r = 0; r < LR; ++r) {
+                                    const uint32_t lo = wd[r] & 0x0F0F0F0Fu, hi = (wd[r] >> 4) & 0x0F0F0F0Fu;
+                                    Q[r][t] = dp2a_hi(v.w, hi, dp2a_lo(v.z, hi, dp2a_hi(v.y, lo,
+                                                                                      dp2a_lo(v.x, lo, Q[r][t]))));
+                                }
+                            }
+                        }
+                        if (--left == 0) {
+                            flush(gcur);
+                            ++gcur;
+                            left = gcb;
+                        }
+                    }
+                    if (left != gcb) flush(gcur);
+    #pragma unroll
+                    for (int t = 0; t < NT; ++t)
+                        if ((mask >> t) & 1u) {
+                            const float wk = rs.w[t][rs.kof[e][t]];
+    #pragma unroll
+                            for (int r = 0; r < LR; ++r) tot[r][t] = fmaf(wk, y[r][t], tot[r][t]);
+                        }
+                    any |= mask;
+                    release_item(empty, ctl, s, ipt_d);
+                }
+                if (!ok) break;
+                if (!see_epochs()) break;
+                const int i = ic * RC + ri;
+    #pragma unroll
+                for (int t = 0; t < NT; ++t)
+                    if ((any >> t) & 1u) add_words<LR>(dst + (size_t)t * h + i, tot, t);
+            }
         }
         if (tid == 0) trace_event(p.trace, 0, 8);
         if (p.out_acc) {

@@ -386,7 +386,12 @@ __device__ __forceinline__ void load_x32_any(const void *x, int is_bf16, size_t 
         const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + at);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const float4 r = __ldcg(p + i);  // coherent: x may come from peers during the launch
+            // a plain (weak, L1-cached) load: x may come from peers during the
+            // launch, which the caller orders before this load by an acquire
+            // and a barrier (the non-coherent __ldg path would not be covered);
+            // L1 merges the chunk's 8 loads into one line fill (__ldcg made 8
+            // L2 requests per line, from every SM at once)
+            const float4 r = p[i];
             v[4 * i] = r.x;
             v[4 * i + 1] = r.y;
             v[4 * i + 2] = r.z;

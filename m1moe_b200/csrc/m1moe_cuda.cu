@@ -256,8 +256,10 @@ constexpr size_t kEpochBytes = (size_t)m1::kMaxCtas * m1::kEpochStride * sizeof(
 // summed by its own CTA, so that up to E*parts CTAs share the router product
 // instead of E.  At least 256 (token, 8-column block) pairs per part, at most
 // 16 parts, and the box (ntok*E*parts tagged words) within
-// kMaxTok*kMaxExperts words.
+// kMaxTok*kMaxExperts words.  Batches of 1 and 2 (the kernels below the slot
+// path) use one part.
 int logit_parts(int grid, int E, int ntok, int h) {
+    if (ntok <= 2) return 1;
     int P = std::min(std::max(1, grid / E), 16);
     P = std::min(P, std::max(1, ntok * h / 2048));
     while (P > 1 && ntok * E * P > m1::kMaxTok * m1::kMaxExperts) --P;
@@ -388,6 +390,7 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt) {
     const size_t keys = take((size_t)nt * p.E * 8);
     const size_t rlog = take((size_t)nt * p.E * 4);
     const size_t lpart = take(8 * m1::kMaxTok * 4);
+    const size_t slots = m1::slot_path(nt) ? take(sizeof(m1::Slots)) : 0;
     const size_t fixed = off;
     // the tile ring: everything else, tiles packed back to back, at most
     // kLayerSlots of them in flight (each slot has a full and an empty barrier)
@@ -409,6 +412,7 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt) {
     p.off_keys = (int)(base + keys);
     p.off_rlog = (int)(base + rlog);
     p.off_lpart = (int)(base + lpart);
+    p.off_slots = (int)(base + slots);
     return base + fixed;
 }
 

@@ -181,7 +181,7 @@ struct LayerParams {
     // shared-memory offsets (bytes, 16-aligned)
     int off_bars, off_ctl, off_xs, off_xsum, off_gup, off_actf, off_act, off_xseg, off_blk, off_keys,
         off_rlog,
-        off_lpart;
+        off_lpart, off_slots;
 };
 
 // The tile in a ring slot.  Gate/up: distinct expert u, first pair-row r0 of
@@ -216,6 +216,11 @@ struct Ctl {
     int vstart[kMaxStages];      // producer: running byte position of each slot's tile
     StageGeo geo[kMaxStages];
     TileCopy copy[32];           // producer: the next (up to) 32 tiles' copies
+};
+
+// Token slots of the distinct experts (slot path only; a shared-memory
+// region of its own, so that smaller batches keep the bytes for tiles).
+struct Slots {
     unsigned char ute[kMaxPairs];            // tokens of distinct expert u
     unsigned char utok[kMaxPairs][kMaxTok];  // its token slots: j-th token, ascending
 };
@@ -327,12 +332,14 @@ __device__ __forceinline__ unsigned long long logit_key(float v, int e) {
     return ((unsigned long long)ord << 32) | (uint32_t)(0xFFFF - e);
 }
 
+template <int NT>
 __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
                           unsigned long long *keys, float *parts, unsigned tag, const volatile int *abort) {
     const int tid = threadIdx.x;
-    const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E, LP = p.lparts, nw = nel * LP;
-    // a. collect the tagged partial logits (all of this thread's loads in
-    //    flight at once; nw <= kMaxTok * kMaxExperts)
+    const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E;
+    // a. collect the tagged (partial) logits: all of this thread's loads in
+    //    flight at once; nw <= kMaxTok * kMaxExperts words
+    const int LP = slot_path(NT) ? p.lparts : 1, nw = nel * LP;
     constexpr int kPer = kMaxTok * kMaxExperts / 256;
     const unsigned long long *box = p.xlog + (size_t)(blockIdx.x % p.nbox) * p.box_words;
     bool ok = false;
@@ -355,26 +362,35 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
         __nanosleep(nap);
         nap = min(nap * 2, 256u);
     }
-    // b. the logit of (token, expert) element i: its parts summed in order
-    auto put = [&](int i, float v) {
-        int e = i;
-        while (e >= E) e -= E;
-        rlog[i] = v;
-        keys[i] = logit_key(v, e);
-    };
+    // b. the logit of (token, expert) element i (its parts summed in order)
+    //    and its ranking key
+    if constexpr (slot_path(NT)) {
+        if (LP > 1) {
+#pragma unroll
+            for (int j = 0; j < kPer; ++j)
+                if (tid + 256 * j < nw) parts[tid + 256 * j] = __uint_as_float((uint32_t)w[j]);
+            named_sync(2, 256);
+            for (int i = tid; i < nel; i += 256) {
+                float v = 0.f;
+                for (int q = 0; q < LP; ++q) v += parts[i * LP + q];
+                int e = i;
+                while (e >= E) e -= E;
+                rlog[i] = v;
+                keys[i] = logit_key(v, e);
+            }
+        }
+    }
     if (LP == 1) {
 #pragma unroll
-        for (int j = 0; j < kPer; ++j)
-            if (tid + 256 * j < nel) put(tid + 256 * j, __uint_as_float((uint32_t)w[j]));
-    } else {
-#pragma unroll
-        for (int j = 0; j < kPer; ++j)
-            if (tid + 256 * j < nw) parts[tid + 256 * j] = __uint_as_float((uint32_t)w[j]);
-        named_sync(2, 256);
-        for (int i = tid; i < nel; i += 256) {
-            float v = 0.f;
-            for (int q = 0; q < LP; ++q) v += parts[i * LP + q];
-            put(i, v);
+        for (int j = 0; j < kPer; ++j) {
+            const int i = tid + 256 * j;
+            if (i < nel) {
+                int e = i;
+                while (e >= E) e -= E;
+                const float v = __uint_as_float((uint32_t)w[j]);
+                rlog[i] = v;
+                keys[i] = logit_key(v, e);
+            }
         }
     }
     if (!named_sync_and(2, 256, ok)) return false;
@@ -563,7 +579,8 @@ __device__ __forceinline__ void add_words(float *dst, const float (&tot)[LR][NT]
 // in units of 8 rows so that row pairs (R, R+4) stay together; ntg gate/up
 // tiles (cut at multiples of GT, so a tile never crosses experts) and ntd =
 // nsub * nic down tiles (column-block runs, dn_run_end, per row chunk).
-__device__ void route_geometry(const LayerParams &p, Ctl &ctl, int blk) {
+template <int NT>
+__device__ void route_geometry(const LayerParams &p, Ctl &ctl, Slots &sl, int blk) {
     RouteInfo &rs = ctl.route;
     const int lane = threadIdx.x & 31;
     unsigned m = lane < kMaxExperts / 32 ? rs.emask[lane] : 0u;
@@ -581,15 +598,17 @@ __device__ void route_geometry(const LayerParams &p, Ctl &ctl, int blk) {
     }
     const int nU = __shfl_sync(0xffffffffu, incl, 31);
     __syncwarp();  // ulist complete
-    // token slots of every distinct expert
-    for (int u = lane; u < nU; u += 32) {
-        unsigned tm = rs.tmask[rs.ulist[u]];
-        int j = 0;
-        while (tm) {
-            ctl.utok[u][j++] = (unsigned char)(__ffs(tm) - 1);
-            tm &= tm - 1;
+    if constexpr (slot_path(NT)) {
+        // token slots of every distinct expert
+        for (int u = lane; u < nU; u += 32) {
+            unsigned tm = rs.tmask[rs.ulist[u]];
+            int j = 0;
+            while (tm) {
+                sl.utok[u][j++] = (unsigned char)(__ffs(tm) - 1);
+                tm &= tm - 1;
+            }
+            sl.ute[u] = (unsigned char)j;
         }
-        ctl.ute[u] = (unsigned char)j;
     }
     const int n8 = p.I >> 3;  // units of 8 rows per expert
     int ua = 0, ub = 0;       // this CTA's units [ua, ub)
@@ -972,6 +991,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.off_bars);
     uint64_t *empty = full + NSL;
     Ctl &ctl = *reinterpret_cast<Ctl *>(smem + p.off_ctl);
+    Slots &sl = *reinterpret_cast<Slots *>(smem + p.off_slots);  // valid on the slot path
     RouteInfo &rs = ctl.route;
     uint32_t *xq = reinterpret_cast<uint32_t *>(smem + p.off_xs);       // [ntok][h/2] int16 pairs
     float *xsc = reinterpret_cast<float *>(smem + p.off_xsum);          // [ntok][nch] chunk scales
@@ -1059,75 +1079,146 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     }
     const int nrows = i1 - i0;
     if (warp < 8) {
-        // ---- phase 2: partial logits, straight from global memory ----
-        // Work item (e, part): W_r[e] . x[t] over the part's 8-column blocks
-        // [n8*part/P, n8*(part+1)/P) for every token; a thread takes token
-        // tid % NT of blocks tid / NT, +256/NT, ...  Fixed order throughout:
-        // lanes of one token by xor shuffles, then the 8 warps in order.
-        for (int e = tid; e < p.E; e += 256) rs.tmask[e] = 0u;
-        if (tid < kMaxExperts / 32) rs.emask[tid] = 0u;
-        const int P = p.lparts, nitems = p.E * P, n8 = h / 8;
-        constexpr int LT = NT == 1 ? 0 : (NT == 2 ? 1 : (NT == 4 ? 2 : 3));
-        const int tt = tid & (NT - 1);
-        const int nmine = (nitems > blk) ? (nitems - blk + G - 1) / G : 0;
-        for (int m = 0; m < nmine; ++m) {
-            const int item = blk + m * G, e = item / P, part = item - e * P;
-            const int g0 = n8 * part / P, g1 = n8 * (part + 1) / P;
-            const uint4 *row = reinterpret_cast<const uint4 *>(p.router + (size_t)e * h);
-            float acc = 0.f;
-            if (tt < p.ntok) {
-                for (int g8 = g0 + (tid >> LT); g8 < g1; g8 += 256 >> LT) {
-                    const uint4 wv = __ldg(row + g8);
-                    float xv[8];
-                    if (Xbf16) {
-                        const uint4 r = *(reinterpret_cast<const uint4 *>(
-                            reinterpret_cast<const uint16_t *>(X) + (size_t)tt * h) + g8);
-                        const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            xv[2 * j] = __uint_as_float(rr[j] << 16);
-                            xv[2 * j + 1] = __uint_as_float(rr[j] & 0xFFFF0000u);
+        if constexpr (slot_path(NT)) {
+            // ---- phase 2: partial logits, straight from global memory ----
+            // Work item (e, part): W_r[e] . x[t] over the part's 8-column blocks
+            // [n8*part/P, n8*(part+1)/P) for every token; a thread takes token
+            // tid % NT of blocks tid / NT, +256/NT, ...  Fixed order throughout:
+            // lanes of one token by xor shuffles, then the 8 warps in order.
+            for (int e = tid; e < p.E; e += 256) rs.tmask[e] = 0u;
+            if (tid < kMaxExperts / 32) rs.emask[tid] = 0u;
+            const int P = p.lparts, nitems = p.E * P, n8 = h / 8;
+            constexpr int LT = NT == 1 ? 0 : (NT == 2 ? 1 : (NT == 4 ? 2 : 3));
+            const int tt = tid & (NT - 1);
+            const int nmine = (nitems > blk) ? (nitems - blk + G - 1) / G : 0;
+            for (int m = 0; m < nmine; ++m) {
+                const int item = blk + m * G, e = item / P, part = item - e * P;
+                const int g0 = n8 * part / P, g1 = n8 * (part + 1) / P;
+                const uint4 *row = reinterpret_cast<const uint4 *>(p.router + (size_t)e * h);
+                float acc = 0.f;
+                if (tt < p.ntok) {
+                    for (int g8 = g0 + (tid >> LT); g8 < g1; g8 += 256 >> LT) {
+                        const uint4 wv = __ldg(row + g8);
+                        float xv[8];
+                        if (Xbf16) {
+                            const uint4 r = *(reinterpret_cast<const uint4 *>(
+                                reinterpret_cast<const uint16_t *>(X) + (size_t)tt * h) + g8);
+                            const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+    #pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                xv[2 * j] = __uint_as_float(rr[j] << 16);
+                                xv[2 * j + 1] = __uint_as_float(rr[j] & 0xFFFF0000u);
+                            }
+                        } else {
+                            const float4 *xf = reinterpret_cast<const float4 *>(
+                                reinterpret_cast<const float *>(X) + (size_t)tt * h) + 2 * g8;
+                            const float4 a0 = xf[0], a1 = xf[1];  // plain loads (load_x32_any)
+                            xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
+                            xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
                         }
-                    } else {
-                        const float4 *xf = reinterpret_cast<const float4 *>(
-                            reinterpret_cast<const float *>(X) + (size_t)tt * h) + 2 * g8;
-                        const float4 a0 = __ldcg(xf), a1 = __ldcg(xf + 1);
-                        xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
-                        xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
-                    }
-                    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        acc = fmaf(__uint_as_float(ww[j] << 16), xv[2 * j], acc);
-                        acc = fmaf(__uint_as_float(ww[j] & 0xFFFF0000u), xv[2 * j + 1], acc);
+                        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    #pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            acc = fmaf(__uint_as_float(ww[j] << 16), xv[2 * j], acc);
+                            acc = fmaf(__uint_as_float(ww[j] & 0xFFFF0000u), xv[2 * j + 1], acc);
+                        }
                     }
                 }
+    #pragma unroll
+                for (int o = NT; o < 32; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (lane < NT) lpart[warp * kMaxTok + lane] = acc;
+                named_sync(2, 256);
+                // publish into every CTA's box (each box is polled by its CTAs only)
+                uint32_t sv[NT];
+    #pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    float s = 0.f;
+                    if (t < p.ntok)
+                        for (int w = 0; w < 8; ++w) s += lpart[w * kMaxTok + t];
+                    sv[t] = __float_as_uint(s);
+                }
+                for (int bx = tid; bx < p.nbox; bx += 256) {
+                    unsigned long long *box = p.xlog + (size_t)bx * p.box_words + (size_t)e * P + part;
+    #pragma unroll
+                    for (int t = 0; t < NT; ++t)
+                        if (t < p.ntok) st_relaxed_u64(box + (size_t)t * p.E * P, tagged(tag, sv[t]));
+                }
+                named_sync(2, 256);
             }
-#pragma unroll
-            for (int o = NT; o < 32; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            if (lane < NT) lpart[warp * kMaxTok + lane] = acc;
-            named_sync(2, 256);
-            // publish into every CTA's box (each box is polled by its CTAs only)
-            uint32_t sv[NT];
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                float s = 0.f;
-                if (t < p.ntok)
-                    for (int w = 0; w < 8; ++w) s += lpart[w * kMaxTok + t];
-                sv[t] = __float_as_uint(s);
+        } else {
+            // ---- phase 2: logits of this CTA's experts, straight from global memory ----
+            // (batches of 1 and 2: one part per logit, a CTA per expert)
+            for (int e = tid; e < p.E; e += 256) rs.tmask[e] = 0u;
+            if (tid < kMaxExperts / 32) rs.emask[tid] = 0u;
+            const int nmine = (p.E > blk) ? (p.E - blk + G - 1) / G : 0;
+            for (int m = 0; m < nmine; ++m) {
+                const int e = blk + m * G;
+                const uint4 *row = reinterpret_cast<const uint4 *>(p.router + (size_t)e * h);
+                float acc[NT];
+    #pragma unroll
+                for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+                for (int g8 = tid; g8 < h / 8; g8 += 256) {
+                    const uint4 wv = __ldg(row + g8);
+                    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+                    float wf[8];
+    #pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        wf[2 * j] = __uint_as_float(ww[j] << 16);
+                        wf[2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
+                    }
+    #pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        if (t < p.ntok) {
+                            float xv[8];
+                            if (Xbf16) {
+                                const uint4 r = *(reinterpret_cast<const uint4 *>(
+                                    reinterpret_cast<const uint16_t *>(X) + (size_t)t * h) + g8);
+                                const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+    #pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    xv[2 * j] = __uint_as_float(rr[j] << 16);
+                                    xv[2 * j + 1] = __uint_as_float(rr[j] & 0xFFFF0000u);
+                                }
+                            } else {
+                                const float4 *xf = reinterpret_cast<const float4 *>(
+                                    reinterpret_cast<const float *>(X) + (size_t)t * h) + 2 * g8;
+                                const float4 a0 = xf[0], a1 = xf[1];  // plain loads (load_x32_any)
+                                xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
+                                xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
+                            }
+    #pragma unroll
+                            for (int j = 0; j < 8; ++j) acc[t] = fmaf(wf[j], xv[j], acc[t]);
+                        }
+                    }
+                }
+    #pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    const float v = warp_sum(acc[t]);
+                    if (lane == 0) lpart[warp * kMaxTok + t] = v;
+                }
+                named_sync(2, 256);
+                // publish into every CTA's box (each box is polled by its CTAs only)
+                uint32_t sv[NT];
+    #pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    float s = 0.f;
+                    if (t < p.ntok)
+                        for (int w = 0; w < 8; ++w) s += lpart[w * kMaxTok + t];
+                    sv[t] = __float_as_uint(s);
+                }
+                for (int bx = tid; bx < p.nbox; bx += 256) {
+                    unsigned long long *box = p.xlog + (size_t)bx * p.box_words + e;
+    #pragma unroll
+                    for (int t = 0; t < NT; ++t)
+                        if (t < p.ntok) st_relaxed_u64(box + (size_t)t * p.E, tagged(tag, sv[t]));
+                }
+                named_sync(2, 256);
             }
-            for (int bx = tid; bx < p.nbox; bx += 256) {
-                unsigned long long *box = p.xlog + (size_t)bx * p.box_words + (size_t)e * P + part;
-#pragma unroll
-                for (int t = 0; t < NT; ++t)
-                    if (t < p.ntok) st_relaxed_u64(box + (size_t)t * p.E * P, tagged(tag, sv[t]));
-            }
-            named_sync(2, 256);
         }
         if (tid == 0) trace_event(p.trace, 0, 2);
         // ---- phase 3: route (warps 0..7 of every CTA) ----
         // partial logits are summed in the tile ring, idle until routing is done
-        const bool ok = route_cta(p, rs, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
+        const bool ok = route_cta<NT>(p, rs, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
         if (tid == 0) trace_event(p.trace, 0, 3);
         if (tid == 0) {
             if (ok) ctl.route_ok = 1;
@@ -1179,7 +1270,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             named_sync(3, 256 + 32);
             if (lane == 0) trace_event(p.trace, 0, 19);
             if (!p.route_only && ctl.route_ok) {
-                route_geometry(p, ctl, blk);
+                route_geometry<NT>(p, ctl, sl, blk);
                 if (lane == 0) {
                     trace_event(p.trace, 0, 16);
                     if (ctl.ntg + ctl.ntd > 0) {
@@ -1252,7 +1343,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 if (q == 0 && lane == 0) trace_event(p.trace, 0, 5);
                 const StageGeo g = ctl.geo[s];
                 if (rr < g.nr)
-                    gu_row_slots<NT>(ctl.ute[g.u], p, ring + g.off + (size_t)rr * tl.pr, ctl.utok[g.u], xq, xsc,
+                    gu_row_slots<NT>(sl.ute[g.u], p, ring + g.off + (size_t)rr * tl.pr, sl.utok[g.u], xq, xsc,
                                      xsum, actf, p.act_cb * 8, g.u * I + g.r0 + rr - a);
                 release_item(empty, ctl, s, ipt_g);
             }
@@ -1397,7 +1488,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             const int cb = i / NT, k = i % NT;
             const int R0 = a + 8 * cb, u = fdiv(R0, p.fd_I);
             // k: a token (row groups) or a token slot of expert u (slot path)
-            if (ctl.abort || (slot_path(NT) ? k >= ctl.ute[u] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
+            if (ctl.abort || (slot_path(NT) ? k >= sl.ute[u] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
             const int gg = fdiv(a8 + cb, p.fd_gcb);
             const int c_lo = max(gg * gcb, a8) - a8, c_hi = min((gg + 1) * gcb, b >> 3) - a8;
             float m = 0.f;
@@ -1471,11 +1562,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 int cur = -1;  // distinct expert whose sums y holds
                 auto flush_expert = [&]() -> bool {
                     if (!see_epochs()) return false;
-                    const int e = rs.ulist[cur], te = ctl.ute[cur];
+                    const int e = rs.ulist[cur], te = sl.ute[cur];
 #pragma unroll
                     for (int j = 0; j < NT; ++j) {
                         if (j < te) {
-                            const int t = ctl.utok[cur][j];
+                            const int t = sl.utok[cur][j];
                             const float wk = rs.w[t][rs.kof[e][t]];
                             float v[LR][1];
 #pragma unroll
@@ -1505,7 +1596,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                         cur = g.u;
                     }
                     const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + g.off) + ri;
-                    dn_tile_slots<LR, NT>(ctl.ute[g.u], p, y, Wt, Wt + (size_t)g.nr * RC, g, act, xseg, a8, ag);
+                    dn_tile_slots<LR, NT>(sl.ute[g.u], p, y, Wt, Wt + (size_t)g.nr * RC, g, act, xseg, a8, ag);
                     release_item(empty, ctl, s, ipt_d);
                 }
                 if (ok && cur >= 0) ok = flush_expert();

@@ -256,10 +256,8 @@ constexpr size_t kEpochBytes = (size_t)m1::kMaxCtas * m1::kEpochStride * sizeof(
 // summed by its own CTA, so that up to E*parts CTAs share the router product
 // instead of E.  At least 256 (token, 8-column block) pairs per part, at most
 // 16 parts, and the box (ntok*E*parts tagged words) within
-// kMaxTok*kMaxExperts words.  Batches of 1 and 2 (the kernels below the slot
-// path) use one part.
+// kMaxTok*kMaxExperts words.  (The row-group kernels use one part.)
 int logit_parts(int grid, int E, int ntok, int h) {
-    if (ntok <= 2) return 1;
     int P = std::min(std::max(1, grid / E), 16);
     P = std::min(P, std::max(1, ntok * h / 2048));
     while (P > 1 && ntok * E * P > m1::kMaxTok * m1::kMaxExperts) --P;
@@ -300,7 +298,6 @@ m1::LayerParams layer_params(m1moe_cuda_ctx *c, int layer, int B) {
     p.xlog = c->xlog;
     p.nbox = c->nbox;
     p.box_words = c->box_words;
-    p.lparts = logit_parts(c->nbox, g.num_experts, B, g.hidden_dim);
     p.acc = c->acc;
     p.done = c->done;
     p.epochs = c->epochs;
@@ -320,7 +317,7 @@ int divisor_tile(int n, int m, long long cap) {
 
 // Plan tiles, stages and the shared-memory map of k_moe_layer<nt>.  Returns
 // the dynamic shared memory size, or 0 if the shape does not fit an SM.
-size_t plan_layer(m1::LayerParams &p, int grid, int nt) {
+size_t plan_layer(m1::LayerParams &p, int grid, int nt, bool slot) {
     const m1::TiledLayout &tl = p.tl;
     const int nch = p.h / m1::kChunkCols;
     const int maxU = std::min(p.ntok * p.K, p.ne);
@@ -335,11 +332,11 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt) {
     // one tile), filling the stage the down tiles need (at least kStageTarget/2)
     const long long stage_target = std::max<long long>(dn_bytes, kStageTarget / 2);
     // (the slot path has no row pairs: any multiple of 4 rows)
-    const int gmul = m1::slot_path(nt) ? 4 : 8;
-    const long long gu_target = m1::slot_path(nt) ? std::min<long long>(stage_target, kSlotTileBytes) : stage_target;
+    const int gmul = slot ? 4 : 8;
+    const long long gu_target = slot ? std::min<long long>(stage_target, kSlotTileBytes) : stage_target;
     p.gu_tile_rows = divisor_tile(p.I, gmul, std::max<long long>(gmul, gu_target / tl.pr));
     p.stage_bytes = (int)m1::round_up_ll(std::max<long long>(p.gu_tile_rows * tl.pr, dn_bytes), 128);
-    p.gu_nslices = nt <= 2 ? (nch + 31) / 32 : 1;
+    p.gu_nslices = (!slot && nt <= 2) ? (nch + 31) / 32 : 1;
     p.nic = p.h / tl.rc;
     p.fd_G = m1::make_fastdiv(grid);
     p.fd_GT = m1::make_fastdiv(p.gu_tile_rows);
@@ -347,7 +344,7 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt) {
     p.fd_ncbE = m1::make_fastdiv(p.I / 8);
     p.fd_gcb = m1::make_fastdiv(gcb);
     p.fd_gs = m1::make_fastdiv(p.gs);
-    p.fd_iptg = m1::make_fastdiv(m1::gu_items_per_tile(nt, p.gu_tile_rows, p.gu_nslices));
+    p.fd_iptg = m1::make_fastdiv(m1::gu_items_per_tile(slot, nt, p.gu_tile_rows, p.gu_nslices));
     p.fd_nslg = m1::make_fastdiv(p.gu_nslices);
     if (tl.rc % (32 * m1::dn_lane_rows(nt))) return 0;
     p.fd_iptd = m1::make_fastdiv(tl.rc / (32 * m1::dn_lane_rows(nt)));
@@ -383,14 +380,14 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt) {
     // the int16 activations and block statistics are written once gate/up is
     // done; the slot path places them over the staged x, which is dead then
     const size_t act_bytes = align16((size_t)nt * p.act_cb * 16), blk_bytes = (size_t)nt * p.act_cb * 8;
-    const bool alias_x = m1::slot_path(nt) && act_bytes + blk_bytes <= (size_t)nt * p.h * 2;
+    const bool alias_x = slot && act_bytes + blk_bytes <= (size_t)nt * p.h * 2;
     const size_t act = alias_x ? xs : take(act_bytes);
     const size_t xseg = take((size_t)nt * p.xseg_max * 8);
     const size_t blk = alias_x ? xs + act_bytes : take(blk_bytes);
     const size_t keys = take((size_t)nt * p.E * 8);
     const size_t rlog = take((size_t)nt * p.E * 4);
     const size_t lpart = take(8 * m1::kMaxTok * 4);
-    const size_t slots = m1::slot_path(nt) ? take(sizeof(m1::Slots)) : 0;
+    const size_t slots = slot ? take(sizeof(m1::Slots)) : 0;
     const size_t fixed = off;
     // the tile ring: everything else, tiles packed back to back, at most
     // kLayerSlots of them in flight (each slot has a full and an empty barrier)
@@ -416,13 +413,14 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt) {
     return base + fixed;
 }
 
-template <int NT>
+template <int NT, bool SL>
 m1moe_status launch_layer(m1moe_cuda_ctx *c, m1::LayerParams p, cudaStream_t st) {
     const int grid = c->nbox;  // one CTA per SM, each with its own logit box
-    const size_t smem = plan_layer(p, grid, NT);
+    p.lparts = SL ? logit_parts(grid, p.E, p.ntok, p.h) : 1;
+    const size_t smem = plan_layer(p, grid, NT, SL);
     if (smem == 0 || smem > kMaxDynSmem)
         return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
-    M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT, SL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -440,17 +438,18 @@ m1moe_status launch_layer(m1moe_cuda_ctx *c, m1::LayerParams p, cudaStream_t st)
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, m1::k_moe_layer<NT>, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, m1::k_moe_layer<NT, SL>, p);
     if (e != cudaSuccess) return cuda_fail(e, "k_moe_layer launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return M1MOE_OK;
 }
 
 m1moe_status dispatch_layer(m1moe_cuda_ctx *c, const m1::LayerParams &p, cudaStream_t st) {
-    if (p.ntok == 1) return launch_layer<1>(c, p, st);
-    if (p.ntok == 2) return launch_layer<2>(c, p, st);
-    if (p.ntok <= 4) return launch_layer<4>(c, p, st);
-    return launch_layer<8>(c, p, st);
+    if (p.ntok == 1) return launch_layer<1, false>(c, p, st);
+    if (p.ntok == 2)
+        return m1::slot_path(2, p.h) ? launch_layer<2, true>(c, p, st) : launch_layer<2, false>(c, p, st);
+    if (p.ntok <= 4) return launch_layer<4, true>(c, p, st);
+    return launch_layer<8, true>(c, p, st);
 }
 
 // ---- router top-K without allocation (m1moe_cuda_router_topk_noalloc) ----
@@ -498,12 +497,13 @@ m1moe_status noalloc_setup(int dev, NoAllocDevice *&out) {
     return M1MOE_OK;
 }
 
-template <int NT>
+template <int NT, bool SL>
 m1moe_status launch_route_noalloc(m1::LayerParams p, int grid, cudaStream_t st) {
-    const size_t smem = plan_layer(p, grid, NT);
+    p.lparts = SL ? logit_parts(grid, p.E, p.ntok, p.h) : 1;
+    const size_t smem = plan_layer(p, grid, NT, SL);
     if (smem == 0 || smem > kMaxDynSmem)
         return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
-    M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT, SL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -515,7 +515,7 @@ m1moe_status launch_route_noalloc(m1::LayerParams p, int grid, cudaStream_t st) 
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, m1::k_moe_layer<NT>, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, m1::k_moe_layer<NT, SL>, p);
     if (e != cudaSuccess) return cuda_fail(e, "k_moe_layer (routing) launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return M1MOE_OK;
@@ -971,17 +971,16 @@ m1moe_status m1moe_cuda_router_topk_noalloc(const uint16_t *d_router, int32_t nu
     p.xlog = reinterpret_cast<unsigned long long *>(nd->scratch);
     p.nbox = 1;  // one shared box: the fixed scratch has no room for a box per CTA
     p.box_words = 0;
-    p.lparts = logit_parts(std::min(nd->num_sms, kNoAllocMaxCtas), E, B, h);
     p.epochs = reinterpret_cast<unsigned *>(nd->scratch + kNoAllocXlog);
     p.err = d_status ? d_status : reinterpret_cast<int *>(nd->scratch + kNoAllocXlog + kNoAllocEpochs);
     p.route_only = 1;
     cudaStream_t st = as_stream(stream);
     M1_CK(cudaMemsetAsync(p.err, 0, sizeof(int), st));
     const int grid = std::min(nd->num_sms, kNoAllocMaxCtas);
-    if (B == 1) return launch_route_noalloc<1>(p, grid, st);
-    if (B == 2) return launch_route_noalloc<2>(p, grid, st);
-    if (B <= 4) return launch_route_noalloc<4>(p, grid, st);
-    return launch_route_noalloc<8>(p, grid, st);
+    if (B == 1) return launch_route_noalloc<1, false>(p, grid, st);
+    if (B == 2) return launch_route_noalloc<2, false>(p, grid, st);
+    if (B <= 4) return launch_route_noalloc<4, true>(p, grid, st);
+    return launch_route_noalloc<8, true>(p, grid, st);
 }
 
 m1moe_status m1moe_cuda_moe_layer(m1moe_cuda_ctx *c, int32_t layer, const void *d_x,

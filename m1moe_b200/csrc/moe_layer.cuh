@@ -106,11 +106,12 @@ struct ItemRows {
 // for a token the expert does not see.  A gate/up item is then ONE row of a
 // tile for all of the expert's tokens; smaller batches keep the row-group
 // items above (with column slices for 1 and 2 tokens).
-__host__ __device__ constexpr bool slot_path(int nt) { return nt >= 4; }
+// The host takes the slot path for 4 and 8 tokens, and for 2 tokens when rows
+// are long (h >= 4096: the row-group items would hold a quarter of a row).
+__host__ __device__ constexpr bool slot_path(int nt, int h) { return nt >= 4 || (nt == 2 && h >= 4096); }
 
-__host__ __device__ constexpr int gu_items_per_tile(int nt, int gt, int nslices) {
-    return slot_path(nt) ? gt
-                         : (gt / 2 / (nt == 1 ? 2 : 1)) * nslices;  // row groups x slices
+__host__ __device__ constexpr int gu_items_per_tile(bool slot, int nt, int gt, int nslices) {
+    return slot ? gt : (gt / 2 / (nt == 1 ? 2 : 1)) * nslices;  // rows, or row groups x slices
 }
 
 // Relative cost of a unit of 8 gate/up rows of an expert with t tokens
@@ -332,14 +333,14 @@ __device__ __forceinline__ unsigned long long logit_key(float v, int e) {
     return ((unsigned long long)ord << 32) | (uint32_t)(0xFFFF - e);
 }
 
-template <int NT>
+template <bool SL>
 __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
                           unsigned long long *keys, float *parts, unsigned tag, const volatile int *abort) {
     const int tid = threadIdx.x;
     const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E;
     // a. collect the tagged (partial) logits: all of this thread's loads in
     //    flight at once; nw <= kMaxTok * kMaxExperts words
-    const int LP = slot_path(NT) ? p.lparts : 1, nw = nel * LP;
+    const int LP = SL ? p.lparts : 1, nw = nel * LP;
     constexpr int kPer = kMaxTok * kMaxExperts / 256;
     const unsigned long long *box = p.xlog + (size_t)(blockIdx.x % p.nbox) * p.box_words;
     bool ok = false;
@@ -364,7 +365,7 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
     }
     // b. the logit of (token, expert) element i (its parts summed in order)
     //    and its ranking key
-    if constexpr (slot_path(NT)) {
+    if constexpr (SL) {
         if (LP > 1) {
 #pragma unroll
             for (int j = 0; j < kPer; ++j)
@@ -579,7 +580,7 @@ __device__ __forceinline__ void add_words(float *dst, const float (&tot)[LR][NT]
 // in units of 8 rows so that row pairs (R, R+4) stay together; ntg gate/up
 // tiles (cut at multiples of GT, so a tile never crosses experts) and ntd =
 // nsub * nic down tiles (column-block runs, dn_run_end, per row chunk).
-template <int NT>
+template <bool SL>
 __device__ void route_geometry(const LayerParams &p, Ctl &ctl, Slots &sl, int blk) {
     RouteInfo &rs = ctl.route;
     const int lane = threadIdx.x & 31;
@@ -598,7 +599,7 @@ __device__ void route_geometry(const LayerParams &p, Ctl &ctl, Slots &sl, int bl
     }
     const int nU = __shfl_sync(0xffffffffu, incl, 31);
     __syncwarp();  // ulist complete
-    if constexpr (slot_path(NT)) {
+    if constexpr (SL) {
         // token slots of every distinct expert
         for (int u = lane; u < nU; u += 32) {
             unsigned tm = rs.tmask[rs.ulist[u]];
@@ -980,7 +981,7 @@ __device__ __forceinline__ void put_act(float *actf, int act_rows, int a, int t,
 }
 
 // ---------------------------------------------------------------- kernel ----
-template <int NT>
+template <int NT, bool SL>
 __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int RG = ItemRows<NT>::gu, PG = ItemRows<NT>::pairs, NPASS = ItemRows<NT>::passes;
@@ -1079,7 +1080,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     }
     const int nrows = i1 - i0;
     if (warp < 8) {
-        if constexpr (slot_path(NT)) {
+        if constexpr (SL) {
             // ---- phase 2: partial logits, straight from global memory ----
             // Work item (e, part): W_r[e] . x[t] over the part's 8-column blocks
             // [n8*part/P, n8*(part+1)/P) for every token; a thread takes token
@@ -1218,7 +1219,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         if (tid == 0) trace_event(p.trace, 0, 2);
         // ---- phase 3: route (warps 0..7 of every CTA) ----
         // partial logits are summed in the tile ring, idle until routing is done
-        const bool ok = route_cta<NT>(p, rs, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
+        const bool ok = route_cta<SL>(p, rs, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
         if (tid == 0) trace_event(p.trace, 0, 3);
         if (tid == 0) {
             if (ok) ctl.route_ok = 1;
@@ -1270,7 +1271,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             named_sync(3, 256 + 32);
             if (lane == 0) trace_event(p.trace, 0, 19);
             if (!p.route_only && ctl.route_ok) {
-                route_geometry<NT>(p, ctl, sl, blk);
+                route_geometry<SL>(p, ctl, sl, blk);
                 if (lane == 0) {
                     trace_event(p.trace, 0, 16);
                     if (ctl.ntg + ctl.ntd > 0) {
@@ -1318,7 +1319,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     const int a = ctl.a, b = ctl.b, ntg = ctl.ntg, ntd = ctl.ntd;
     const int a8 = a >> 3, ag = fdiv(a, p.fd_gs), gcb = p.gs >> 3;
     const int nslg = p.gu_nslices;
-    const int ipt_g = gu_items_per_tile(NT, GT, nslg);  // work items per gate/up tile
+    const int ipt_g = gu_items_per_tile(SL, NT, GT, nslg);  // work items per gate/up tile
     const int ipt_d = RC / (32 * DnRows<NT>::lane);  // work items per down tile
 
     if (warp == kConsumerWarps) {
@@ -1332,7 +1333,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     } else {
         // ================= consumers: gate/up =================
         const int ng_items = ntg * ipt_g;
-        if constexpr (slot_path(NT)) {
+        if constexpr (SL) {
             // item = one row of a tile, for all of its expert's token slots
             for (;;) {
                 const int q = grab(&ctl.next_gu);
@@ -1488,7 +1489,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             const int cb = i / NT, k = i % NT;
             const int R0 = a + 8 * cb, u = fdiv(R0, p.fd_I);
             // k: a token (row groups) or a token slot of expert u (slot path)
-            if (ctl.abort || (slot_path(NT) ? k >= sl.ute[u] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
+            if (ctl.abort || (SL ? k >= sl.ute[u] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
             const int gg = fdiv(a8 + cb, p.fd_gcb);
             const int c_lo = max(gg * gcb, a8) - a8, c_hi = min((gg + 1) * gcb, b >> 3) - a8;
             float m = 0.f;
@@ -1542,7 +1543,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             }
             return seen;
         };
-        if constexpr (slot_path(NT)) {
+        if constexpr (SL) {
             // Item as above; the chunk's tiles come expert by expert (a tile
             // never spans two), and each expert's run of tiles is summed per
             // token slot and added to the output once, weighted by the

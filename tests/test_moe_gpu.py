@@ -86,7 +86,7 @@ def _device_layer(E, h, I, seed):
     return synth.layer_image_device(E, h, I, 64, seed=seed, device="cuda").cpu().numpy()
 
 
-@pytest.mark.parametrize("B", [1, 4, 8])
+@pytest.mark.parametrize("B", [1, 2, 4, 8])
 def test_moe_layer_olmoe_shape(oracle_lib, B):
     """Config 1: h 2048, 64 experts, top-8, I 1024, no renormalisation."""
     h, I, E, K = 2048, 1024, 64, 8
@@ -95,9 +95,10 @@ def test_moe_layer_olmoe_shape(oracle_lib, B):
               seed=10 * B)
 
 
-@pytest.mark.parametrize("B", [1, 8])
+@pytest.mark.parametrize("B", [1, 2, 4, 8])
 def test_moe_layer_mixtral_shape(oracle_lib, B):
-    """Config 3 decode: h 4096, 8 experts, top-2 renormalised, I 14336."""
+    """Config 3 decode: h 4096, 8 experts, top-2 renormalised, I 14336 (batches
+    of 2 take the token-slot path here, the row-group path at h 2048)."""
     h, I, E, K = 4096, 14336, 8, 2
     img = _device_layer(E, h, I, 17)
     _run_case(oracle_lib, img, synth.router_weights(18, E, h), h=h, I=I, E=E, K=K, norm=True, B=B,

@@ -8,9 +8,10 @@
 //
 // One CTA per SM (cooperative launch: every CTA is resident, which the waits
 // on other CTAs need).  Phases:
-//   1. warps 8..24 stage x in shared memory as int16 chunks with per-chunk
-//      scales and exact fp32 sums (common.cuh) and initialise this CTA's rows
-//      of the output with the residual (or zero); meanwhile
+//   1. warps 8..24 initialise this CTA's rows of the output with the
+//      residual (or zero) and, once this CTA's logits are out, stage x in
+//      shared memory as int16 chunks with per-chunk scales and exact fp32
+//      sums (common.cuh); meanwhile
 //   2. warps 0..7 compute logits[t][e] = W_r[e] . x[t] for this CTA's experts
 //      straight from global memory (bf16 router upcast exactly, the caller's
 //      x, fp32 FMA, fixed reduction order), publish them as TAGGED words
@@ -1217,6 +1218,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             }
         }
         if (tid == 0) trace_event(p.trace, 0, 2);
+        named_arrive(6, kLayerThreads);  // this CTA's logits are out: x staging may start
         // ---- phase 3: route (warps 0..7 of every CTA) ----
         // partial logits are summed in the tile ring, idle until routing is done
         const bool ok = route_cta<SL>(p, rs, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
@@ -1256,6 +1258,10 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             __threadfence();
             st_release_u32(my_epoch, tag);
         }
+        // The router warps' loads of x and of the router rows go first: x
+        // staging (every CTA reading all of x at once) waits until this CTA's
+        // logits are published (barrier 6), overlapping the logit exchange.
+        named_sync(6, kLayerThreads);
         // x as int16 chunks (dp2a layout, common.cuh) with scales and exact sums
         for (int q = st; q < p.ntok * nch; q += nst) {
             const int t = q / nch, c = q - t * nch;

@@ -346,8 +346,8 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, bool slot) {
     p.fd_gs = m1::make_fastdiv(p.gs);
     p.fd_iptg = m1::make_fastdiv(m1::gu_items_per_tile(slot, nt, p.gu_tile_rows, p.gu_nslices));
     p.fd_nslg = m1::make_fastdiv(p.gu_nslices);
-    if (tl.rc % (32 * m1::dn_lane_rows(nt))) return 0;
-    p.fd_iptd = m1::make_fastdiv(tl.rc / (32 * m1::dn_lane_rows(nt)));
+    if (tl.rc % (32 * m1::dn_lane_rows(slot, nt))) return 0;
+    p.fd_iptd = m1::make_fastdiv(tl.rc / (32 * m1::dn_lane_rows(slot, nt)));
     // rows per CTA: an even split, or the cost-weighted one (route_geometry):
     // a CTA's cost share is at most ceil(total / grid) and a unit costs at
     // least beta + 1, so it gets at most share / (beta + 1) + 1 units

@@ -128,7 +128,6 @@ constexpr int kBalBeta = M1_BAL_BETA;
 struct RouteInfo {
     int idx[kMaxTok][kMaxTopK];    // top-K experts per token, descending
     float w[kMaxTok][kMaxTopK];    // their weights (renormalised if asked)
-    unsigned emask[kMaxExperts / 32];        // routed local experts (bit e)
     unsigned tmask[kMaxExperts];             // tokens routed to expert e
     unsigned char kof[kMaxExperts][kMaxTok];  // k of (expert e, token t)
     int ulist[kMaxPairs];          // distinct local experts, ascending
@@ -209,6 +208,7 @@ struct Ctl {
     int next_gu, next_dn;  // work-item counters
     int issued;            // tiles issued by the producer
     int a, b;              // this CTA's gate/up rows [a, b) of the distinct-expert row space
+    int range[2];          // cost-weighted split: this CTA's units [range[0], range[1])
     int ntg, ntd;          // gate/up and down tiles of this CTA
     int nsub;              // down tiles per row chunk (ntd = nsub * nic)
     int last;              // this CTA finished last (bf16 output)
@@ -223,8 +223,8 @@ struct Ctl {
 // Token slots of the distinct experts (slot path only; a shared-memory
 // region of its own, so that smaller batches keep the bytes for tiles).
 struct Slots {
-    unsigned char ute[kMaxPairs];            // tokens of distinct expert u
-    unsigned char utok[kMaxPairs][kMaxTok];  // its token slots: j-th token, ascending
+    unsigned char ute[kMaxExperts];            // tokens of expert e
+    unsigned char utok[kMaxExperts][kMaxTok];  // its token slots: j-th token, ascending
 };
 
 __device__ __forceinline__ bool is_local(const LayerParams &p, int e) {
@@ -335,7 +335,7 @@ __device__ __forceinline__ unsigned long long logit_key(float v, int e) {
 }
 
 template <bool SL>
-__device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
+__device__ bool route_cta(const LayerParams &p, RouteInfo &rs, Slots &sl, int *range, float *rlog,
                           unsigned long long *keys, float *parts, unsigned tag, const volatile int *abort) {
     const int tid = threadIdx.x;
     const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E;
@@ -398,14 +398,13 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
     if (!named_sync_and(2, 256, ok)) return false;
     if (tid == 0) trace_event(p.trace, 0, 12);
     // marks of token t's k-th expert: the caller's index output, and for a
-    // local expert its token mask, the token's k and the expert bit
+    // local expert its token mask and the token's k
     auto mark = [&](int t, int k) {
         const int e = rs.idx[t][k];
         if (p.user_idx && blockIdx.x == 0) p.user_idx[t * K + k] = e;
         if (is_local(p, e)) {
             atomicOr(&rs.tmask[e], 1u << t);
             rs.kof[e][t] = (unsigned char)k;
-            atomicOr(&rs.emask[e >> 5], 1u << (e & 31));
         }
     };
     // b. rank of every (token, expert): P threads per element, each
@@ -447,6 +446,70 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, float *rlog,
         mark(t, k);
     }
     named_sync(2, 256);
+    // d. one thread per expert e (E <= 256): on the slot path its token slots;
+    //    with the cost-weighted split (route_geometry), this CTA's range of
+    //    units -- a block scan of the costs beta + t of the routed local
+    //    experts in ascending order, and the thread whose expert holds a
+    //    cost target writes the unit there.  Done here by 256 threads rather
+    //    than by the producer warp alone, whose path leads to the first copy.
+    const int e = tid;
+    const unsigned tm = e < E ? rs.tmask[e] : 0u;
+    const int te = __popc(tm);
+    if constexpr (SL) {
+        if (te) {
+            unsigned m = tm;
+            int j = 0;
+            while (m) {
+                sl.utok[e][j++] = (unsigned char)(__ffs(m) - 1);
+                m &= m - 1;
+            }
+            sl.ute[e] = (unsigned char)te;
+        }
+    }
+    // the distinct local experts in ascending order (ulist, nU) and, with
+    // the cost-weighted split, this CTA's range: block scans of one per
+    // routed expert and of its cost
+    const int lane = tid & 31, warp = tid >> 5, n8 = p.I >> 3;
+    const int c = (p.bal_beta > 0 && te) ? p.bal_beta + te : 0, one = te ? 1 : 0;
+    int ci = c, ui = one;  // inclusive prefixes within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int yc = __shfl_up_sync(0xffffffffu, ci, o), yu = __shfl_up_sync(0xffffffffu, ui, o);
+        if (lane >= o) {
+            ci += yc;
+            ui += yu;
+        }
+    }
+    int *wt = reinterpret_cast<int *>(parts);  // warp totals (the ring is idle until routing ends)
+    if (lane == 31) {
+        wt[2 * warp] = ci;
+        wt[2 * warp + 1] = ui;
+    }
+    named_sync(2, 256);
+    int cpre = ci - c, upre = ui - one, ctot = 0, utot = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        const int wc = wt[2 * w], wu = wt[2 * w + 1];
+        if (w < warp) {
+            cpre += wc;
+            upre += wu;
+        }
+        ctot += wc;
+        utot += wu;
+    }
+    if (te) rs.ulist[upre] = e;
+    if (tid == 0) rs.nU = utot;
+    if (p.bal_beta > 0) {
+        // costs are ints: total * G < 2^31 (checked on the host)
+        const int total = ctot * n8, blk = blockIdx.x;
+        const int T[2] = {fdiv(total * blk, p.fd_G), fdiv(total * (blk + 1), p.fd_G)};
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            if (te && T[q] >= cpre * n8 && T[q] < (cpre + c) * n8)
+                range[q] = upre * n8 + (T[q] - cpre * n8 + c - 1) / c;
+            if (tid == 0 && T[q] >= total) range[q] = utot * n8;
+        }
+    }
     return true;
 }
 
@@ -540,12 +603,10 @@ __device__ __forceinline__ int dn_run_end(const LayerParams &p, int cb, int b8) 
 // load per column block and one vector atomic per token, and independent
 // dot-product chains; fewer for larger batches (registers: LR*NT of each of
 // Q, y and the totals).
-__host__ __device__ constexpr int dn_lane_rows(int nt) { return nt <= 2 ? 4 : (nt == 4 ? 2 : 1); }
+__host__ __device__ constexpr int dn_lane_rows(bool slot, int nt) {
+    return nt <= 2 ? (slot ? 2 : 4) : (nt == 4 ? 2 : 1);  // the slot path keeps two Q chains per row
+}
 
-template <int NT>
-struct DnRows {
-    static constexpr int lane = dn_lane_rows(NT);
-};
 
 // LR consecutive 32-bit words from shared memory (4*LR-byte aligned).
 template <int LR>
@@ -575,91 +636,30 @@ __device__ __forceinline__ void add_words(float *dst, const float (&tot)[LR][NT]
 }
 
 // ------------------------------------------------------------ producer ----
-// One warp, right after routing: the distinct local experts (ascending, from
-// the expert bit mask) and this CTA's share of the work.  Gate/up rows [a, b)
+// One warp, right after routing: this CTA's share of the work.  Gate/up rows [a, b)
 // of the distinct-expert row space (expert u's rows are u*I .. u*I+I-1), cut
 // in units of 8 rows so that row pairs (R, R+4) stay together; ntg gate/up
 // tiles (cut at multiples of GT, so a tile never crosses experts) and ntd =
 // nsub * nic down tiles (column-block runs, dn_run_end, per row chunk).
-template <bool SL>
-__device__ void route_geometry(const LayerParams &p, Ctl &ctl, Slots &sl, int blk) {
+__device__ void route_geometry(const LayerParams &p, Ctl &ctl, int blk) {
     RouteInfo &rs = ctl.route;
     const int lane = threadIdx.x & 31;
-    unsigned m = lane < kMaxExperts / 32 ? rs.emask[lane] : 0u;
-    const int c = __popc(m);
-    int incl = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    int pos = incl - c;
-    while (m) {
-        rs.ulist[pos++] = lane * 32 + __ffs(m) - 1;
-        m &= m - 1;
-    }
-    const int nU = __shfl_sync(0xffffffffu, incl, 31);
-    __syncwarp();  // ulist complete
-    if constexpr (SL) {
-        // token slots of every distinct expert
-        for (int u = lane; u < nU; u += 32) {
-            unsigned tm = rs.tmask[rs.ulist[u]];
-            int j = 0;
-            while (tm) {
-                sl.utok[u][j++] = (unsigned char)(__ffs(tm) - 1);
-                tm &= tm - 1;
-            }
-            sl.ute[u] = (unsigned char)j;
-        }
-    }
+    const int nU = rs.nU;  // the distinct local experts are in ulist (route_cta)
     const int n8 = p.I >> 3;  // units of 8 rows per expert
-    int ua = 0, ub = 0;       // this CTA's units [ua, ub)
+    int ua, ub;               // this CTA's units [ua, ub)
     if (p.bal_beta == 0) {
         const int units = nU * n8;  // units * G < 2^31 (kMaxPairs, I, kMaxCtas)
         ua = fdiv(units * blk, p.fd_G);
         ub = fdiv(units * (blk + 1), p.fd_G);
     } else {
-        // cost-weighted: unit i of expert u costs c_u = beta + t_u; lane l
-        // holds experts 4l..4l+3 (nU <= kMaxPairs = 128).  The boundary for a
-        // cost target T is the first unit whose preceding cost reaches T, so
-        // neighbouring CTAs agree on it.
-        int cu[4], cs = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int u = 4 * lane + i;
-            cu[i] = u < nU ? p.bal_beta + __popc(rs.tmask[rs.ulist[u]]) : 0;
-            cs += cu[i];
-        }
-        int ci = cs;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, ci, o);
-            if (lane >= o) ci += y;
-        }
-        // costs are ints: total * G < 2^31 (checked on the host)
-        const int pre = (ci - cs) * n8;  // cost before this lane's experts
-        const int total = __shfl_sync(0xffffffffu, ci, 31) * n8;
-        auto boundary = [&](int T) {
-            if (T >= total) return nU * n8;
-            const bool own = T >= pre && T < pre + cs * n8;
-            const unsigned who = __ballot_sync(0xffffffffu, own);
-            int unit = 0;
-            if (own) {
-                int c0 = pre;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int c1 = c0 + cu[i] * n8;
-                    if (T >= c0 && T < c1) unit = (4 * lane + i) * n8 + (T - c0 + cu[i] - 1) / cu[i];
-                    c0 = c1;
-                }
-            }
-            return __shfl_sync(0xffffffffu, unit, __ffs(who) - 1);
-        };
-        ua = boundary(fdiv(total * blk, p.fd_G));
-        ub = boundary(fdiv(total * (blk + 1), p.fd_G));
+        // cost-weighted: unit i of expert u costs c_u = beta + t_u, and the
+        // boundary for a cost target T is the first unit whose preceding
+        // cost reaches T, so that neighbouring CTAs agree on it (computed by
+        // the router warps, route_cta)
+        ua = ctl.range[0];
+        ub = ctl.range[1];
     }
     if (lane == 0) {
-        rs.nU = nU;
         int a = ua * 8, b = ub * 8;
         if (b - a > p.gu_rows_max) {  // cannot happen (host bound); never overrun the buffers
             set_abort(ctl, p.err);
@@ -1088,7 +1088,6 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             // tid % NT of blocks tid / NT, +256/NT, ...  Fixed order throughout:
             // lanes of one token by xor shuffles, then the 8 warps in order.
             for (int e = tid; e < p.E; e += 256) rs.tmask[e] = 0u;
-            if (tid < kMaxExperts / 32) rs.emask[tid] = 0u;
             const int P = p.lparts, nitems = p.E * P, n8 = h / 8;
             constexpr int LT = NT == 1 ? 0 : (NT == 2 ? 1 : (NT == 4 ? 2 : 3));
             const int tt = tid & (NT - 1);
@@ -1151,7 +1150,6 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             // ---- phase 2: logits of this CTA's experts, straight from global memory ----
             // (batches of 1 and 2: one part per logit, a CTA per expert)
             for (int e = tid; e < p.E; e += 256) rs.tmask[e] = 0u;
-            if (tid < kMaxExperts / 32) rs.emask[tid] = 0u;
             const int nmine = (p.E > blk) ? (p.E - blk + G - 1) / G : 0;
             for (int m = 0; m < nmine; ++m) {
                 const int e = blk + m * G;
@@ -1221,7 +1219,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         named_arrive(6, kLayerThreads);  // this CTA's logits are out: x staging may start
         // ---- phase 3: route (warps 0..7 of every CTA) ----
         // partial logits are summed in the tile ring, idle until routing is done
-        const bool ok = route_cta<SL>(p, rs, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
+        const bool ok = route_cta<SL>(p, rs, sl, ctl.range, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
         if (tid == 0) trace_event(p.trace, 0, 3);
         if (tid == 0) {
             if (ok) ctl.route_ok = 1;
@@ -1277,7 +1275,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             named_sync(3, 256 + 32);
             if (lane == 0) trace_event(p.trace, 0, 19);
             if (!p.route_only && ctl.route_ok) {
-                route_geometry<SL>(p, ctl, sl, blk);
+                route_geometry(p, ctl, blk);
                 if (lane == 0) {
                     trace_event(p.trace, 0, 16);
                     if (ctl.ntg + ctl.ntd > 0) {
@@ -1326,7 +1324,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     const int a8 = a >> 3, ag = fdiv(a, p.fd_gs), gcb = p.gs >> 3;
     const int nslg = p.gu_nslices;
     const int ipt_g = gu_items_per_tile(SL, NT, GT, nslg);  // work items per gate/up tile
-    const int ipt_d = RC / (32 * DnRows<NT>::lane);  // work items per down tile
+    const int ipt_d = RC / (32 * dn_lane_rows(SL, NT));  // work items per down tile
 
     if (warp == kConsumerWarps) {
         // ================= producer (warp 24) =================
@@ -1350,7 +1348,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 if (q == 0 && lane == 0) trace_event(p.trace, 0, 5);
                 const StageGeo g = ctl.geo[s];
                 if (rr < g.nr)
-                    gu_row_slots<NT>(sl.ute[g.u], p, ring + g.off + (size_t)rr * tl.pr, sl.utok[g.u], xq, xsc,
+                    gu_row_slots<NT>(sl.ute[rs.ulist[g.u]], p, ring + g.off + (size_t)rr * tl.pr, sl.utok[rs.ulist[g.u]], xq, xsc,
                                      xsum, actf, p.act_cb * 8, g.u * I + g.r0 + rr - a);
                 release_item(empty, ctl, s, ipt_g);
             }
@@ -1495,7 +1493,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             const int cb = i / NT, k = i % NT;
             const int R0 = a + 8 * cb, u = fdiv(R0, p.fd_I);
             // k: a token (row groups) or a token slot of expert u (slot path)
-            if (ctl.abort || (SL ? k >= sl.ute[u] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
+            if (ctl.abort || (SL ? k >= sl.ute[rs.ulist[u]] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
             const int gg = fdiv(a8 + cb, p.fd_gcb);
             const int c_lo = max(gg * gcb, a8) - a8, c_hi = min((gg + 1) * gcb, b >> 3) - a8;
             float m = 0.f;
@@ -1526,7 +1524,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         // nibble pairs of each shared by the tokens; per group:
         // y += s*sa*Q + b*X; per tile (one expert): total += w_k * y.  One
         // LR-wide atomic per lane and token at the end.
-        constexpr int LR = DnRows<NT>::lane;
+        constexpr int LR = dn_lane_rows(SL, NT);
         const int nsub = ctl.nsub;  // down tiles per row chunk
         const int nd_items = (ctl.abort || ntd == 0) ? 0 : nic * ipt_d;
         float *dst = p.out_acc ? p.acc : reinterpret_cast<float *>(p.out);
@@ -1569,11 +1567,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 int cur = -1;  // distinct expert whose sums y holds
                 auto flush_expert = [&]() -> bool {
                     if (!see_epochs()) return false;
-                    const int e = rs.ulist[cur], te = sl.ute[cur];
+                    const int e = rs.ulist[cur], te = sl.ute[e];
 #pragma unroll
                     for (int j = 0; j < NT; ++j) {
                         if (j < te) {
-                            const int t = sl.utok[cur][j];
+                            const int t = sl.utok[e][j];
                             const float wk = rs.w[t][rs.kof[e][t]];
                             float v[LR][1];
 #pragma unroll
@@ -1603,7 +1601,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                         cur = g.u;
                     }
                     const uint32_t *Wt = reinterpret_cast<const uint32_t *>(ring + g.off) + ri;
-                    dn_tile_slots<LR, NT>(sl.ute[g.u], p, y, Wt, Wt + (size_t)g.nr * RC, g, act, xseg, a8, ag);
+                    dn_tile_slots<LR, NT>(sl.ute[rs.ulist[g.u]], p, y, Wt, Wt + (size_t)g.nr * RC, g, act, xseg, a8, ag);
                     release_item(empty, ctl, s, ipt_d);
                 }
                 if (ok && cur >= 0) ok = flush_expert();

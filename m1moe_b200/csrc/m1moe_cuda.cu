@@ -172,9 +172,10 @@ struct m1moe_cuda_ctx {
     uint8_t *table = nullptr;     // [layers][ne] tiled blocks
     uint16_t *router = nullptr;   // [layers][E][h]
     std::vector<uint8_t> layer_loaded, router_loaded;
-    unsigned long long *xlog = nullptr;  // [nbox][box_words] tagged partial logits, a box per CTA
-    int nbox = 0;                        // = the layer kernel's grid
-    int box_words = 0;                   // logit_box_words(nbox, E, h)
+    unsigned long long *xlog = nullptr;  // [nbox][box_words] tagged partial logits
+    int grid = 0;                        // the layer kernel's grid (one CTA per SM)
+    int nbox = 0;                        // logit boxes (CTA c polls box c % nbox)
+    int box_words = 0;                   // logit_box_words(grid, E, h)
     float *acc = nullptr;                // [max_batch][h] fp32 sums for bf16 output
     int *done = nullptr;                 // CTAs finished with their atomics (bf16 output)
     unsigned *epochs = nullptr;          // per-CTA call counters (moe_layer.cuh)
@@ -250,6 +251,10 @@ void free_ctx(m1moe_cuda_ctx *c) {
     delete c;
 }
 
+#ifndef M1_BOX_SHARE
+#define M1_BOX_SHARE 4
+#endif
+constexpr int kBoxShare = M1_BOX_SHARE;  // CTAs polling one logit box
 constexpr size_t kEpochBytes = (size_t)m1::kMaxCtas * m1::kEpochStride * sizeof(unsigned);
 
 // Partial sums per router logit: h is cut into `parts` column ranges, each
@@ -415,8 +420,8 @@ size_t plan_layer(m1::LayerParams &p, int grid, int nt, bool slot) {
 
 template <int NT, bool SL>
 m1moe_status launch_layer(m1moe_cuda_ctx *c, m1::LayerParams p, cudaStream_t st) {
-    const int grid = c->nbox;  // one CTA per SM, each with its own logit box
-    p.lparts = SL ? logit_parts(grid, p.E, p.ntok, p.h) : 1;
+    const int grid = c->grid;  // one CTA per SM
+    p.lparts = SL ? logit_parts(grid, p.E, NT, p.h) : 1;  // slot path: boxes padded to NT tokens
     const size_t smem = plan_layer(p, grid, NT, SL);
     if (smem == 0 || smem > kMaxDynSmem)
         return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
@@ -499,7 +504,7 @@ m1moe_status noalloc_setup(int dev, NoAllocDevice *&out) {
 
 template <int NT, bool SL>
 m1moe_status launch_route_noalloc(m1::LayerParams p, int grid, cudaStream_t st) {
-    p.lparts = SL ? logit_parts(grid, p.E, p.ntok, p.h) : 1;
+    p.lparts = SL ? logit_parts(grid, p.E, NT, p.h) : 1;
     const size_t smem = plan_layer(p, grid, NT, SL);
     if (smem == 0 || smem > kMaxDynSmem)
         return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
@@ -699,8 +704,9 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     c->layer_loaded.assign(g.num_layers, 0);
     c->router_loaded.assign(g.num_layers, 0);
     c->num_sms = sm_count();
-    c->nbox = std::min(c->num_sms, m1::kMaxCtas);
-    c->box_words = logit_box_words(c->nbox, g.num_experts, g.hidden_dim);
+    c->grid = std::min(c->num_sms, m1::kMaxCtas);
+    c->nbox = (c->grid + kBoxShare - 1) / kBoxShare;
+    c->box_words = logit_box_words(c->grid, g.num_experts, g.hidden_dim);
     const size_t B = g.max_batch, E = g.num_experts, K = g.top_k;
     cudaError_t e;
 #define M1_ALLOC(ptr, bytes)                                        \

@@ -252,6 +252,13 @@ __device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned l
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+// Two adjacent tagged words in one 16-byte store (each 64-bit element is
+// single-copy atomic on its own, which is all a reader relies on).
+__device__ __forceinline__ void st_relaxed_v2_u64(unsigned long long *p, unsigned long long a,
+                                                  unsigned long long b) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
 __device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -334,16 +341,18 @@ __device__ __forceinline__ unsigned long long logit_key(float v, int e) {
     return ((unsigned long long)ord << 32) | (uint32_t)(0xFFFF - e);
 }
 
-template <bool SL>
+template <int NT, bool SL>
 __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, Slots &sl, int *range, float *rlog,
                           unsigned long long *keys, float *parts, unsigned tag, const volatile int *abort) {
     const int tid = threadIdx.x;
     const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E;
     // a. collect the tagged (partial) logits: all of this thread's loads in
-    //    flight at once; nw <= kMaxTok * kMaxExperts words
-    const int LP = SL ? p.lparts : 1, nw = nel * LP;
+    //    flight at once.  Slot path: word (e, part, t) at (e*LP + part)*NT + t,
+    //    t < ntok; otherwise word (t, e) at t*E + e.  nw <= kMaxTok * kMaxExperts.
+    const int LP = SL ? p.lparts : 1, nw = SL ? E * LP * NT : nel;
     constexpr int kPer = kMaxTok * kMaxExperts / 256;
     const unsigned long long *box = p.xlog + (size_t)(blockIdx.x % p.nbox) * p.box_words;
+    auto used = [&](int i) { return i < nw && (!SL || (i & (NT - 1)) < ntok); };
     bool ok = false;
     unsigned long long w[kPer];
     for (uint32_t it = 0, nap = 32; it < kWaitLimit; ++it) {
@@ -351,11 +360,11 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, Slots &sl, int *r
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
             const int i = tid + 256 * j;
-            if (i < nw) w[j] = ld_relaxed_u64(box + i);
+            if (used(i)) w[j] = ld_relaxed_u64(box + i);
         }
 #pragma unroll
         for (int j = 0; j < kPer; ++j)
-            if (tid + 256 * j < nw) all = all && (unsigned)(w[j] >> 32) == tag;
+            if (used(tid + 256 * j)) all = all && (unsigned)(w[j] >> 32) == tag;
         if (all) {
             ok = true;
             break;
@@ -364,25 +373,36 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, Slots &sl, int *r
         __nanosleep(nap);
         nap = min(nap * 2, 256u);
     }
-    // b. the logit of (token, expert) element i (its parts summed in order)
-    //    and its ranking key
+    // b. the logit of (token, expert) element t*E + e (its parts summed in
+    //    order) and its ranking key
+    auto put = [&](int t, int e, float v) {
+        rlog[t * E + e] = v;
+        keys[t * E + e] = logit_key(v, e);
+    };
     if constexpr (SL) {
         if (LP > 1) {
 #pragma unroll
             for (int j = 0; j < kPer; ++j)
-                if (tid + 256 * j < nw) parts[tid + 256 * j] = __uint_as_float((uint32_t)w[j]);
+                if (used(tid + 256 * j)) parts[tid + 256 * j] = __uint_as_float((uint32_t)w[j]);
             named_sync(2, 256);
             for (int i = tid; i < nel; i += 256) {
+                int t = 0, e = i;
+                while (e >= E) {
+                    e -= E;
+                    ++t;
+                }
                 float v = 0.f;
-                for (int q = 0; q < LP; ++q) v += parts[i * LP + q];
-                int e = i;
-                while (e >= E) e -= E;
-                rlog[i] = v;
-                keys[i] = logit_key(v, e);
+                for (int q = 0; q < LP; ++q) v += parts[(e * LP + q) * NT + t];
+                put(t, e, v);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int i = tid + 256 * j;
+                if (used(i)) put(i & (NT - 1), i / NT, __uint_as_float((uint32_t)w[j]));
             }
         }
-    }
-    if (LP == 1) {
+    } else {
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
             const int i = tid + 256 * j;
@@ -1138,11 +1158,13 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                         for (int w = 0; w < 8; ++w) s += lpart[w * kMaxTok + t];
                     sv[t] = __float_as_uint(s);
                 }
+                // box layout [e][part][t], t padded to NT: an item's tokens
+                // are NT adjacent words, written with 16-byte stores
                 for (int bx = tid; bx < p.nbox; bx += 256) {
-                    unsigned long long *box = p.xlog + (size_t)bx * p.box_words + (size_t)e * P + part;
+                    unsigned long long *box = p.xlog + (size_t)bx * p.box_words + (size_t)item * NT;
     #pragma unroll
-                    for (int t = 0; t < NT; ++t)
-                        if (t < p.ntok) st_relaxed_u64(box + (size_t)t * p.E * P, tagged(tag, sv[t]));
+                    for (int t = 0; t < NT; t += 2)
+                        st_relaxed_v2_u64(box + t, tagged(tag, sv[t]), tagged(tag, sv[t + 1]));
                 }
                 named_sync(2, 256);
             }
@@ -1219,7 +1241,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         named_arrive(6, kLayerThreads);  // this CTA's logits are out: x staging may start
         // ---- phase 3: route (warps 0..7 of every CTA) ----
         // partial logits are summed in the tile ring, idle until routing is done
-        const bool ok = route_cta<SL>(p, rs, sl, ctl.range, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
+        const bool ok = route_cta<NT, SL>(p, rs, sl, ctl.range, rlog, keys, reinterpret_cast<float *>(ring), tag, vabort);
         if (tid == 0) trace_event(p.trace, 0, 3);
         if (tid == 0) {
             if (ok) ctl.route_ok = 1;

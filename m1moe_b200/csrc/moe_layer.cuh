@@ -427,32 +427,53 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, Slots &sl, int *r
             rs.kof[e][t] = (unsigned char)k;
         }
     };
-    // b. rank of every (token, expert): P threads per element, each
-    //    counting the keys above it in one slice of the token's E keys
-    int lp = 0;
-    while (lp < 5 && (nel << (lp + 1)) <= 256) ++lp;
-    const int P = 1 << lp;
-    for (int base = 0; base < (nel << lp); base += 256) {
-        const int gidx = base + tid, i = gidx >> lp, part = gidx & (P - 1);
-        int cnt = 0, t = 0, e = i;
-        if (i < nel) {
-            while (e >= E) {
-                e -= E;
-                ++t;
-            }
+    // b. rank of every (token, expert).  Many tokens over at most 64 experts
+    //    (slot path, more than 256 elements): a warp per token holds its keys
+    //    in registers, two per lane, and counts the larger ones over 32
+    //    shuffle rounds.  Otherwise P threads per element, each counting the
+    //    keys above it in one slice of the token's E keys.
+    if (SL && E <= 64 && nel > 256) {
+        const int lane = tid & 31;
+        for (int t = tid >> 5; t < ntok; t += 8) {
             const unsigned long long *kt = keys + (size_t)t * E;
-            const unsigned long long ki = kt[e];
-            // four independent loads in flight per round (a plain loop waits
-            // out each shared-memory load in turn)
-            int f = part;
-            for (; f + 3 * P < E; f += 4 * P) {
-                const unsigned long long k0 = kt[f], k1 = kt[f + P], k2 = kt[f + 2 * P], k3 = kt[f + 3 * P];
-                cnt += (k0 > ki ? 1 : 0) + (k1 > ki ? 1 : 0) + (k2 > ki ? 1 : 0) + (k3 > ki ? 1 : 0);
+            // absent slots hold 0, below every key (a key's low bits hold 0xFFFF - e)
+            const unsigned long long k0 = lane < E ? kt[lane] : 0ull, k1 = lane + 32 < E ? kt[lane + 32] : 0ull;
+            int c0 = 0, c1 = 0;
+#pragma unroll 8
+            for (int j = 0; j < 32; ++j) {
+                const unsigned long long a = __shfl_sync(0xffffffffu, k0, j), b = __shfl_sync(0xffffffffu, k1, j);
+                c0 += (a > k0 ? 1 : 0) + (b > k0 ? 1 : 0);
+                c1 += (a > k1 ? 1 : 0) + (b > k1 ? 1 : 0);
             }
-            for (; f < E; f += P) cnt += kt[f] > ki ? 1 : 0;
+            if (lane < E && c0 < K) rs.idx[t][c0] = lane;
+            if (lane + 32 < E && c1 < K) rs.idx[t][c1] = lane + 32;
         }
-        for (int o = 1; o < P; o <<= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-        if (i < nel && part == 0 && cnt < K) rs.idx[t][cnt] = e;
+    } else {
+        int lp = 0;
+        while (lp < 5 && (nel << (lp + 1)) <= 256) ++lp;
+        const int P = 1 << lp;
+        for (int base = 0; base < (nel << lp); base += 256) {
+            const int gidx = base + tid, i = gidx >> lp, part = gidx & (P - 1);
+            int cnt = 0, t = 0, e = i;
+            if (i < nel) {
+                while (e >= E) {
+                    e -= E;
+                    ++t;
+                }
+                const unsigned long long *kt = keys + (size_t)t * E;
+                const unsigned long long ki = kt[e];
+                // four independent loads in flight per round (a plain loop waits
+                // out each shared-memory load in turn)
+                int f = part;
+                for (; f + 3 * P < E; f += 4 * P) {
+                    const unsigned long long k0 = kt[f], k1 = kt[f + P], k2 = kt[f + 2 * P], k3 = kt[f + 3 * P];
+                    cnt += (k0 > ki ? 1 : 0) + (k1 > ki ? 1 : 0) + (k2 > ki ? 1 : 0) + (k3 > ki ? 1 : 0);
+                }
+                for (; f < E; f += P) cnt += kt[f] > ki ? 1 : 0;
+            }
+            for (int o = 1; o < P; o <<= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+            if (i < nel && part == 0 && cnt < K) rs.idx[t][cnt] = e;
+        }
     }
     named_sync(2, 256);
     if (tid == 0) trace_event(p.trace, 0, 13);

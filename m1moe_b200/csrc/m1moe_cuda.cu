@@ -184,9 +184,11 @@ struct m1moe_cuda_ctx {
     uint8_t *staging = nullptr;   // device staging for repacking host layer images
     size_t staging_bytes = 0;
     // synchronous host-buffer path
-    float *hx = nullptr, *hres = nullptr, *hout = nullptr;
-    int *hidx = nullptr;
-    float *hw = nullptr;
+    // m1moe_cuda_moe_layer_host: device inputs [x | residual] and outputs
+    // [out | idx | w], each laid out per call so that one copy moves them,
+    // and a pinned host mirror of both
+    float *hin = nullptr, *hio = nullptr;
+    void *hpin = nullptr;
     cudaStream_t stream = nullptr;  // for the *_host calls and staging copies
     void *pinned[2] = {nullptr, nullptr};
     cudaEvent_t staged[2] = {nullptr, nullptr};
@@ -231,11 +233,9 @@ void free_ctx(m1moe_cuda_ctx *c) {
     cudaFree(c->epochs);
     cudaFree(c->err);
     cudaFree(c->staging);
-    cudaFree(c->hx);
-    cudaFree(c->hres);
-    cudaFree(c->hout);
-    cudaFree(c->hidx);
-    cudaFree(c->hw);
+    cudaFree(c->hin);
+    cudaFree(c->hio);
+    if (c->hpin) cudaFreeHost(c->hpin);
     for (void *q : {(void *)c->pf_idx, (void *)c->pf_tok_slot, (void *)c->pf_slot_tok,
                     (void *)c->pf_ntiles, (void *)c->pf_w, (void *)c->pf_ypart, (void *)c->pf_tiles,
                     (void *)c->pf_xg, (void *)c->pf_act})
@@ -723,12 +723,15 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     M1_ALLOC(c->done, 4);
     M1_ALLOC(c->epochs, kEpochBytes);
     M1_ALLOC(c->err, 4);
-    M1_ALLOC(c->hx, B * g.hidden_dim * 4);
-    M1_ALLOC(c->hres, B * g.hidden_dim * 4);
-    M1_ALLOC(c->hout, B * g.hidden_dim * 4);
-    M1_ALLOC(c->hidx, B * K * 4);
-    M1_ALLOC(c->hw, B * K * 4);
+    M1_ALLOC(c->hin, 2 * B * g.hidden_dim * 4);
+    M1_ALLOC(c->hio, B * g.hidden_dim * 4 + 2 * B * K * 4);
 #undef M1_ALLOC
+    e = cudaHostAlloc(&c->hpin, 3 * B * g.hidden_dim * 4 + 2 * B * K * 4, cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+        m1moe_status st_ = cuda_fail(e, "cudaHostAlloc host-call staging");
+        free_ctx(c);
+        return st_;
+    }
     e = cudaMemset(c->err, 0, 4);
     if (e == cudaSuccess) e = clear_exchange(c);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
@@ -1177,17 +1180,27 @@ m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *c, int32_t layer, const f
     if (B < 1 || B > c->cfg.max_batch)
         return fail(M1MOE_ERR_INVALID_ARG, "batch %d outside [1,%d]", B, c->cfg.max_batch);
     DeviceGuard dg(c->cfg.device);
-    const size_t hb = (size_t)B * c->cfg.hidden_dim * 4, kb = (size_t)B * c->cfg.top_k * 4;
-    M1_CK(cudaMemcpyAsync(c->hx, h_x, hb, cudaMemcpyHostToDevice, c->stream));
-    if (h_res) M1_CK(cudaMemcpyAsync(c->hres, h_res, hb, cudaMemcpyHostToDevice, c->stream));
-    m1moe_status st = m1moe_cuda_moe_layer(c, layer, c->hx, M1MOE_DTYPE_F32,
-                                           h_res ? c->hres : nullptr, M1MOE_DTYPE_F32, c->hout,
-                                           M1MOE_DTYPE_F32, B, c->hidx, c->hw, c->stream);
+    const size_t n = (size_t)B * c->cfg.hidden_dim, hb = n * 4, kb = (size_t)B * c->cfg.top_k * 4;
+    // one copy each way through the pinned mirror: x and the residual in,
+    // out, indices and weights back (each host-to-device or device-to-host
+    // copy costs a few microseconds of its own on the stream)
+    float *pin_in = static_cast<float *>(c->hpin);
+    float *pin_out = pin_in + 2 * n;
+    memcpy(pin_in, h_x, hb);
+    if (h_res) memcpy(pin_in + n, h_res, hb);
+    M1_CK(cudaMemcpyAsync(c->hin, pin_in, h_res ? 2 * hb : hb, cudaMemcpyHostToDevice, c->stream));
+    float *d_out = c->hio;
+    int32_t *d_idx = reinterpret_cast<int32_t *>(d_out + n);
+    float *d_w = reinterpret_cast<float *>(d_idx) + (size_t)B * c->cfg.top_k;
+    m1moe_status st = m1moe_cuda_moe_layer(c, layer, c->hin, M1MOE_DTYPE_F32,
+                                           h_res ? c->hin + n : nullptr, M1MOE_DTYPE_F32, d_out,
+                                           M1MOE_DTYPE_F32, B, d_idx, d_w, c->stream);
     if (st) return st;
-    M1_CK(cudaMemcpyAsync(h_out, c->hout, hb, cudaMemcpyDeviceToHost, c->stream));
-    if (h_idx) M1_CK(cudaMemcpyAsync(h_idx, c->hidx, kb, cudaMemcpyDeviceToHost, c->stream));
-    if (h_w) M1_CK(cudaMemcpyAsync(h_w, c->hw, kb, cudaMemcpyDeviceToHost, c->stream));
+    M1_CK(cudaMemcpyAsync(pin_out, d_out, hb + 2 * kb, cudaMemcpyDeviceToHost, c->stream));
     M1_CK(cudaStreamSynchronize(c->stream));
+    memcpy(h_out, pin_out, hb);
+    if (h_idx) memcpy(h_idx, pin_out + n, kb);
+    if (h_w) memcpy(h_w, reinterpret_cast<const uint8_t *>(pin_out + n) + kb, kb);
     return M1MOE_OK;
 }
 

@@ -209,6 +209,41 @@ def test_router_topk_ties_lowest_index():
     blk2.close()
 
 
+def test_router_topk_ties_many_tokens():
+    """Batch 8 over 64 experts (the warp-per-token ranking of the token-slot
+    kernel): exactly tied scores still leave in ascending expert order, and
+    each token's experts come in descending score."""
+    from m1moe_b200 import MoEBlock
+    h, E, K, B = 128, 64, 8, 8
+    router = synth.router_weights(3, E, h)
+    tie = (4, 9, 17, 40, 63)
+    for e in tie[1:]:
+        router[e] = router[tie[0]]
+    x = synth.hidden_states(4, B, h)
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=64, num_experts=E, top_k=K, num_layers=1,
+                   max_batch=B)
+    blk.load_router(0, router)
+    idx, w, scores = blk.route(0, _bf16_dev(x))
+    idx, sc = idx.cpu().numpy(), scores.cpu().numpy()
+    for t in range(B):
+        assert len(set(idx[t].tolist())) == K
+        s_t = sc[t][idx[t]]
+        assert np.all(s_t[:-1] >= s_t[1:])  # descending
+        assert len(set(sc[t][list(tie)].tolist())) == 1  # the tie is exact on the device
+        tied = [e for e in idx[t].tolist() if e in tie]
+        assert tied == sorted(tied)
+        # every expert left out scores no higher than the K-th
+        assert sc[t].max(initial=-1.0, where=~np.isin(np.arange(E), idx[t])) <= s_t[-1]
+    # all-equal scores: the K lowest indices, ascending, for every token
+    blk2 = MoEBlock(hidden_dim=h, intermediate_dim=64, num_experts=E, top_k=K, num_layers=1,
+                    max_batch=B)
+    blk2.load_router(0, np.tile(router[0], (E, 1)))
+    idx2, _, _ = blk2.route(0, _bf16_dev(x))
+    assert idx2.cpu().numpy().tolist() == [list(range(K))] * B
+    blk.close()
+    blk2.close()
+
+
 def test_moe_layer_not_loaded_is_an_error():
     from m1moe_b200 import M1MoECudaError, MoEBlock
     blk = MoEBlock(hidden_dim=128, intermediate_dim=64, num_experts=4, top_k=2, num_layers=2)

@@ -18,10 +18,12 @@
 //      (below) and
 //   3. route every token from all logits (identical in every CTA,
 //      deterministic): top-K by rank (descending, ties to the lower index),
-//      distinct local experts; the softmax weights (with optional
-//      renormalisation) are computed while the first copies are in flight;
+//      the distinct local experts, their token slots and this CTA's share of
+//      the rows; the softmax weights (with optional renormalisation) are
+//      computed while the first copies are in flight;
 //   4. the routed experts' gate/up rows, concatenated, are split over the CTAs
-//      in runs of 8 rows.  A producer warp streams this CTA's gate/up tiles and
+//      in runs of 8 rows (evenly for one token, else by the cost beta + tokens
+//      of each expert's rows).  A producer warp streams this CTA's gate/up tiles and
 //      then the matching COLUMNS of the down matrices (split-K; the table
 //      stores them column-block major, tiled_layout.cuh) through a ring of
 //      shared-memory stages, one or two bulk copies per tile.  24 consumer

@@ -23,8 +23,16 @@
  *    nibble b of word w = column 8w+b, then S and B as bf16[rows][cols/gs];
  *    dequant w = q*S + B.  One expert block is
  *    [gateW|gateS|gateB|upW|upS|upB|downW|downS|downB] (ModelSpec.swift:36-52).
- *  - Matvec arithmetic is fp32 (fp32 FMA accumulation); activations may be
- *    passed as f32 or bf16 and outputs written as f32 or bf16.
+ *  - Decode arithmetic (matvec and MoE block): activations are quantised to
+ *    int16 per 32-column chunk of x (gate/up) or per group of SwiGLU
+ *    activations (down), multiplied with the int4 nibbles by dp2a into
+ *    int32 per chunk or group, and scaled in fp32 as s*s_x*Q + b*X (s, b the
+ *    group's bf16 scale and bias, s_x the chunk's scale, X its exact fp32
+ *    sum); sums over chunks, groups and experts are fp32.  Results agree with
+ *    the reference's fp32 FMA loop within 1e-3 of the output's L2 norm.
+ *    Activations may be passed as f32 or bf16 and outputs written as f32 or
+ *    bf16.  The dense decode step (m1moe_dense_*) computes bf16 weights x
+ *    f32 activations with fp32 FMA accumulation.
  */
 #ifndef M1MOE_CUDA_H
 #define M1MOE_CUDA_H
@@ -156,22 +164,27 @@ M1MOE_API m1moe_status m1moe_cuda_router_topk(m1moe_cuda_ctx *ctx, int32_t layer
                                     float *d_topk_w, float *d_scores_out, void *stream);
 
 /* Router top-K for callers that cannot allocate GPU memory (no counterpart in
- * the reference).  Same results as m1moe_cuda_router_topk, but needs no
- * context: the caller passes the bf16 router [num_experts][hidden_dim] and x
- * (16-byte aligned device pointers) and the outputs; the kernel's scratch is
- * a fixed 49,408-byte array compiled into this library, present on every GPU
- * that loads it until the process exits.  It calls no cudaMalloc, cudaFree or
+ * the reference).  Bit-identical to m1moe_cuda_router_topk on the same router
+ * and x (the same kernel variant per batch), but needs no context: the caller
+ * passes the bf16 router [num_experts][hidden_dim] and x (16-byte aligned
+ * device pointers) and the outputs; the kernel's scratch is a fixed
+ * 49,152-byte array compiled into this library, present on every GPU that
+ * loads it until the process exits.  It calls no cudaMalloc, cudaFree or
  * other allocating routine, for callers whose memory is allocated up front
  * or by someone else (a host runtime that owns the GPU heap, a plugin that
  * may not grow the process's footprint, code that runs where allocation is
- * not allowed).  Limits: num_experts <= 256, batch <= 8, top_k <= 16.
+ * not allowed).  Limits: num_experts <= 256, batch <= 8, top_k <= 16,
+ * hidden_dim a multiple of 64 (any size: routing stages nothing in shared
+ * memory that grows with it).
  * The first call on a device (with that device current) looks up and clears
  * the array and waits for the device; make it before any stream capture.
  * All calls on a device share the array: calls that overlap on the GPU race,
  * so issue them on one stream or otherwise one after another.  d_status
- * (int32, may be NULL) receives 0, or a nonzero error word if a bounded
- * device wait gave up; d_topk_idx, d_topk_w ([batch][top_k]) and
- * d_scores_out ([batch][num_experts]) may be NULL. */
+ * (int32 device word, required) is cleared on the stream and receives a
+ * nonzero error bit if a bounded device wait gave up -- read it after the
+ * stream to trust the outputs; NULL is rejected with M1MOE_ERR_INVALID_ARG.
+ * d_topk_idx, d_topk_w ([batch][top_k]) and d_scores_out
+ * ([batch][num_experts]) may be NULL. */
 M1MOE_API m1moe_status m1moe_cuda_router_topk_noalloc(const uint16_t *d_router,
                                     int32_t num_experts, int32_t hidden_dim, int32_t top_k,
                                     int32_t norm_topk_prob, const void *d_x, int32_t x_dtype,

@@ -320,9 +320,44 @@ int divisor_tile(int n, int m, long long cap) {
     return best;
 }
 
+// Shared-memory map of a routing-only call (route_only): the kernel stops
+// after the top-K and weights, so it needs no x staging, tile ring or
+// activation buffers -- only the control block, the ranking keys and logits,
+// the slot arrays and, in the ring's place, room for the partial logits
+// (at most kMaxTok * kMaxExperts floats).  Fits an SM for any hidden size.
+size_t plan_route_only(m1::LayerParams &p, int grid, int nt, bool slot) {
+    p.fd_G = m1::make_fastdiv(grid);
+    p.bal_beta = 0;  // no row split to compute
+    p.ring_bytes = m1::kMaxTok * m1::kMaxExperts * 4;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off = align16(off + bytes);
+        return at;
+    };
+    const size_t ctl = take(sizeof(m1::Ctl));
+    const size_t dummy = take(16);  // the unused regions all point here
+    const size_t keys = take((size_t)nt * p.E * 8);
+    const size_t rlog = take((size_t)nt * p.E * 4);
+    const size_t lpart = take(8 * m1::kMaxTok * 4);
+    const size_t slots = slot ? take(sizeof(m1::Slots)) : 0;
+    const size_t bars = (size_t)p.ring_bytes;
+    const size_t base = align16(bars + 2 * sizeof(uint64_t) * (size_t)m1::kLayerSlots);
+    p.off_bars = (int)bars;
+    p.off_ctl = (int)(base + ctl);
+    p.off_xs = p.off_xsum = p.off_gup = p.off_actf = p.off_act = p.off_xseg = p.off_blk =
+        (int)(base + dummy);
+    p.off_keys = (int)(base + keys);
+    p.off_rlog = (int)(base + rlog);
+    p.off_lpart = (int)(base + lpart);
+    p.off_slots = (int)(base + slots);
+    return base + off;
+}
+
 // Plan tiles, stages and the shared-memory map of k_moe_layer<nt>.  Returns
 // the dynamic shared memory size, or 0 if the shape does not fit an SM.
 size_t plan_layer(m1::LayerParams &p, int grid, int nt, bool slot) {
+    if (p.route_only) return plan_route_only(p, grid, nt, slot);
     const m1::TiledLayout &tl = p.tl;
     const int nch = p.h / m1::kChunkCols;
     const int maxU = std::min(p.ntok * p.K, p.ne);
@@ -460,12 +495,13 @@ m1moe_status dispatch_layer(m1moe_cuda_ctx *c, const m1::LayerParams &p, cudaStr
 // ---- router top-K without allocation (m1moe_cuda_router_topk_noalloc) ----
 // Scratch of the k_moe_layer routing pass in a file-scope device array instead
 // of a context's cudaMalloc'd buffers: the tagged logits (8 tokens x 256
-// experts x 8 bytes), one 128-byte epoch line per CTA for up to 256 CTAs, and
-// the device error word.  49,408 bytes on every GPU that loads the library.
+// experts x 8 bytes) and one 128-byte epoch line per CTA for up to 256 CTAs.
+// 49,152 bytes on every GPU that loads the library.  (The device error word
+// is the caller's d_status.)
 constexpr int kNoAllocMaxCtas = 256;
 constexpr size_t kNoAllocXlog = (size_t)m1::kMaxTok * m1::kMaxExperts * 8;
 constexpr size_t kNoAllocEpochs = (size_t)kNoAllocMaxCtas * m1::kEpochStride * 4;
-constexpr size_t kNoAllocBytes = kNoAllocXlog + kNoAllocEpochs + 256;
+constexpr size_t kNoAllocBytes = kNoAllocXlog + kNoAllocEpochs;
 static __device__ __align__(256) uint8_t g_route_scratch[kNoAllocBytes];
 
 // Per-device address of g_route_scratch (host code cannot use the symbol as a
@@ -954,6 +990,13 @@ m1moe_status m1moe_cuda_router_topk_noalloc(const uint16_t *d_router, int32_t nu
         return fail(M1MOE_ERR_INVALID_ARG, "hidden_dim %d must be a positive multiple of 64", h);
     if ((reinterpret_cast<uintptr_t>(d_router) | reinterpret_cast<uintptr_t>(d_x)) & 15)
         return fail(M1MOE_ERR_INVALID_ARG, "router and x must be 16-byte aligned");
+    // The call is stream-ordered, so a device-side failure can only reach the
+    // caller through a word the caller reads after the stream: without one
+    // it would pass unseen.
+    if (!d_status)
+        return fail(M1MOE_ERR_INVALID_ARG,
+                    "d_status is NULL: the device status word is required (a bounded wait that "
+                    "gives up is reported only there)");
     int dev = 0;
     M1_CK(cudaGetDevice(&dev));
     NoAllocDevice *nd = nullptr;
@@ -981,13 +1024,17 @@ m1moe_status m1moe_cuda_router_topk_noalloc(const uint16_t *d_router, int32_t nu
     p.nbox = 1;  // one shared box: the fixed scratch has no room for a box per CTA
     p.box_words = 0;
     p.epochs = reinterpret_cast<unsigned *>(nd->scratch + kNoAllocXlog);
-    p.err = d_status ? d_status : reinterpret_cast<int *>(nd->scratch + kNoAllocXlog + kNoAllocEpochs);
+    p.err = d_status;
     p.route_only = 1;
     cudaStream_t st = as_stream(stream);
     M1_CK(cudaMemsetAsync(p.err, 0, sizeof(int), st));
     const int grid = std::min(nd->num_sms, kNoAllocMaxCtas);
+    // the kernel variant per batch is the one m1moe_cuda_router_topk takes
+    // (dispatch_layer), so both give bit-identical results
     if (B == 1) return launch_route_noalloc<1, false>(p, grid, st);
-    if (B == 2) return launch_route_noalloc<2, false>(p, grid, st);
+    if (B == 2)
+        return m1::slot_path(2, h) ? launch_route_noalloc<2, true>(p, grid, st)
+                                   : launch_route_noalloc<2, false>(p, grid, st);
     if (B <= 4) return launch_route_noalloc<4, true>(p, grid, st);
     return launch_route_noalloc<8, true>(p, grid, st);
 }

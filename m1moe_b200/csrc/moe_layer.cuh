@@ -1305,8 +1305,10 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         // staging (every CTA reading all of x at once) waits until this CTA's
         // logits are published (barrier 6), overlapping the logit exchange.
         named_sync(6, kLayerThreads);
-        // x as int16 chunks (dp2a layout, common.cuh) with scales and exact sums
-        for (int q = st; q < p.ntok * nch; q += nst) {
+        // x as int16 chunks (dp2a layout, common.cuh) with scales and exact
+        // sums (a routing-only call has no use for it, nor room: the host
+        // plans no x staging then)
+        for (int q = st; !p.route_only && q < p.ntok * nch; q += nst) {
             const int t = q / nch, c = q - t * nch;
             float v[32];
             load_x32_any(X, Xbf16, (size_t)t * h + (size_t)c * kChunkCols, v);

@@ -1,9 +1,9 @@
 """Small, self-contained GPU cases for profiling the library's kernels.
 
-    python -m m1moe_b200.profile_cases layer olmoe 1     # k_moe_layer, OLMoE shapes, batch 1
-    python -m m1moe_b200.profile_cases layer mixtral 1   # k_moe_layer, Mixtral shapes
-    python -m m1moe_b200.profile_cases matvec 1          # k_matvec4_ring over 2048 matrices
-    python -m m1moe_b200.profile_cases prefill mixtral 512  # k_prefill_gemm, 512 tokens
+    python profile_cases.py layer olmoe 1     # k_moe_layer, OLMoE shapes, batch 1
+    python profile_cases.py layer mixtral 1   # k_moe_layer, Mixtral shapes
+    python profile_cases.py matvec 1          # k_matvec4_ring over 2048 matrices
+    python profile_cases.py prefill mixtral 512  # k_prefill_gemm, 512 tokens
 
 Each case builds synthetic weights (m1moe_b200.synth), runs the kernel a few
 times and exits 0; the device footprint stays at a few GB so that a profiler

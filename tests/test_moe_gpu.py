@@ -64,9 +64,13 @@ def _run_case(oracle_lib, img, router, *, h, I, E, K, norm, B, xdt=torch.bfloat1
                                          E=E, K=K, gs=64, norm=norm, nthreads=8)
     blk.synchronize()  # raises if a bounded device wait gave up
     _check_routing(idx, w, ridx, rw, xf, router, K)
+    checked = 0
     for t in range(B):
         if set(idx[t].tolist()) == set(ridx[t].tolist()):
             assert rel_max_err(out[t], ref[t]) < TOL, t
+            checked += 1
+    # a token routed differently at a near-tie is skipped, but never most of them
+    assert checked >= max(1, (9 * B) // 10), (checked, B)
     blk.close()
     return out, idx, w
 

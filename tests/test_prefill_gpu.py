@@ -4,10 +4,11 @@ The reference has no batched MoE path (it runs runLayer per token), so the
 oracle is the same per-token restatement as for the decode kernel.  Bars as
 in test_moe_gpu.py: expert indices equal wherever the K-th and (K+1)-th
 scores differ by more than 1e-5, weights within 1e-5 relative, outputs
-max |out - ref| <= 1e-3 * ||ref||_2.  The weights and the SwiGLU
-activations enter the tensor cores as bf16 (fp32 accumulation); that error
-is inside the output bar, which is checked here without the residual, on
-the expert sum alone.
+max |out - ref| <= 1e-3 * ||ref||_2, on at least 90 % of the tokens (a
+token whose expert set differs from the oracle's at a near-tie is skipped).
+The weights (q*s + b, one rounding), tokens and SwiGLU activations enter the
+tensor cores as fp16 with fp32 accumulation; that error is inside the output
+bar, which is checked here without the residual, on the expert sum alone.
 """
 from __future__ import annotations
 

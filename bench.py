@@ -19,9 +19,19 @@ e2e      = the same bytes through the reference-facing synchronous C-ABI call
            (m1moe_cuda_moe_layer_host, one per layer, like runLayer's
            commitSync) with pinned host buffers; copies inside the timed region.
 N GPUs   = expert parallel: rank r holds experts [r*64/N, (r+1)*64/N) of every
-           layer and owns one decode token; per layer the tokens are
-           all-gathered, each rank applies its experts to every token routed to
-           them, and a reduce-scatter returns each token's sum (weak scaling).
+           layer and owns one decode token; per layer one m1moe_cuda_moe_layer_ep
+           launch per GPU gathers the tokens over NVLink peer memory, applies the
+           rank's experts to every token routed to them and returns each token's
+           sum to its owner (weak scaling).
+parity   = after the timed region, the first and the last layer's outputs of
+           every rank's tokens against the CPU oracle (the C restatement of the
+           reference's arithmetic) on the same weights; the run exits non-zero
+           above 1e-3 of ||ref||_2.
+matvec_c0      (1 GPU) config 0: the 1024x2048 int4 matvec over 3072 distinct
+           matrices per launch, GB/s and fraction of the measured HBM peak.
+mixtral_decode (1 GPU) config 3 decode at batch 1, 4 and 8 (4 distinct layers).
+mixtral_ep     config 3 decode expert-parallel: 8 experts over N GPUs (one per
+           GPU at N=8), one token per rank, with its own oracle parity check.
 prefill  = (1 GPU) config 3's prefill mode beside the decode line: one
            Mixtral-shaped layer over 512 tokens through m1moe_cuda_moe_prefill
            (tensor-core grouped GEMMs), TFLOP/s against the measured bf16 peak.
@@ -204,28 +214,29 @@ def host_layers_for_cpu(wl, n_layers: int, device=None):
 
 
 def run_reference(args, wl) -> None:
-    """CPU arm: the oracle (C restatement of the reference path), all host threads."""
+    """CPU arm: the oracle (C restatement of the reference path), all host
+    threads, on the GPU arm's workload: one token through the MoE blocks of
+    `layers` distinct synthetic layers per step (the same layer count)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from m1moe_b200 import synth
     threads = os.cpu_count() or 1
-    layers = host_layers_for_cpu(wl, 2)
-    routers = [synth.router_weights(SEED + 1000 + L, wl["E"], wl["h"]) for L in range(2)]
+    L = wl["layers"]
+    layers = host_layers_for_cpu(wl, L)
+    routers = [synth.router_weights(SEED + 1000 + layer, wl["E"], wl["h"]) for layer in range(L)]
     import oracle
     oracle.build()
     x = synth.bf16_to_f32(synth.hidden_states(SEED + 99, 1, wl["h"]))
-    res = x.copy()
 
     def step():
-        nonlocal x, res
+        # every layer reads the same hidden state, as in the GPU arm
         nb = 0
-        for L in range(2):
-            out, idx, _ = oracle.moe_layer(layers[L], routers[L], x, res, h=wl["h"],
+        for layer in range(L):
+            out, idx, _ = oracle.moe_layer(layers[layer], routers[layer], x, x, h=wl["h"],
                                            inter=wl["I"], E=wl["E"], K=wl["K"], gs=wl["gs"],
                                            norm=wl["norm"], nthreads=threads)
             nb += len(set(idx[0].tolist())) * expert_bytes(wl) + router_bytes(wl)
-            x = res = out
         return nb
 
     for _ in range(args.warmup):
@@ -234,14 +245,15 @@ def run_reference(args, wl) -> None:
     nbytes = sum(step() for _ in range(args.steps))
     dt = time.perf_counter() - t0
     val = nbytes / dt / 1e9
-    sample = (f"each step: one token through 2 synthetic {wl['name']} MoE layers "
-              f"(C oracle, {threads} threads)")
+    sample = (f"each step: one token through the MoE blocks of {L} synthetic {wl['name']} "
+              f"layers (C oracle, persistent pool of {threads} threads)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl["name"], "tokens_per_step": 1, "layers_per_step": 2},
+        "config": {"workload": wl["name"], "tokens_per_step": 1, "layers_per_step": L},
+        "tok_s": args.steps / dt,
         "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -297,6 +309,272 @@ def prefill_measure(dev, steps: int, warmup: int) -> dict:
             "dtype": "fp16 operands (int4 weights dequantised), fp32 accumulation"}
 
 
+def oracle_parity(wl: dict, layer: int, x_f32: np.ndarray, out: np.ndarray, idx: np.ndarray,
+                  dev, seed_base: int = SEED) -> dict:
+    """Checker (after the timed region, outside it): one layer's outputs for
+    these tokens against the CPU oracle (a C restatement of the reference's
+    arithmetic) on the same weights -- the layer image regenerated from its
+    seed and copied to the host.  residual = x, as in the timed step.  Returns
+    the largest max|out - ref| / ||ref||_2 over the tokens whose expert set
+    equals the oracle's (a near-tie may route one differently), and counts."""
+    import oracle
+    oracle.build()
+    from m1moe_b200 import synth
+    img = synth.layer_image_device(wl["E"], wl["h"], wl["I"], wl["gs"], seed=seed_base + layer,
+                                   device=dev).cpu().numpy()
+    router = synth.router_weights(seed_base + 1000 + layer, wl["E"], wl["h"])
+    ref, ridx, _ = oracle.moe_layer(img, router, x_f32, x_f32, h=wl["h"], inter=wl["I"],
+                                    E=wl["E"], K=wl["K"], gs=wl["gs"], norm=wl["norm"],
+                                    nthreads=os.cpu_count() or 1)
+    errs, same = [], 0
+    for t in range(x_f32.shape[0]):
+        if set(idx[t].tolist()) == set(ridx[t].tolist()):
+            same += 1
+            errs.append(float(np.max(np.abs(out[t] - ref[t])) / max(np.linalg.norm(ref[t]), 1e-30)))
+    return {"max_rel_err": max(errs) if errs else None, "tokens_checked": same,
+            "tokens": int(x_f32.shape[0])}
+
+
+def merge_parity(parts: list[dict], tol: float = 1e-3) -> dict:
+    errs = [p["max_rel_err"] for p in parts if p["max_rel_err"] is not None]
+    checked = sum(p["tokens_checked"] for p in parts)
+    total = sum(p["tokens"] for p in parts)
+    worst = max(errs) if errs else None
+    ok = worst is not None and worst <= tol and checked >= 0.9 * total
+    return {"max_rel_err": worst, "tokens_checked": checked, "tokens": total, "tol": tol,
+            "ok": bool(ok), "oracle": "C restatement of the reference (oracle/m1moe_oracle.c)"}
+
+
+def timed_replays(graph, n: int, stream, world: int):
+    """Device time (ms) of n graph replays on `stream`, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(n):
+            graph.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+MATVEC_C0 = dict(name="c0_matvec_1024x2048_g64_b1_stream", out=1024, inn=2048, gs=64, mats=3072)
+
+
+def matvec_c0_measure(dev) -> dict:
+    """The metric's first half: config 0's int4 dequant-matvec (1024 x 2048,
+    group 64, batch 1, bf16 x and y) over a stream of 3072 distinct matrices
+    (3.6 GB > L2), one m1moe_cuda_matvec4_strided launch per pass over all of
+    them, CUDA events around >= 100 ms of launches.  Algorithmic bytes per
+    matvec: out*in/2 + out*(in/64)*4 + in*2 + out*2 = 1,185,792 B."""
+    import torch
+
+    from m1moe_b200 import _lib
+    c = MATVEC_C0
+    out, inn, gs, nm = c["out"], c["inn"], c["gs"], c["mats"]
+    wbytes, sbytes = out * inn // 2, out * (inn // gs) * 2
+    stride = wbytes + 2 * sbytes
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 5)
+    buf = torch.empty((nm, stride), dtype=torch.uint8, device=dev)
+    buf[:, :wbytes] = torch.randint(0, 256, (nm, wbytes), dtype=torch.uint8, generator=g, device=dev)
+    scale = (torch.rand((nm, sbytes // 2), generator=g, device=dev) * 0.015 + 0.005).to(torch.bfloat16)
+    bias = (-8.0 * scale.float() + 1e-3 * torch.randn((nm, sbytes // 2), generator=g, device=dev)
+            ).to(torch.bfloat16)
+    buf[:, wbytes:wbytes + sbytes] = scale.view(torch.uint8).view(nm, sbytes)
+    buf[:, wbytes + sbytes:] = bias.view(torch.uint8).view(nm, sbytes)
+    del scale, bias
+    x = torch.randn((1, inn), generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty((nm, out), dtype=torch.bfloat16, device=dev)
+    base = buf.data_ptr()
+    stream = torch.cuda.Stream(device=dev)
+
+    def launch():
+        _lib.call("m1moe_cuda_matvec4_strided", base, base + wbytes, base + wbytes + sbytes, stride,
+                  nm, x.data_ptr(), _lib.DTYPE_BF16, y.data_ptr(), _lib.DTYPE_BF16, out, inn, gs, 1,
+                  stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(5):
+            launch()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        launch()
+        b.record(stream)
+    torch.cuda.synchronize()
+    n = max(20, int(120.0 / max(a.elapsed_time(b), 1e-3)))  # >= ~100 ms
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(n):
+            launch()
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    per_mv = out * inn // 2 + out * (inn // gs) * 4 + inn * 2 + out * 2
+    gbs = per_mv * nm * n / (ms * 1e-3) / 1e9
+    peak, kind = measured_peaks()
+    del buf
+    return {"workload": c["name"], "value": gbs, "unit": "GB/s", "frac": gbs / peak,
+            "peak": peak, "peak_source": kind, "matrices_per_launch": nm, "launches": n,
+            "timed_ms": ms, "us_per_matvec": ms * 1e3 / (n * nm),
+            "algorithmic_bytes_per_matvec": per_mv, "kernel": "k_matvec4_ring<1>",
+            "l2": "3.6 GB of distinct matrices per launch (> 126 MB L2)"}
+
+
+MIXTRAL = dict(name="mixtral_moe_decode_x4L", h=4096, I=14336, E=8, K=2, gs=64, layers=4,
+               norm=True)
+
+
+def mixtral_decode_measure(dev, steps: int, warmup: int, batches=(1, 4, 8)) -> dict:
+    """Config 3's decode mode on one GPU: Mixtral-shaped MoE blocks (4 distinct
+    layers, 3.2 GB) at batch 1, 4 and 8, one k_moe_layer launch per layer,
+    replayed from a CUDA graph.  GB/s = distinct experts read x 99,090,432 B +
+    router 65,536 B per layer, over the device time."""
+    import torch
+
+    from m1moe_b200 import MoEBlock, _lib, synth
+    c = MIXTRAL
+    h, I, E, K, L = c["h"], c["I"], c["E"], c["K"], c["layers"]
+    seed = SEED + 500
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, group_size=c["gs"],
+                   num_layers=L, norm_topk_prob=c["norm"], max_batch=8, device=dev.index)
+    for layer in range(L):
+        img = synth.layer_image_device(E, h, I, c["gs"], seed=seed + layer, device=dev)
+        blk.load_expert_layer(layer, img)
+        del img
+        blk.load_router(layer, synth.router_weights(seed + 1000 + layer, E, h))
+    stream = torch.cuda.Stream(device=dev)
+    peak, kind = measured_peaks()
+    eb = expert_bytes(c)
+    res = {"workload": c["name"], "unit": "GB/s", "peak": peak, "peak_source": kind}
+    for B in batches:
+        xb = synth.hidden_states(seed + 99 + B, B, h)
+        x = torch.from_numpy(synth.bf16_to_f32(xb)).to(dev)
+        out = torch.empty((B, h), dtype=torch.float32, device=dev)
+        idx = torch.zeros((L, B, K), dtype=torch.int32, device=dev)
+
+        def one_step():
+            for layer in range(L):
+                _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, x.data_ptr(), 0, x.data_ptr(), 0,
+                          out.data_ptr(), 0, B, idx[layer].data_ptr(), 0, stream.cuda_stream)
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                one_step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            one_step()
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, warmup)):
+                graph.replay()
+        n = max(10, min(steps, 200))
+        ms = timed_replays(graph, n, stream, 1)
+        blk.synchronize()
+        il = idx.cpu().numpy()
+        step_bytes = sum(len(set(il[layer].ravel().tolist())) * eb + router_bytes(c)
+                         for layer in range(L))
+        gbs = step_bytes * n / (ms * 1e-3) / 1e9
+        res[f"b{B}"] = {"us_per_layer": ms * 1e3 / (n * L), "value": gbs, "frac": gbs / peak,
+                        "tok_s_moe_blocks": B * n / (ms * 1e-3) * L / 32,
+                        "distinct_experts_per_layer": step_bytes / L / eb}
+        del graph
+    blk.close()
+    res["note"] = ("tok_s_moe_blocks scales the 4-layer time to Mixtral's 32 MoE blocks "
+                   "(MoE blocks only, no dense layers)")
+    return res
+
+
+def mixtral_ep_measure(dev, world: int, rank: int, steps: int, warmup: int) -> dict:
+    """Mixtral-shaped expert parallelism (config 3 decode): E = 8 experts, one
+    per GPU at N = 8 (8/N per GPU), one token per rank (B = N), 4 distinct
+    layers, one m1moe_cuda_moe_layer_ep launch per layer and GPU, replayed from
+    a CUDA graph; the device time is the max over ranks.  N = 1 runs the same
+    step on one GPU (all 8 experts, batch 1).  Each rank's outputs of the last
+    layer are checked against the oracle after the timed region."""
+    import torch
+
+    from m1moe_b200 import MoEBlock, _lib, synth
+    from m1moe_b200.expert_parallel import EPFused, shard
+    c = MIXTRAL
+    h, I, E, K, L = c["h"], c["I"], c["E"], c["K"], c["layers"]
+    seed = SEED + 700
+    e0, ne = shard(E, world, rank)
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, group_size=c["gs"],
+                   num_layers=L, norm_topk_prob=c["norm"], max_batch=max(world, 1),
+                   device=dev.index, expert_begin=e0, expert_count=ne)
+    for layer in range(L):
+        img = synth.layer_image_device(E, h, I, c["gs"], seed=seed + layer, device=dev)
+        blk.load_expert_layer(layer, img)
+        del img
+        blk.load_router(layer, synth.router_weights(seed + 1000 + layer, E, h))
+    xb = synth.hidden_states(seed + 7 + rank, 1, h)
+    x = torch.from_numpy(synth.bf16_to_f32(xb)).to(dev)
+    out = torch.empty((1, h), dtype=torch.float32, device=dev)
+    idx = torch.zeros((L, world, K), dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    if world > 1:
+        ep = EPFused(blk, 1)
+
+        def one_step():
+            for layer in range(L):
+                ep(layer, x, x, out=out, idx=idx[layer], stream=stream)
+    else:
+        def one_step():
+            for layer in range(L):
+                _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, x.data_ptr(), 0, x.data_ptr(), 0,
+                          out.data_ptr(), 0, 1, idx[layer].data_ptr(), 0, stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            one_step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        one_step()
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, warmup)):
+            graph.replay()
+    n = max(10, min(steps, 200))
+    ms = timed_replays(graph, n, stream, world)
+    blk.synchronize()
+    il = idx.cpu().numpy()
+    eb = expert_bytes(c)
+    local = sum(len({e for e in il[layer].ravel().tolist() if e0 <= e < e0 + ne}) * eb
+                + router_bytes(c) for layer in range(L))
+    tb = torch.tensor([float(local)], dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+    gbs = float(tb.item()) * n / (ms * 1e-3) / 1e9
+    out_np = out.cpu().numpy()
+    par = oracle_parity(c, L - 1, synth.bf16_to_f32(xb), out_np, il[L - 1][rank:rank + 1], dev,
+                        seed_base=seed)
+    parts = [par]
+    if world > 1:
+        import torch.distributed as dist
+        allp: list = [None] * world
+        dist.all_gather_object(allp, par)
+        parts = allp
+    del graph
+    blk.close()
+    return {"workload": f"mixtral_moe_decode_ep{world}_x4L", "value": gbs, "unit": "GB/s",
+            "tokens_per_rank": 1, "experts_per_gpu": ne, "us_per_layer": ms * 1e3 / (n * L),
+            "tok_s_moe_blocks": world * n / (ms * 1e-3) * L / 32,
+            "parity": merge_parity(parts),
+            "note": "tok_s_moe_blocks scales the 4-layer time to Mixtral's 32 MoE blocks"}
+
+
 def run_gpu(args, wl) -> None:
     import torch
     import torch.distributed as dist
@@ -333,8 +611,8 @@ def run_gpu(args, wl) -> None:
         blk.load_router(layer, synth.router_weights(SEED + 1000 + layer, E, h))
     torch.cuda.synchronize()
 
-    x0 = torch.from_numpy(synth.hidden_states(SEED + 7 + rank, b, h).view(np.int16)).to(dev)
-    x0 = x0.view(torch.bfloat16)
+    xb = synth.hidden_states(SEED + 7 + rank, b, h)
+    x0 = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
     part = torch.zeros((B, h), dtype=torch.float32, device=dev)  # layer output (1 GPU)
     own = torch.zeros((b, h), dtype=torch.float32, device=dev)   # this rank's token state
     own.copy_(x0.float())
@@ -343,16 +621,13 @@ def run_gpu(args, wl) -> None:
     stream = torch.cuda.Stream(device=dev)
 
     # Single GPU: every layer reads `own` (x and residual) and writes `part`.
+    ep = None
     if world == 1:
-        def one_step(events=None):
-            for layer in range(L):
-                if events is not None:
-                    events[layer].record()
-                _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, own.data_ptr(), 0,
-                          own.data_ptr(), 0, part.data_ptr(), 0, B, idx_log[layer].data_ptr(),
-                          w_log[layer].data_ptr(), stream.cuda_stream)
-            if events is not None:
-                events[L].record()
+        def run_layer(layer, dst):
+            _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, own.data_ptr(), 0,
+                      own.data_ptr(), 0, dst.data_ptr(), 0, B, idx_log[layer].data_ptr(),
+                      w_log[layer].data_ptr(), stream.cuda_stream)
+        result = part
     else:
         # Expert parallel in the kernel over NVLink peer memory
         # (m1moe_b200.expert_parallel.EPFused): per layer one launch per GPU
@@ -362,16 +637,19 @@ def run_gpu(args, wl) -> None:
         ep = EPFused(blk, b)
         nxt = torch.zeros((b, h), dtype=torch.float32, device=dev)
 
-        def one_step(events=None):
-            for layer in range(L):
-                if events is not None:
-                    events[layer].record()
-                ep(layer, own, own, out=nxt, idx=idx_log[layer], w=w_log[layer], stream=stream)
+        def run_layer(layer, dst):
+            ep(layer, own, own, out=dst, idx=idx_log[layer], w=w_log[layer], stream=stream)
+        result = nxt
+
+    def one_step(events=None):
+        for layer in range(L):
             if events is not None:
-                events[L].record()
+                events[layer].record()
+            run_layer(layer, result)
+        if events is not None:
+            events[L].record()
 
     launches_per_step = L  # k_moe_layer, one per layer
-    # Eager warm-up (initialises NCCL communicators before capture).
     with torch.cuda.stream(stream):
         for _ in range(3):
             one_step()
@@ -388,29 +666,27 @@ def run_gpu(args, wl) -> None:
         one_step(ev)
     torch.cuda.synchronize()
 
-    def replay(n):
-        for _ in range(n):
-            graph.replay()
-
     with torch.cuda.stream(stream):
-        replay(args.warmup)
+        for _ in range(args.warmup):
+            graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    layer_ms = []
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
             t_start.record(stream)
-            replay(args.steps)
+            for _ in range(args.steps):
+                graph.replay()
             t_end.record(stream)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     ms = t_start.elapsed_time(t_end)
+    blk.synchronize()  # raises if a bounded device wait gave up during the timed steps
     # per-layer durations: the event graph, replayed after the timed region
     # (its event nodes add a little time between layers)
     with torch.cuda.stream(stream):
@@ -421,8 +697,29 @@ def run_gpu(args, wl) -> None:
         dist.barrier()
     layer_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(L)]
 
-    # Distinct local experts per layer from the last step's routing.
+    # Parity (after the timed region): the last layer's outputs of this rank's
+    # tokens (left in `result` by the last replay) and, from one more call, the
+    # first layer's, against the CPU oracle on the same weights.
+    out_last = result.cpu().numpy()
     idx_last = idx_log.cpu().numpy()
+    first = torch.empty_like(result)
+    with torch.cuda.stream(stream):
+        run_layer(0, first)
+    torch.cuda.synchronize()
+    blk.synchronize()
+    out_first = first.cpu().numpy()
+    idx_first = idx_log[0].cpu().numpy()
+    x_f32 = synth.bf16_to_f32(xb)
+    tok = slice(rank * b, (rank + 1) * b)
+    par = [oracle_parity(wl, L - 1, x_f32, out_last, idx_last[L - 1][tok], dev),
+           oracle_parity(wl, 0, x_f32, out_first, idx_first[tok], dev)]
+    if world > 1:
+        allp: list = [None] * world
+        dist.all_gather_object(allp, par)
+        par = [p for rp in allp for p in rp]
+    parity = merge_parity(par)
+
+    # Distinct local experts per layer from the last step's routing.
     eb = expert_bytes(wl)
     step_bytes_local = sum(
         len({e for e in idx_last[layer].ravel().tolist() if e0 <= e < e0 + ne}) * eb
@@ -498,10 +795,17 @@ def run_gpu(args, wl) -> None:
         e2e = {"value": job_step_bytes * args.steps / (te.item() * 1e-3) / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": b * h * 4, "d2h_bytes_per_step": b * h * 4,
                "api": "pinned H2D + captured EP step + D2H per step"}
+    del graph, graph_ev
+    blk.close()
 
-    prefill = None
-    if world == 1 and not args.no_prefill:
-        prefill = prefill_measure(dev, args.steps, args.warmup)
+    # sub-measurements, each with its own context (the decode tables are freed)
+    mixtral_ep = mixtral_ep_measure(dev, world, rank, args.steps, args.warmup)
+    matvec_c0 = mixtral_dec = prefill = None
+    if world == 1:
+        matvec_c0 = matvec_c0_measure(dev)
+        mixtral_dec = mixtral_decode_measure(dev, args.steps, args.warmup)
+        if not args.no_prefill:
+            prefill = prefill_measure(dev, args.steps, args.warmup)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -528,18 +832,22 @@ def run_gpu(args, wl) -> None:
                          "peak_source": peak_kind, "launch_us": launch_ms * 1e3,
                          "layer_us_isolated": lay_ms * 1e3,
                          "algorithmic_bytes_per_launch": per_layer_bytes},
+            "parity": parity,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "matvec_c0": matvec_c0,
+            "mixtral_decode": mixtral_dec,
+            "mixtral_ep": mixtral_ep,
             "prefill": prefill,
             "gpu_launches": launches_per_step * (args.steps + 0),
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
-    del graph, graph_ev
-    blk.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if not parity["ok"] or not mixtral_ep["parity"]["ok"]:
+        raise SystemExit(f"parity check failed: {parity} {mixtral_ep['parity']}")
 
 
 def main():

@@ -61,6 +61,8 @@ def lib():
         L.orc_expert_offsets.argtypes = [c_int, c_int, c_int, ctypes.POINTER(ctypes.c_size_t)]
         L.orc_matvec4bit.argtypes = [u32p, u16p, u16p, f32p, f32p, c_int, c_int, c_int]
         L.orc_matvec4bit_mt.argtypes = [u32p, u16p, u16p, f32p, f32p, c_int, c_int, c_int, c_int]
+        L.orc_matvec4bit_rows.argtypes = [u32p, u16p, u16p, f32p, f32p, c_int, c_int, c_int,
+                                          c_int, c_int]
         L.orc_swiglu.argtypes = [f32p, f32p, f32p, c_int]
         L.orc_moe_combine.argtypes = [f32p, f32p, f32p, f32p, c_int, c_int]
         L.orc_router_scores.argtypes = [u16p, f32p, c_int, c_int, f32p]
@@ -105,6 +107,22 @@ def matvec4bit(W: np.ndarray, S: np.ndarray, B: np.ndarray, x: np.ndarray, gs: i
     lib().orc_matvec4bit_mt(_p(W, ctypes.c_uint32), _p(S, ctypes.c_uint16),
                             _p(B, ctypes.c_uint16), _p(x, ctypes.c_float),
                             _p(y, ctypes.c_float), out_dim, in_dim, gs, nthreads)
+    return y
+
+
+def matvec4bit_plain(W: np.ndarray, S: np.ndarray, B: np.ndarray, x: np.ndarray,
+                     gs: int) -> np.ndarray:
+    """The literal lane-by-lane restatement of Shaders.metal:39-92 (lanes outermost,
+    single thread); matvec4bit() runs the lane-vectorised form, bit-identical."""
+    W = np.ascontiguousarray(W, dtype=np.uint32)
+    S = np.ascontiguousarray(S, dtype=np.uint16)
+    B = np.ascontiguousarray(B, dtype=np.uint16)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out_dim, in_dim = W.shape[0], W.shape[1] * 8
+    y = np.empty(out_dim, dtype=np.float32)
+    lib().orc_matvec4bit_rows(_p(W, ctypes.c_uint32), _p(S, ctypes.c_uint16),
+                              _p(B, ctypes.c_uint16), _p(x, ctypes.c_float),
+                              _p(y, ctypes.c_float), out_dim, in_dim, gs, 0, out_dim)
     return y
 
 

@@ -12,6 +12,7 @@
 
 #include <math.h>
 #include <pthread.h>
+#include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -92,9 +93,66 @@ void orc_matvec4bit_rows(const uint32_t *W, const uint16_t *S, const uint16_t *B
     }
 }
 
+/* The same arithmetic as orc_matvec4bit_rows, lane by lane in the same
+ * order (for each lane: words lid, lid+64, ... ascending, nibbles 0..7), but
+ * with the 64 lanes innermost so that the compiler vectorises across lanes:
+ * per block of 64 words, x is read transposed (xT[b][lid] = x[8*(w0+lid)+b])
+ * and the lanes' scales and biases are gathered once.  Bit-identical to the
+ * plain restatement (tests/test_oracle_golden.py checks it); used for the
+ * timed CPU baseline and for the large parity checks. */
+void orc_matvec4bit_rows_lanes(const uint32_t *W, const uint16_t *S, const uint16_t *B,
+                               const float *x, float *y, int out_dim, int in_dim, int gs,
+                               int row0, int row1) {
+    const unsigned numWords = (unsigned)in_dim / 8;
+    const unsigned numGroups = (unsigned)in_dim / (unsigned)gs;
+    const unsigned nblk = (numWords + ORC_TG - 1) / ORC_TG;
+    float *xT = (float *)malloc(sizeof(float) * (size_t)nblk * 8 * ORC_TG);
+    if (!xT) {
+        orc_matvec4bit_rows(W, S, B, x, y, out_dim, in_dim, gs, row0, row1);
+        return;
+    }
+    for (unsigned k = 0; k < nblk; ++k)
+        for (unsigned b = 0; b < 8; ++b)
+            for (unsigned lid = 0; lid < ORC_TG; ++lid) {
+                const unsigned w = k * ORC_TG + lid;
+                xT[((size_t)k * 8 + b) * ORC_TG + lid] = w < numWords ? x[w * 8 + b] : 0.0f;
+            }
+    float acc[ORC_TG], sc[ORC_TG], bi[ORC_TG], nib[ORC_TG];
+    for (int row = row0; row < row1 && row < out_dim; ++row) {
+        const uint32_t *wRow = W + (size_t)row * numWords;
+        const uint16_t *sRow = S + (size_t)row * numGroups;
+        const uint16_t *bRow = B + (size_t)row * numGroups;
+        for (unsigned lid = 0; lid < ORC_TG; ++lid) acc[lid] = 0.0f;
+        for (unsigned k = 0; k < nblk; ++k) {
+            const unsigned w0 = k * ORC_TG;
+            const unsigned nl = numWords - w0 < ORC_TG ? numWords - w0 : ORC_TG;
+            for (unsigned lid = 0; lid < nl; ++lid) {
+                const unsigned g = ((w0 + lid) * 8) / (unsigned)gs;
+                sc[lid] = orc_bf16_to_f32(sRow[g]);
+                bi[lid] = orc_bf16_to_f32(bRow[g]);
+            }
+            for (unsigned b = 0; b < 8; ++b) {
+                const float *xb = xT + ((size_t)k * 8 + b) * ORC_TG;
+                for (unsigned lid = 0; lid < nl; ++lid)
+                    nib[lid] = (float)((wRow[w0 + lid] >> (b * 4)) & 0xFu);
+                for (unsigned lid = 0; lid < nl; ++lid) {
+                    const float xv = xb[lid];
+                    /* Shaders.metal:77 */
+                    acc[lid] = fmaf(nib[lid], sc[lid] * xv, fmaf(bi[lid], xv, acc[lid]));
+                }
+            }
+        }
+        /* Shaders.metal:86-90: tree reduction. */
+        for (unsigned s2 = ORC_TG / 2; s2 > 0; s2 >>= 1)
+            for (unsigned lid = 0; lid < s2; ++lid) acc[lid] += acc[lid + s2];
+        y[row] = acc[0];
+    }
+    free(xT);
+}
+
 void orc_matvec4bit(const uint32_t *W, const uint16_t *S, const uint16_t *B,
                     const float *x, float *y, int out_dim, int in_dim, int gs) {
-    orc_matvec4bit_rows(W, S, B, x, y, out_dim, in_dim, gs, 0, out_dim);
+    orc_matvec4bit_rows_lanes(W, S, B, x, y, out_dim, in_dim, gs, 0, out_dim);
 }
 
 typedef struct {
@@ -107,8 +165,42 @@ typedef struct {
 
 static void *orc_mv_worker(void *p) {
     orc_mv_job *j = (orc_mv_job *)p;
-    orc_matvec4bit_rows(j->W, j->S, j->B, j->x, j->y, j->out_dim, j->in_dim, j->gs, j->row0,
-                        j->row1);
+    orc_matvec4bit_rows_lanes(j->W, j->S, j->B, j->x, j->y, j->out_dim, j->in_dim, j->gs, j->row0,
+                              j->row1);
+    return NULL;
+}
+
+/* A persistent pool of host threads for the row-partitioned matvec (threads
+ * are created once, not per matvec): the caller publishes `njobs` jobs,
+ * bumps the generation, runs job 0 itself and waits for the others. */
+#define ORC_MAX_THREADS 256
+static struct {
+    pthread_mutex_t mu;
+    pthread_cond_t go, done;
+    pthread_t th[ORC_MAX_THREADS];
+    int nthreads;          /* workers started (jobs 1..nthreads) */
+    unsigned gen;          /* bumped per batch of jobs */
+    int pending;           /* jobs of this batch not finished yet */
+    int njobs;
+    orc_mv_job jobs[ORC_MAX_THREADS];
+} orc_pool = {PTHREAD_MUTEX_INITIALIZER, PTHREAD_COND_INITIALIZER, PTHREAD_COND_INITIALIZER};
+static pthread_mutex_t orc_pool_call = PTHREAD_MUTEX_INITIALIZER; /* one batch at a time */
+
+static void *orc_pool_worker(void *arg) {
+    const int id = (int)(intptr_t)arg;
+    unsigned seen = 0;
+    pthread_mutex_lock(&orc_pool.mu);
+    for (;;) {
+        while (orc_pool.gen == seen) pthread_cond_wait(&orc_pool.go, &orc_pool.mu);
+        seen = orc_pool.gen;
+        if (id < orc_pool.njobs) {
+            orc_mv_job j = orc_pool.jobs[id];
+            pthread_mutex_unlock(&orc_pool.mu);
+            orc_mv_worker(&j);
+            pthread_mutex_lock(&orc_pool.mu);
+            if (--orc_pool.pending == 0) pthread_cond_signal(&orc_pool.done);
+        }
+    }
     return NULL;
 }
 
@@ -121,23 +213,35 @@ void orc_matvec4bit_mt(const uint32_t *W, const uint16_t *S, const uint16_t *B,
         orc_matvec4bit(W, S, B, x, y, out_dim, in_dim, gs);
         return;
     }
-    if (nthreads > 256) nthreads = 256;
-    pthread_t th[256];
-    orc_mv_job jobs[256];
-    int per = (out_dim + nthreads - 1) / nthreads;
-    int started = 0;
-    for (int t = 0; t < nthreads; ++t) {
-        jobs[t] = (orc_mv_job){W, S, B, x, y, out_dim, in_dim, gs, t * per,
-                               (t + 1) * per < out_dim ? (t + 1) * per : out_dim};
-        if (jobs[t].row0 >= jobs[t].row1) break;
-        if (pthread_create(&th[t], NULL, orc_mv_worker, &jobs[t]) != 0) {
-            orc_mv_worker(&jobs[t]); /* run inline if a thread cannot start */
-            continue;
-        }
-        th[started] = th[t];
-        ++started;
+    if (nthreads > ORC_MAX_THREADS) nthreads = ORC_MAX_THREADS;
+    pthread_mutex_lock(&orc_pool_call);
+    pthread_mutex_lock(&orc_pool.mu);
+    while (orc_pool.nthreads < nthreads - 1) { /* grow the pool on demand, once */
+        const int id = orc_pool.nthreads + 1;
+        if (pthread_create(&orc_pool.th[id - 1], NULL, orc_pool_worker, (void *)(intptr_t)id) != 0)
+            break;
+        ++orc_pool.nthreads;
     }
-    for (int t = 0; t < started; ++t) pthread_join(th[t], NULL);
+    int workers = orc_pool.nthreads + 1 < nthreads ? orc_pool.nthreads + 1 : nthreads;
+    const int per = (out_dim + workers - 1) / workers;
+    int njobs = 0;
+    for (int t = 0; t < workers; ++t) {
+        const int r0 = t * per, r1 = (t + 1) * per < out_dim ? (t + 1) * per : out_dim;
+        if (r0 >= r1) break;
+        orc_pool.jobs[t] = (orc_mv_job){W, S, B, x, y, out_dim, in_dim, gs, r0, r1};
+        ++njobs;
+    }
+    orc_pool.njobs = njobs;
+    orc_pool.pending = njobs - 1;
+    ++orc_pool.gen;
+    pthread_cond_broadcast(&orc_pool.go);
+    orc_mv_job j0 = orc_pool.jobs[0];
+    pthread_mutex_unlock(&orc_pool.mu);
+    orc_mv_worker(&j0);
+    pthread_mutex_lock(&orc_pool.mu);
+    while (orc_pool.pending > 0) pthread_cond_wait(&orc_pool.done, &orc_pool.mu);
+    pthread_mutex_unlock(&orc_pool.mu);
+    pthread_mutex_unlock(&orc_pool_call);
 }
 
 void orc_swiglu(const float *gate, const float *up, float *act, int n) {

@@ -46,6 +46,11 @@ void orc_expert_offsets(int hidden, int inter, int gs, size_t off[9]);
 void orc_matvec4bit_rows(const uint32_t *W, const uint16_t *S, const uint16_t *B,
                          const float *x, float *y, int out_dim, int in_dim, int gs,
                          int row0, int row1);
+/* The same rows with the 64 lanes innermost (vectorisable), bit-identical to
+ * orc_matvec4bit_rows; orc_matvec4bit and orc_matvec4bit_mt use it. */
+void orc_matvec4bit_rows_lanes(const uint32_t *W, const uint16_t *S, const uint16_t *B,
+                               const float *x, float *y, int out_dim, int in_dim, int gs,
+                               int row0, int row1);
 void orc_matvec4bit(const uint32_t *W, const uint16_t *S, const uint16_t *B,
                     const float *x, float *y, int out_dim, int in_dim, int gs);
 
@@ -82,7 +87,8 @@ int orc_moe_layer(const uint8_t *table, const uint16_t *router_bf16, const float
                   const float *residual, float *out, int B, int hidden, int inter, int E,
                   int K, int gs, int norm, int32_t *idx, float *w, int nthreads);
 
-/* Multi-threaded matvec for the CPU baseline: rows split over nthreads. */
+/* Multi-threaded matvec for the CPU baseline: rows split over nthreads of a
+ * persistent thread pool (threads are created once per process). */
 void orc_matvec4bit_mt(const uint32_t *W, const uint16_t *S, const uint16_t *B,
                        const float *x, float *y, int out_dim, int in_dim, int gs,
                        int nthreads);

@@ -1,12 +1,16 @@
-"""Expert parallelism over NVLink peer memory (m1moe_cuda_moe_layer_ep), 2 GPUs.
+"""Expert parallelism over NVLink peer memory (m1moe_cuda_moe_layer_ep) vs the CPU oracle.
 
-Two processes, one per GPU, each holding half of the experts; every rank owns
-two tokens.  Each call gathers all ranks' tokens inside the kernel, applies
-the local experts and returns each rank its own tokens' full output.  The
-result must equal the single-context MoE block (all experts) on the same
-tokens within the FFN tolerance, over several calls in a row (the exchange
-slots alternate between calls), with the residual added once.  Skipped when
-fewer than two GPUs are visible.
+One process per GPU, each holding world-th of the experts; every rank owns
+`b` tokens.  Each call gathers all ranks' tokens inside the kernel, applies
+the local experts and returns each rank its own tokens' full output
+(residual included, added once).  Every rank checks its tokens against the
+oracle (the C restatement of the reference's runLayer MoE arithmetic) on the
+same weights: expert indices equal wherever the logit gaps exceed 1e-5 and
+max |out - ref| <= 1e-3 ||ref||_2 on at least 90 % of the tokens, over
+several calls in a row (the exchange slots alternate between calls).
+Parametrised over world in {2, 4, 8} up to the visible GPU count, at a small
+shape and at Mixtral's (h 4096, I 14336, 8 experts, top-2 renormalised: one
+expert per GPU at world 8).  Skipped when fewer GPUs are visible.
 """
 from __future__ import annotations
 
@@ -20,7 +24,14 @@ import torch
 import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
-H, I, E, K, B = 512, 256, 8, 2, 2  # B tokens per rank
+TOL = 1e-3
+GAP = 1e-5
+
+SHAPES = {
+    # h, I, E, K, norm, tokens per rank, layers, calls
+    "small": (512, 256, 8, 2, True, 2, 2, 5),
+    "mixtral": (4096, 14336, 8, 2, True, 1, 1, 2),
+}
 
 
 def _port() -> int:
@@ -29,46 +40,61 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, shape, q):
     import torch.distributed as dist
 
+    import oracle
     from conftest import rel_max_err
     from m1moe_b200 import MoEBlock, synth
     from m1moe_b200.expert_parallel import EPFused, shard
+    H, I, E, K, norm, b, layers, calls = SHAPES[shape]
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     try:
+        oracle.build()
         torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
         dist.init_process_group("gloo", rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=60))
-        layers = 2
-        imgs = [synth.layer_image(40 + L, E, H, I, 64) for L in range(layers)]
+                                timeout=datetime.timedelta(seconds=120))
+        # the same images on every rank: the device generator is seeded alike
+        imgs = [synth.layer_image_device(E, H, I, 64, seed=40 + L, device=dev) for L in range(layers)]
         routers = [synth.router_weights(50 + L, E, H) for L in range(layers)]
         e0, ne = shard(E, world, rank)
-        kw = dict(hidden_dim=H, intermediate_dim=I, num_experts=E, top_k=K, num_layers=layers,
-                  norm_topk_prob=True, max_batch=world * B, device=rank)
-        part = MoEBlock(expert_begin=e0, expert_count=ne, **kw)
-        full = MoEBlock(**kw)
+        part = MoEBlock(hidden_dim=H, intermediate_dim=I, num_experts=E, top_k=K,
+                        num_layers=layers, norm_topk_prob=norm, max_batch=world * b, device=rank,
+                        expert_begin=e0, expert_count=ne)
         for L in range(layers):
-            for blk in (part, full):
-                blk.load_expert_layer(L, imgs[L])
-                blk.load_router(L, routers[L])
-        ep = EPFused(part, B)
-        errs = []
-        for call in range(5):
+            part.load_expert_layer(L, imgs[L])
+            part.load_router(L, routers[L])
+        host = [im.cpu().numpy() for im in imgs]
+        del imgs
+        ep = EPFused(part, b)
+        errs, checked, total = [], 0, 0
+        for call in range(calls):
             L = call % layers
-            xall = torch.from_numpy(synth.bf16_to_f32(synth.hidden_states(60 + call, world * B, H))).cuda()
-            own = xall[rank * B:(rank + 1) * B].contiguous()
-            res = own * 0.5
-            got = ep(L, own, res)
-            ref = full.forward(L, own, res)
+            xall = synth.bf16_to_f32(synth.hidden_states(60 + call, world * b, H))
+            own = xall[rank * b:(rank + 1) * b]
+            res = (own * 0.5).astype(np.float32)
+            idx = torch.zeros((world * b, K), dtype=torch.int32, device=dev)
+            got = ep(L, torch.from_numpy(own).to(dev), torch.from_numpy(res).to(dev), idx=idx)
             torch.cuda.synchronize()
-            part.synchronize()
-            errs.append(rel_max_err(got.cpu().numpy(), ref.cpu().numpy()))
-        q.put((rank, max(errs)))
+            part.synchronize()  # raises if a bounded device wait gave up
+            got = got.cpu().numpy()
+            idx = idx.cpu().numpy()[rank * b:(rank + 1) * b]
+            ref, ridx, _ = oracle.moe_layer(host[L], routers[L], own, res, h=H, inter=I, E=E, K=K,
+                                            gs=64, norm=norm, nthreads=4)
+            for t in range(b):
+                total += 1
+                scores = oracle.router_scores(routers[L], own[t])
+                srt = np.sort(scores)[::-1]
+                if srt[K - 1] - srt[K] > GAP:
+                    assert set(idx[t].tolist()) == set(ridx[t].tolist()), (call, t)
+                if set(idx[t].tolist()) == set(ridx[t].tolist()):
+                    errs.append(rel_max_err(got[t], ref[t]))
+                    checked += 1
+        q.put((rank, (max(errs) if errs else float("nan"), checked, total)))
         dist.barrier()
         part.close()
-        full.close()
     except Exception as exc:  # reported to the parent
         q.put((rank, f"{type(exc).__name__}: {exc}"))
     finally:
@@ -76,17 +102,19 @@ def _worker(rank, world, port, q):
             dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_expert_parallel_matches_single_context():
-    world = 2
+@pytest.mark.parametrize("shape", ["small", "mixtral"])
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_expert_parallel_vs_oracle(world, shape):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=300)
+        p.join(timeout=600)
     for p in procs:
         if p.is_alive():
             p.kill()
@@ -95,6 +123,9 @@ def test_fused_expert_parallel_matches_single_context():
     while not q.empty():
         r, v = q.get()
         res[r] = v
-    assert sorted(res) == [0, 1], res
+    assert sorted(res) == list(range(world)), res
     for r, v in res.items():
-        assert isinstance(v, float) and v < 1e-3, (r, v)
+        assert isinstance(v, tuple), (r, v)
+        err, checked, total = v
+        assert checked >= 0.9 * total, (r, checked, total)
+        assert err < TOL, (r, err)

@@ -85,6 +85,21 @@ def test_oracle_matvec_threads_identical(oracle_lib):
     assert np.array_equal(y1, y4)
 
 
+@pytest.mark.parametrize("out_dim,in_dim,gs", [(64, 512, 64), (37, 4096 + 512, 64),
+                                               (16, 8 * 72, 32), (8, 14336, 64)])
+def test_oracle_lane_vectorised_matvec_bit_identical(oracle_lib, out_dim, in_dim, gs):
+    """The lane-innermost matvec (used for the timed baseline and the large checks)
+    gives the same bits as the literal lanes-outermost restatement, including a
+    ragged last block of 64 words."""
+    rng = np.random.default_rng(out_dim + in_dim)
+    W, S, B, _ = synth.quant_matrix(rng, out_dim, in_dim, gs)
+    x = rng.normal(0.0, 1.0, size=in_dim).astype(np.float32)
+    y_plain = oracle_lib.matvec4bit_plain(W, S, B, x, gs)
+    for nt in (1, 3):
+        y = oracle_lib.matvec4bit(W, S, B, x, gs, nthreads=nt)
+        assert np.array_equal(y.view(np.uint32), y_plain.view(np.uint32)), nt
+
+
 @pytest.mark.parametrize("name", ["olmoe_tiny", "mixtral_tiny"])
 def test_layer_file_layout(golden, tmp_path, name):
     """The reference extractor's layer_NN.bin splits at our offsets into blocks whose

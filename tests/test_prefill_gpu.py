@@ -87,6 +87,24 @@ def test_prefill_mixtral_shape(oracle_lib):
                           norm=True)
 
 
+def test_prefill_mixtral_512_tokens(oracle_lib):
+    """The benchmarked prefill case (bench.py's `prefill`): Mixtral's layer shape
+    over 512 tokens, so every expert's token tiles are full-sized (~128 tokens
+    each).  A seeded sample of 48 tokens is checked against the oracle, with
+    the same bars and the same >= 90 % floor."""
+    h, I, E, K, T = 4096, 14336, 8, 2, 512
+    img = synth.layer_image_device(E, h, I, 64, seed=23, device="cuda").cpu().numpy()
+    router = synth.router_weights(24, E, h)
+    out, idx, w, xf, _ = _prefill_case(oracle_lib, img, router, h=h, I=I, E=E, K=K, norm=True,
+                                       T=T, seed=25)
+    # every expert got a full-sized share of the 1024 (token, expert) pairs
+    counts = np.bincount(idx.ravel(), minlength=E)
+    assert counts.min() >= 32, counts
+    pick = np.sort(np.random.default_rng(26).choice(T, size=48, replace=False))
+    _check_against_oracle(oracle_lib, img, router, out[pick], idx[pick], w[pick], xf[pick], None,
+                          h=h, I=I, E=E, K=K, norm=True)
+
+
 @pytest.mark.parametrize("xdt,odt", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16)])
 def test_prefill_dtypes_with_residual(golden, oracle_lib, xdt, odt):
     from golden.make_golden import router_weights

@@ -1,0 +1,534 @@
+// dense.cuh — the dense half of a decode step (sm_100a): BF16 GEMV with fused
+// RMSNorm / residual / argmax, and decode attention over a BF16 KV cache with
+// the QK-norm, RoPE and KV store fused in.
+//
+// Replaces the reference's per-layer CMD1/CMD2 Metal work and its CPU steps
+// (InferenceEngine.swift:167-238, 521-548; Shaders.metal:97-134 rmsNorm,
+// :153-163 residualAdd, :209-313 attention, :328-353 matvecBF16) and the LM
+// head + greedy sampling of forward() (:141-155, :550-555).
+//
+// GEMV (k_dense_gemv).  y[t][r] = W[r] . xn[t] for bf16 W [rows][K] and up to 8
+// tokens.  The reference gives every row a 64-thread threadgroup that walks
+// the row (Shaders.metal:340-352), reading x again per row.  Here the K
+// columns are split over the warps of a CTA, 256 per warp (8 bf16 = one
+// 16-byte load per lane per row), so every lane keeps its 8 columns of x --
+// RMS-normalised in the prologue when asked -- in registers for all rows,
+// and a CTA walks a contiguous block of rows U at a time (U 16-byte weight
+// loads in flight per lane; the first round is issued before waiting on the
+// previous kernel, since weights do not depend on it).  Per round the lanes'
+// U*NT partial dot products are reduced with one multi-value butterfly; per
+// 64-row chunk the warps' partials are added in shared memory in warp order.
+// Epilogues: store (+ residual, which may alias y); store + RMSNorm of the
+// finished rows into a second buffer by the last CTA (the post-attention
+// norm feeding the MoE block); argmax over the rows (the LM head's greedy
+// sample, ties to the lower index), where the last CTA also writes the next
+// step's embedding.  Accumulation is fp32 FMA on exact bf16->f32 upcasts.
+//
+// Attention (k_attn_decode).  One CTA per (token, KV head, position split):
+// its q heads (the GQA group) are loaded, head-RMS-normalised (OLMoE's QK-norm,
+// with the first head_dim weights as the reference does) and rotated (RoPE,
+// half-split pairs, pos * theta^(-2i/hd)); the CTA whose split holds `pos`
+// also normalises and rotates k and writes k and v, as bf16, into the cache.
+// Four warps stream the split's K and V rows (8 positions per warp round, all
+// loads in flight), score them (q.k * scale), and keep an online softmax
+// (running max, sum and weighted V); the last CTA of a (token, KV head)
+// merges the splits' partials into the attention output.  The position is
+// read from device memory, so a captured step can be replayed while the
+// position advances (the LM head's last CTA adds one).
+#pragma once
+
+#include <math.h>
+
+#include "common.cuh"
+#include "pipeline.cuh"
+
+namespace m1 {
+
+constexpr int kGemvColsPerWarp = 256;  // 32 lanes x 8 bf16
+constexpr int kGemvChunkRows = 64;     // rows per shared-memory reduction round
+constexpr int kGemvMaxWarps = 32;      // K <= 8192
+constexpr int kDenseMaxTok = 8;
+
+enum GemvEpi { kEpiStore = 0, kEpiPostNorm = 1, kEpiArgmax = 2 };
+
+struct GemvParams {
+    const uint16_t *w;  // bf16 [rows][K]
+    int rows, K;
+    const void *x;      // [ntok][K], f32 or bf16
+    int x_bf16;
+    const uint16_t *norm_w;  // RMS-normalise x first with this bf16 [K] weight, or null
+    float eps;
+    float *y;           // [ntok][rows] f32 (argmax: may be null)
+    const float *res;   // added to y, [ntok][rows] (may alias y), or null
+    int ntok;
+    // kEpiPostNorm: the last CTA writes post_out[t] = rmsnorm(y[t]) * post_w
+    const uint16_t *post_w;
+    float *post_out;
+    float *ss_acc;      // [kDenseMaxTok] sums of squares of y (zero between calls)
+    unsigned *done;     // CTAs finished (zero between calls)
+    // kEpiArgmax: keys[t] = max over rows of {ordered logit, ~row}; the last
+    // CTA writes tokens[t] and, with embed, embed_out[t] = embed[tokens[t]]
+    unsigned long long *keys;  // [kDenseMaxTok] (zero between calls)
+    int32_t *tokens;
+    const uint16_t *embed;     // bf16 [vocab][embed_dim], or null
+    float *embed_out;
+    int embed_dim;
+    int *pos;           // device position, advanced by the argmax's last CTA (or null)
+};
+
+__device__ __forceinline__ float dot8_bf16(const uint4 w, const float (&x)[8], float acc) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        acc = fmaf(__uint_as_float(ws[i] << 16), x[2 * i], acc);
+        acc = fmaf(__uint_as_float(ws[i] & 0xFFFF0000u), x[2 * i + 1], acc);
+    }
+    return acc;
+}
+
+// Ordered key of a logit for a max-reduction: larger value first, then the
+// lower row (the reference's `if logits[i] > bestV` keeps the first maximum,
+// InferenceEngine.swift:552-555); NaN lowest, -0 equal to +0.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+    const uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
+    uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    if (v != v) ord = 0u;
+    return ((unsigned long long)ord << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)row);
+}
+
+// This lane's 8 columns of token t's x, as f32.
+__device__ __forceinline__ void load_x8(const void *x, int x_bf16, size_t off, float (&v)[8]) {
+    if (x_bf16) {
+        const uint4 r = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(x) + off);
+        const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[2 * j] = __uint_as_float(rr[j] << 16);
+            v[2 * j + 1] = __uint_as_float(rr[j] & 0xFFFF0000u);
+        }
+    } else {
+        const float4 *f = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + off);
+        const float4 a = f[0], b = f[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+}
+
+// Rows per round for NT tokens: U*NT values per warp reduction (<= 32).
+template <int NT>
+struct GemvRound {
+    static constexpr int U = NT <= 4 ? 8 : 4;
+};
+
+// Dynamic shared memory of k_dense_gemv: the warps' partials of one chunk.
+__host__ __device__ inline size_t gemv_smem(int nwarps, int nt) {
+    return (size_t)nwarps * kGemvChunkRows * nt * 4;
+}
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__(1024) k_dense_gemv(const GemvParams p) {
+    constexpr int U = GemvRound<NT>::U, NV = U * NT, kS = 32 / NV;
+    extern __shared__ __align__(16) float part[];  // [nw][kGemvChunkRows][NT]
+    __shared__ float red[kGemvMaxWarps][NT];
+    __shared__ unsigned long long kred[NT];
+    __shared__ int is_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int G = gridDim.x, K = p.K;
+    const int c0 = warp * kGemvColsPerWarp + lane * 8;
+    const int r0 = (int)((long long)p.rows * blockIdx.x / G);
+    const int r1 = (int)((long long)p.rows * (blockIdx.x + 1) / G);
+    pdl_trigger();
+    uint4 wv[U];
+    auto load_round = [&](int r) {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            wv[u] = (r + u < r1) ? ld_stream16(p.w + (size_t)(r + u) * K + c0) : make_uint4(0, 0, 0, 0);
+    };
+    // the weights are constants: the first round goes out before the wait
+    if (r0 < r1) load_round(r0);
+    pdl_wait();
+    float xr[NT][8];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (t < p.ntok) {
+            load_x8(p.x, p.x_bf16, (size_t)t * K + c0, xr[t]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) xr[t][j] = 0.f;
+        }
+    }
+    if (p.norm_w) {
+        // RMSNorm (Shaders.metal:97-134): x * rsqrt(mean(x^2) + eps) * w
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float s = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s = fmaf(xr[t][j], xr[t][j], s);
+            s = warp_sum(s);
+            if (lane == 0) red[warp][t] = s;
+        }
+        __syncthreads();
+        float nwv[8];
+        {
+            const uint4 r = *reinterpret_cast<const uint4 *>(p.norm_w + c0);
+            const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                nwv[2 * j] = __uint_as_float(rr[j] << 16);
+                nwv[2 * j + 1] = __uint_as_float(rr[j] & 0xFFFF0000u);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float ss = 0.f;
+            for (int w = 0; w < nw; ++w) ss += red[w][t];
+            const float rms = rsqrtf(ss / (float)K + p.eps);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) xr[t][j] = (xr[t][j] * rms) * nwv[j];
+        }
+    }
+    float ssl[NT];  // post-norm: sums of squares of this thread's outputs
+    unsigned long long kmax[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        ssl[t] = 0.f;
+        kmax[t] = 0ull;
+    }
+    for (int cr = r0; cr < r1; cr += kGemvChunkRows) {
+        const int ce = min(cr + kGemvChunkRows, r1);
+        for (int r = cr; r < ce; r += U) {
+            float acc[NV];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) acc[u * NT + t] = dot8_bf16(wv[u], xr[t], 0.f);
+            // the next round's loads are in flight during the reduction
+            if (r + U < r1) load_round(r + U);
+            const float tot = warp_reduce_multi(acc);
+            if (lane % kS == 0) {
+                const int v = lane / kS, u = v / NT, t = v - u * NT;
+                if (r + u < ce) part[((size_t)warp * kGemvChunkRows + (r + u - cr)) * NT + t] = tot;
+            }
+        }
+        __syncthreads();
+        const int nrow = ce - cr;
+        for (int i = tid; i < nrow * NT; i += blockDim.x) {
+            const int rr = i / NT, t = i - rr * NT, row = cr + rr;
+            float v = 0.f;
+            for (int w = 0; w < nw; ++w) v += part[((size_t)w * kGemvChunkRows + rr) * NT + t];
+            if (t >= p.ntok) continue;
+            const size_t o = (size_t)t * p.rows + row;
+            if (p.res) v += p.res[o];
+            if (p.y) p.y[o] = v;
+            if constexpr (EPI == kEpiPostNorm) ssl[t] = fmaf(v, v, ssl[t]);
+            if constexpr (EPI == kEpiArgmax) {
+                const unsigned long long k = argmax_key(v, row);
+                kmax[t] = k > kmax[t] ? k : kmax[t];
+            }
+        }
+        __syncthreads();
+    }
+    if constexpr (EPI == kEpiStore) return;
+    // ---- the CTA's contribution, then the last CTA finishes the call ----
+    if constexpr (EPI == kEpiPostNorm) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const float s = warp_sum(ssl[t]);
+            if (lane == 0) red[warp][t] = s;
+        }
+        __syncthreads();
+        if (tid < p.ntok) {
+            float s = 0.f;
+            for (int w = 0; w < nw; ++w) s += red[w][tid];
+            atomicAdd(p.ss_acc + tid, s);
+        }
+    } else {
+        if (tid < NT) kred[tid] = 0ull;
+        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+            if (kmax[t]) atomicMax(&kred[t], kmax[t]);
+        __syncthreads();
+        if (tid < p.ntok) atomicMax(p.keys + tid, kred[tid]);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        is_last = atomicAdd(p.done, 1u) == (unsigned)G - 1u;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    if constexpr (EPI == kEpiPostNorm) {
+        const int n = p.rows;
+        for (int i = tid; i < p.ntok * n; i += blockDim.x) {
+            const int t = i / n, c = i - t * n;
+            const float rms = rsqrtf(__ldcg(p.ss_acc + t) / (float)n + p.eps);
+            p.post_out[i] = (__ldcg(p.y + i) * rms) * bf16_bits(p.post_w[c]);
+        }
+        __syncthreads();
+        if (tid < kDenseMaxTok) p.ss_acc[tid] = 0.f;
+    } else {
+        __shared__ int tok[kDenseMaxTok];
+        if (tid < p.ntok) {
+            const unsigned long long k = __ldcg(p.keys + tid);
+            tok[tid] = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+            if (p.tokens) p.tokens[tid] = tok[tid];
+        }
+        __syncthreads();
+        if (p.embed)
+            for (int i = tid; i < p.ntok * p.embed_dim; i += blockDim.x) {
+                const int t = i / p.embed_dim, c = i - t * p.embed_dim;
+                p.embed_out[i] = bf16_bits(p.embed[(size_t)tok[t] * p.embed_dim + c]);
+            }
+        __syncthreads();
+        if (tid < kDenseMaxTok) p.keys[tid] = 0ull;
+        if (tid == 0 && p.pos) *p.pos += 1;
+    }
+    if (tid == 0) *p.done = 0u;
+}
+
+// ---------------------------------------------------------------- embed ----
+// residual[t] = embed[token[t]] (InferenceEngine.swift:482-488); an id
+// outside the vocabulary sets the error word and reads row 0.
+__global__ void k_embed(const uint16_t *embed, const int32_t *tokens, int vocab, int h, float *out,
+                        int ntok, int *err) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x;
+    if (t >= ntok) return;
+    int tok = tokens[t];
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0 && err) atomicOr(err, kErrBadExpert);
+        tok = 0;
+    }
+    for (int i = threadIdx.x; i < h; i += blockDim.x)
+        out[(size_t)t * h + i] = bf16_bits(embed[(size_t)tok * h + i]);
+}
+
+// ------------------------------------------------------------ attention ----
+constexpr int kHeadDim = 128;   // dims per head (32 lanes x 4)
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * 32;
+
+struct AttnParams {
+    const float *qkv;   // [ntok][qkv_stride]: q [nh*hd] | k [nkv*hd] | v [nkv*hd]
+    int qkv_stride;
+    int nh, nkv, ntok;
+    const int *pos;     // device position of this step (the new token's index)
+    int max_seq;
+    const uint16_t *qn_w, *kn_w;  // QK-norm weights (bf16, first hd used), or null
+    float eps, theta, scale;
+    uint16_t *kc, *vc;  // this layer's caches, bf16 [max_batch][nkv][max_seq][hd]
+    int nsplit;         // position splits (gridDim.x)
+    float *part;        // [ntok][nh][nsplit][hd + 2]: unnormalised o, max, sum
+    unsigned *cnt;      // [kDenseMaxTok][nkv] splits finished (zero between calls)
+    float *out;         // [ntok][nh*hd]
+    int *err;
+};
+
+// Per-head RMSNorm of a 128-dim head held 4 per lane (InferenceEngine.swift
+// :538-548: the first hd weights of the norm apply to every head).
+__device__ __forceinline__ void head_rmsnorm(float (&v)[4], const uint16_t *w, float eps) {
+    const int lane = threadIdx.x & 31;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s = fmaf(v[i], v[i], s);
+    s = warp_sum(s);
+    const float rms = 1.0f / sqrtf(s / (float)kHeadDim + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] *= rms * bf16_bits(w[4 * lane + i]);
+}
+
+// RoPE on a head held 4 per lane (InferenceEngine.swift:521-536): pairs
+// (i, i + hd/2) -- lanes l and l ^ 16 -- rotate by pos * theta^(-2i/hd).
+__device__ __forceinline__ void head_rope(float (&v)[4], int pos, float theta) {
+    const int lane = threadIdx.x & 31;
+    const bool lo = lane < 16;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[i], 16);
+        const int pair = 4 * (lane & 15) + i;
+        const float freq = 1.0f / powf(theta, (float)(2 * pair) / (float)kHeadDim);
+        const float ang = (float)pos * freq;
+        const float c = cosf(ang), s = sinf(ang);
+        // lo: x0' = x0 c - x1 s; hi: x1' = x0 s + x1 c
+        v[i] = lo ? (v[i] * c - other * s) : (other * s + v[i] * c);
+    }
+}
+
+__device__ __forceinline__ void load4(const float *p, float (&v)[4]) {
+    const float4 a = *reinterpret_cast<const float4 *>(p);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+
+__device__ __forceinline__ uint2 pack4_bf16(const float (&v)[4]) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 r;
+    r.x = *reinterpret_cast<const uint32_t *>(&a);
+    r.y = *reinterpret_cast<const uint32_t *>(&b);
+    return r;
+}
+
+// HP: q heads per KV head (the GQA group size), 1..8.
+template <int HP>
+__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p) {
+    constexpr int P = HP <= 4 ? 8 : 4;  // positions per warp round (P*HP <= 32)
+    constexpr int NV = P * HP, kS = 32 / NV;
+    const int split = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ float sm_m[kAttnWarps][HP], sm_l[kAttnWarps][HP];
+    __shared__ __align__(16) float sm_o[kAttnWarps][HP][kHeadDim];
+    __shared__ int is_last;
+    pdl_trigger();
+    pdl_wait();
+    const int pos = *p.pos;
+    const int seq = pos + 1;
+    const int hd = kHeadDim, qd = p.nh * hd, kvd = p.nkv * hd;
+    // this split's positions: seq cut into nsplit runs of a multiple of 32
+    const int slen = ((seq + p.nsplit - 1) / p.nsplit + 31) & ~31;
+    const int p0 = split * slen, p1 = min(seq, p0 + slen);
+    if (pos < 0 || pos >= p.max_seq) {
+        if (threadIdx.x == 0 && split == 0 && g == 0 && t == 0) atomicOr(p.err, kErrBadExpert);
+        return;
+    }
+    const float *qt = p.qkv + (size_t)t * p.qkv_stride;
+    float q[HP][4];
+#pragma unroll
+    for (int hh = 0; hh < HP; ++hh) {
+        load4(qt + (size_t)(g * HP + hh) * hd + 4 * lane, q[hh]);
+        if (p.qn_w) head_rmsnorm(q[hh], p.qn_w, p.eps);
+        head_rope(q[hh], pos, p.theta);
+    }
+    const size_t slab = ((size_t)t * p.nkv + g) * p.max_seq * hd;
+    uint16_t *kb = p.kc + slab, *vb = p.vc + slab;
+    if (warp == 0 && p0 <= pos && pos < p1) {
+        // the new token's k (QK-norm, RoPE) and v into the cache, as bf16
+        float k[4], v[4];
+        load4(qt + qd + (size_t)g * hd + 4 * lane, k);
+        load4(qt + qd + kvd + (size_t)g * hd + 4 * lane, v);
+        if (p.kn_w) head_rmsnorm(k, p.kn_w, p.eps);
+        head_rope(k, pos, p.theta);
+        *reinterpret_cast<uint2 *>(kb + (size_t)pos * hd + 4 * lane) = pack4_bf16(k);
+        *reinterpret_cast<uint2 *>(vb + (size_t)pos * hd + 4 * lane) = pack4_bf16(v);
+    }
+    __syncthreads();  // the stores above reach this CTA's loads below
+    float m[HP], l[HP], o[HP][4];
+#pragma unroll
+    for (int hh = 0; hh < HP; ++hh) {
+        m[hh] = -INFINITY;
+        l[hh] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[hh][i] = 0.f;
+    }
+    for (int pb = p0 + warp * P; pb < p1; pb += kAttnWarps * P) {
+        uint2 kw[P], vw[P];
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+            const int pp = pb + j;
+            if (pp < p1) {
+                kw[j] = *reinterpret_cast<const uint2 *>(kb + (size_t)pp * hd + 4 * lane);
+                vw[j] = *reinterpret_cast<const uint2 *>(vb + (size_t)pp * hd + 4 * lane);
+            } else {
+                kw[j] = vw[j] = make_uint2(0, 0);
+            }
+        }
+        float acc[NV];
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+            const float k0 = __uint_as_float(kw[j].x << 16), k1 = __uint_as_float(kw[j].x & 0xFFFF0000u);
+            const float k2 = __uint_as_float(kw[j].y << 16), k3 = __uint_as_float(kw[j].y & 0xFFFF0000u);
+#pragma unroll
+            for (int hh = 0; hh < HP; ++hh)
+                acc[j * HP + hh] = fmaf(q[hh][3], k3, fmaf(q[hh][2], k2, fmaf(q[hh][1], k1, q[hh][0] * k0)));
+        }
+        const float tot = warp_reduce_multi(acc);  // lane holds value lane / kS
+#pragma unroll
+        for (int hh = 0; hh < HP; ++hh) {
+            float s[P];
+            float mx = m[hh];
+#pragma unroll
+            for (int j = 0; j < P; ++j) {
+                s[j] = __shfl_sync(0xffffffffu, tot, (j * HP + hh) * kS) * p.scale;
+                if (pb + j >= p1) s[j] = -INFINITY;
+                mx = fmaxf(mx, s[j]);
+            }
+            const float corr = expf(m[hh] - mx);  // 0 on the first round (m = -inf)
+            l[hh] *= corr;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[hh][i] *= corr;
+#pragma unroll
+            for (int j = 0; j < P; ++j) {
+                const float e = expf(s[j] - mx);
+                l[hh] += e;
+                const float v0 = __uint_as_float(vw[j].x << 16), v1 = __uint_as_float(vw[j].x & 0xFFFF0000u);
+                const float v2 = __uint_as_float(vw[j].y << 16), v3 = __uint_as_float(vw[j].y & 0xFFFF0000u);
+                o[hh][0] = fmaf(e, v0, o[hh][0]);
+                o[hh][1] = fmaf(e, v1, o[hh][1]);
+                o[hh][2] = fmaf(e, v2, o[hh][2]);
+                o[hh][3] = fmaf(e, v3, o[hh][3]);
+            }
+            m[hh] = mx;
+        }
+    }
+    // merge the warps, then write this split's partial
+#pragma unroll
+    for (int hh = 0; hh < HP; ++hh) {
+        if (lane == 0) {
+            sm_m[warp][hh] = m[hh];
+            sm_l[warp][hh] = l[hh];
+        }
+        *reinterpret_cast<float4 *>(&sm_o[warp][hh][4 * lane]) = make_float4(o[hh][0], o[hh][1], o[hh][2], o[hh][3]);
+    }
+    __syncthreads();
+    const int hd2 = hd + 2;
+    for (int i = threadIdx.x; i < HP * hd; i += kAttnThreads) {
+        const int hh = i / hd, d = i - hh * hd;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][hh]);
+        float L = 0.f, O = 0.f;
+        if (M > -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kAttnWarps; ++w) {
+                const float f = expf(sm_m[w][hh] - M);
+                L = fmaf(sm_l[w][hh], f, L);
+                O = fmaf(sm_o[w][hh][d], f, O);
+            }
+        }
+        float *dst = p.part + (((size_t)t * p.nh + g * HP + hh) * p.nsplit + split) * hd2;
+        dst[d] = O;
+        if (d == 0) {
+            dst[hd] = M;
+            dst[hd + 1] = L;
+        }
+    }
+    // the last split of (t, g) merges all splits into the output
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        unsigned *c = p.cnt + (size_t)t * p.nkv + g;
+        is_last = atomicAdd(c, 1u) == (unsigned)p.nsplit - 1u;
+        if (is_last) *c = 0u;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < HP * hd; i += kAttnThreads) {
+        const int hh = i / hd, d = i - hh * hd;
+        const float *src = p.part + ((size_t)t * p.nh + g * HP + hh) * p.nsplit * hd2;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < p.nsplit; ++s2) M = fmaxf(M, __ldcg(src + (size_t)s2 * hd2 + hd));
+        float L = 0.f, O = 0.f;
+        for (int s2 = 0; s2 < p.nsplit; ++s2) {
+            const float ms = __ldcg(src + (size_t)s2 * hd2 + hd);
+            if (ms == -INFINITY) continue;
+            const float f = expf(ms - M);
+            L = fmaf(__ldcg(src + (size_t)s2 * hd2 + hd + 1), f, L);
+            O = fmaf(__ldcg(src + (size_t)s2 * hd2 + d), f, O);
+        }
+        p.out[(size_t)t * p.nh * hd + (size_t)(g * HP + hh) * hd + d] = O / L;
+    }
+}
+
+}  // namespace m1

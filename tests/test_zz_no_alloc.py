@@ -43,17 +43,17 @@ def _noalloc(router_dev, E, h, K, norm, x, B):
     return idx.cpu().numpy(), w.cpu().numpy(), scores.cpu().numpy()
 
 
-def _check_vs_oracle(idx, w, scores, router, x_f32, K, norm):
+def _check_vs_oracle(idx, w, scores, router, x_f32, K, norm, tol=W_TOL):
     """Experts equal to the oracle's wherever the K-th and (K+1)-th scores are
     more than GAP apart (and in order where neighbours are), weights and
-    scores within W_TOL relative."""
+    scores within `tol` relative."""
     import oracle
     oracle.build()
     checked = 0
     for t in range(idx.shape[0]):
         ref_s = oracle.router_scores(router, x_f32[t])
         ref_i, ref_w = oracle.select_topk(ref_s, K, norm)
-        assert np.all(np.abs(scores[t] - ref_s) <= W_TOL * np.abs(ref_s) + 1e-7), t
+        assert np.all(np.abs(scores[t] - ref_s) <= tol * np.abs(ref_s) + 1e-7), t
         srt = np.sort(ref_s)[::-1]
         if K < len(ref_s) and srt[K - 1] - srt[K] <= GAP:
             continue
@@ -63,7 +63,7 @@ def _check_vs_oracle(idx, w, scores, router, x_f32, K, norm):
             if k == 0 or srt[k - 1] - srt[k] > GAP:
                 assert idx[t][k] == ref_i[k], (t, k)
         wd, rd = dict(zip(idx[t].tolist(), w[t].tolist())), dict(zip(ref_i.tolist(), ref_w.tolist()))
-        assert all(abs(wd[e] - rd[e]) <= W_TOL * abs(rd[e]) + 1e-7 for e in rd), t
+        assert all(abs(wd[e] - rd[e]) <= tol * abs(rd[e]) + 1e-7 for e in rd), t
     assert checked >= max(1, (9 * idx.shape[0]) // 10), checked
 
 
@@ -94,13 +94,15 @@ def test_noalloc_router_matches_context_router(E, K, h, norm, B):
 
 def test_noalloc_router_wide_hidden():
     """Routing stages nothing that grows with the hidden size, so a 32768-wide
-    router (beyond any model shape here) routes as well."""
+    router (beyond any model shape here) routes as well.  A logit here sums 16x
+    more terms than at h 2048, in another order than the oracle's, so scores
+    and weights are held to 1e-4 relative (experts still exactly)."""
     E, K, h, B = 16, 4, 32768, 4
     router = synth.router_weights(77, E, h)
     xb = synth.hidden_states(78, B, h)
     x = torch.from_numpy(synth.bf16_to_f32(xb)).cuda()
     idx, w, s = _noalloc(_dev_bf16(router), E, h, K, True, x, B)
-    _check_vs_oracle(idx, w, s, router, synth.bf16_to_f32(xb), K, True)
+    _check_vs_oracle(idx, w, s, router, synth.bf16_to_f32(xb), K, True, tol=1e-4)
 
 
 def test_noalloc_router_rejects_null_status_and_sizes_beyond_its_scratch():

@@ -286,6 +286,130 @@ M1MOE_API int64_t m1moe_cuda_launch_count(void);
  * row range (first | end << 32) and its tile counts (gate/up | down << 32). */
 M1MOE_API m1moe_status m1moe_cuda_set_trace(m1moe_cuda_ctx *ctx, uint64_t *d_trace);
 
+/* ===================== the dense half of a decode step =====================
+ * The reference runs the non-MoE part of a layer as two Metal command buffers
+ * with CPU work between them (InferenceEngine.swift:167-238): CMD1 = input
+ * RMSNorm + q/k/v matvecBF16 (Shaders.metal:97-134, :328-353), then on the CPU
+ * QK-norm (OLMoE), RoPE and the KV store (:194-220, :521-548), then CMD2 =
+ * attention scores/softmax/values, o_proj, residual add and the post-attention
+ * RMSNorm (:222-238; Shaders.metal:153-163, :209-313); forward() ends with the
+ * final RMSNorm, the LM head and greedy sampling (:140-155, :550-555).  The
+ * entry points below replace those encoders and CPU steps; a dense context
+ * owns the non-expert weights (WeightStore's mmap, WeightStore.swift:47-126),
+ * the bf16 KV cache and the step buffers (MetalContext.swift:134-152). */
+
+typedef struct m1moe_dense_cfg {
+    int32_t hidden_dim;
+    int32_t num_heads;      /* attention.numHeads                                  */
+    int32_t num_kv_heads;   /* attention.numKvHeads (GQA when < num_heads)          */
+    int32_t head_dim;       /* 128                                                 */
+    int32_t num_layers;
+    int32_t vocab_size;
+    int32_t qk_norm;        /* per-head RMSNorm of q and k (architecture "olmoe")  */
+    float rms_norm_eps;
+    float rope_theta;
+    int32_t max_batch;      /* sequences decoded together, 1..8                    */
+    int32_t max_seq;        /* KV cache positions per sequence                    */
+    int32_t device;
+} m1moe_dense_cfg;
+
+/* Tensor names of m1moe_cuda_dense_load (the reference's model_weights.json
+ * keys, InferenceEngine.swift:577-598; bf16 in the model file). */
+typedef enum m1moe_dense_tensor {
+    M1MOE_W_EMBED = 0,       /* model.embed_tokens.weight [vocab][h]            */
+    M1MOE_W_FINAL_NORM = 1,  /* model.norm.weight [h]                           */
+    M1MOE_W_LM_HEAD = 2,     /* lm_head.weight [vocab][h]                       */
+    M1MOE_W_INPUT_NORM = 3,  /* layers.L.input_layernorm.weight [h]             */
+    M1MOE_W_POST_NORM = 4,   /* layers.L.post_attention_layernorm.weight [h]    */
+    M1MOE_W_Q = 5,           /* layers.L.self_attn.q_proj.weight [nh*hd][h]     */
+    M1MOE_W_K = 6,           /* layers.L.self_attn.k_proj.weight [nkv*hd][h]    */
+    M1MOE_W_V = 7,           /* layers.L.self_attn.v_proj.weight [nkv*hd][h]    */
+    M1MOE_W_O = 8,           /* layers.L.self_attn.o_proj.weight [h][nh*hd]     */
+    M1MOE_W_Q_NORM = 9,      /* layers.L.self_attn.q_norm.weight [nh*hd] or [hd] */
+    M1MOE_W_K_NORM = 10      /* layers.L.self_attn.k_norm.weight [nkv*hd] or [hd] */
+} m1moe_dense_tensor;
+
+typedef struct m1moe_dense_ctx m1moe_dense_ctx;
+
+/* Create a dense context: weights, the bf16 KV cache [layers][max_batch]
+ * [num_kv_heads][max_seq][head_dim] (zeroed), the step buffers and a device
+ * position counter at 0.  Replaces MetalContext's dense buffers
+ * (MetalContext.swift:134-152) and WeightStore's Metal buffer (:119-126). */
+M1MOE_API m1moe_status m1moe_cuda_dense_create(const m1moe_dense_cfg *cfg, m1moe_dense_ctx **out_ctx);
+M1MOE_API m1moe_status m1moe_cuda_dense_destroy(m1moe_dense_ctx *ctx);
+
+/* Copy one bf16 tensor (host memory, e.g. WeightStore's mmap) into the
+ * context; `layer` is ignored for the model-wide tensors.  QK-norm weights
+ * may be given whole ([nh*hd] / [nkv*hd]) or as their first head_dim values:
+ * the reference applies the first head_dim to every head
+ * (InferenceEngine.swift:538-548). */
+M1MOE_API m1moe_status m1moe_cuda_dense_load(m1moe_dense_ctx *ctx, int32_t tensor, int32_t layer,
+                                   const uint16_t *h_bf16, size_t count);
+/* The same from device memory (stream-ordered). */
+M1MOE_API m1moe_status m1moe_cuda_dense_load_device(m1moe_dense_ctx *ctx, int32_t tensor, int32_t layer,
+                                          const uint16_t *d_bf16, size_t count, void *stream);
+
+/* Device pointers of one layer's K and V caches, bf16
+ * [max_batch][num_kv_heads][max_seq][head_dim], for callers that prefill them. */
+M1MOE_API m1moe_status m1moe_cuda_dense_kv_cache(m1moe_dense_ctx *ctx, int32_t layer, void **d_k,
+                                       void **d_v);
+
+/* The position of the next token (the reference's seqPos,
+ * InferenceEngine.swift:23-24): set (synchronous), read (synchronous), and
+ * reset() = zero the KV cache and the position (:159-163). */
+M1MOE_API m1moe_status m1moe_cuda_dense_set_position(m1moe_dense_ctx *ctx, int32_t pos);
+M1MOE_API m1moe_status m1moe_cuda_dense_get_position(m1moe_dense_ctx *ctx, int32_t *pos);
+M1MOE_API m1moe_status m1moe_cuda_dense_reset(m1moe_dense_ctx *ctx);
+
+/* Wait for the device and report (then clear) the dense context's error
+ * word: M1MOE_ERR_DEVICE if a token id or the position was out of range. */
+M1MOE_API m1moe_status m1moe_cuda_dense_synchronize(m1moe_dense_ctx *ctx);
+
+/* y[t] = W . xn[t] (+ res[t]) for bf16 W [rows][in_dim] and `batch` tokens
+ * (1..8), xn = x or, with d_norm_w, RMSNorm(x) * norm_w.  Replaces matvecBF16
+ * (Shaders.metal:328-353), with the RMSNorm (:97-134) and residual add
+ * (:153-163) fused.  in_dim a multiple of 256 (<= 8192); d_w and d_x 16-byte
+ * aligned; d_res may alias d_y; y and res are f32 [batch][rows]. */
+M1MOE_API m1moe_status m1moe_cuda_dense_gemv(const uint16_t *d_w, int32_t rows, int32_t in_dim,
+                                   const void *d_x, int32_t x_dtype, const uint16_t *d_norm_w,
+                                   float eps, const float *d_res, float *d_y, int32_t batch,
+                                   void *stream);
+
+/* y[t] = x[t] * rsqrt(mean(x[t]^2) + eps) * w (rmsNormSum + rmsNormApply,
+ * Shaders.metal:97-134), f32 out, `batch` rows of `dim`. */
+M1MOE_API m1moe_status m1moe_cuda_dense_rmsnorm(const void *d_x, int32_t x_dtype, const uint16_t *d_w,
+                                      float eps, float *d_y, int32_t dim, int32_t batch,
+                                      void *stream);
+
+/* One layer's attention for `batch` sequences at the context's position:
+ * from the q|k|v projections (f32 [batch][(nh + 2 nkv) * hd]) it applies the
+ * QK-norm (if configured), RoPE, stores k and v (bf16) at the position and
+ * attends over positions 0..pos (softmax(q.k / sqrt(hd)) . v, GQA groups of
+ * nh / nkv heads), writing f32 [batch][nh * hd].  Replaces the CPU steps of
+ * InferenceEngine.swift:194-220 and encodeAttention (:349-399,
+ * Shaders.metal:209-313).  It does not advance the position. */
+M1MOE_API m1moe_status m1moe_cuda_dense_attention(m1moe_dense_ctx *ctx, int32_t layer, const float *d_qkv,
+                                        int32_t batch, float *d_out, void *stream);
+
+/* Final RMSNorm + LM head + greedy sample (InferenceEngine.swift:140-155,
+ * :550-555: the first maximum wins): d_tokens[t] = argmax_v logits[t][v].
+ * d_logits (f32 [batch][vocab]) may be NULL. */
+M1MOE_API m1moe_status m1moe_cuda_dense_lm_head(m1moe_dense_ctx *ctx, const float *d_x, int32_t batch,
+                                      int32_t *d_tokens, float *d_logits, void *stream);
+
+/* One whole decode step for `batch` sequences (stream-ordered, capturable in a
+ * CUDA graph): embed d_tokens, then per layer the input RMSNorm + q/k/v,
+ * QK-norm + RoPE + KV store + attention, o_proj + residual + post-attention
+ * RMSNorm, and the MoE block of `moe` (m1moe_cuda_moe_layer on this layer);
+ * then the final norm, the LM head and the greedy next tokens
+ * (d_next_tokens [batch]; d_logits [batch][vocab] may be NULL), and the
+ * device position advances by one.  Replaces InferenceEngine.forward
+ * (:124-156) at temperature 0.  `moe` must have the same hidden size, layer
+ * count and device, and max_batch >= batch. */
+M1MOE_API m1moe_status m1moe_cuda_decode_step(m1moe_dense_ctx *ctx, m1moe_cuda_ctx *moe,
+                                    const int32_t *d_tokens, int32_t batch, int32_t *d_next_tokens,
+                                    float *d_logits, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

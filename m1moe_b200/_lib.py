@@ -33,6 +33,19 @@ class Cfg(ctypes.Structure):
         "norm_topk_prob", "max_batch", "device", "expert_begin", "expert_count")]
 
 
+class DenseCfg(ctypes.Structure):
+    _fields_ = [("hidden_dim", ctypes.c_int32), ("num_heads", ctypes.c_int32),
+                ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("num_layers", ctypes.c_int32), ("vocab_size", ctypes.c_int32),
+                ("qk_norm", ctypes.c_int32), ("rms_norm_eps", ctypes.c_float),
+                ("rope_theta", ctypes.c_float), ("max_batch", ctypes.c_int32),
+                ("max_seq", ctypes.c_int32), ("device", ctypes.c_int32)]
+
+
+# m1moe_dense_tensor
+W_EMBED, W_FINAL_NORM, W_LM_HEAD, W_INPUT_NORM, W_POST_NORM = 0, 1, 2, 3, 4
+W_Q, W_K, W_V, W_O, W_Q_NORM, W_K_NORM = 5, 6, 7, 8, 9, 10
+
 _lib = None
 
 # (name, restype, argtypes) for every entry point in include/m1moe_cuda.h.
@@ -67,6 +80,23 @@ _SIGS = [
     ("m1moe_cuda_synchronize", ctypes.c_int, [_vp]),
     ("m1moe_cuda_launch_count", ctypes.c_int64, []),
     ("m1moe_cuda_set_trace", ctypes.c_int, [_vp, _vp]),
+    ("m1moe_cuda_dense_create", ctypes.c_int, [ctypes.POINTER(DenseCfg), ctypes.POINTER(_vp)]),
+    ("m1moe_cuda_dense_destroy", ctypes.c_int, [_vp]),
+    ("m1moe_cuda_dense_load", ctypes.c_int, [_vp, _i32, _i32, _vp, ctypes.c_size_t]),
+    ("m1moe_cuda_dense_load_device", ctypes.c_int, [_vp, _i32, _i32, _vp, ctypes.c_size_t, _vp]),
+    ("m1moe_cuda_dense_kv_cache", ctypes.c_int,
+     [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+    ("m1moe_cuda_dense_set_position", ctypes.c_int, [_vp, _i32]),
+    ("m1moe_cuda_dense_get_position", ctypes.c_int, [_vp, ctypes.POINTER(_i32)]),
+    ("m1moe_cuda_dense_reset", ctypes.c_int, [_vp]),
+    ("m1moe_cuda_dense_synchronize", ctypes.c_int, [_vp]),
+    ("m1moe_cuda_dense_gemv", ctypes.c_int,
+     [_vp, _i32, _i32, _vp, _i32, _vp, ctypes.c_float, _vp, _vp, _i32, _vp]),
+    ("m1moe_cuda_dense_rmsnorm", ctypes.c_int,
+     [_vp, _i32, _vp, ctypes.c_float, _vp, _i32, _i32, _vp]),
+    ("m1moe_cuda_dense_attention", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _vp]),
+    ("m1moe_cuda_dense_lm_head", ctypes.c_int, [_vp, _vp, _i32, _vp, _vp, _vp]),
+    ("m1moe_cuda_decode_step", ctypes.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _vp]),
 ]
 
 

@@ -46,7 +46,7 @@ namespace m1 {
 
 constexpr int kGemvColsPerWarp = 256;  // 32 lanes x 8 bf16
 constexpr int kGemvChunkRows = 64;     // rows per shared-memory reduction round
-constexpr int kGemvMaxWarps = 32;      // K <= 8192
+constexpr int kGemvMaxWarps = 16;      // K <= 4096 (512 threads: up to 128 registers)
 constexpr int kDenseMaxTok = 8;
 
 enum GemvEpi { kEpiStore = 0, kEpiPostNorm = 1, kEpiArgmax = 2 };
@@ -126,7 +126,7 @@ __host__ __device__ inline size_t gemv_smem(int nwarps, int nt) {
 }
 
 template <int NT, int EPI>
-__global__ void __launch_bounds__(1024) k_dense_gemv(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvMaxWarps * 32) k_dense_gemv(const GemvParams p) {
     constexpr int U = GemvRound<NT>::U, NV = U * NT, kS = 32 / NV;
     extern __shared__ __align__(16) float part[];  // [nw][kGemvChunkRows][NT]
     __shared__ float red[kGemvMaxWarps][NT];
@@ -306,6 +306,30 @@ __global__ void k_embed(const uint16_t *embed, const int32_t *tokens, int vocab,
         out[(size_t)t * h + i] = bf16_bits(embed[(size_t)tok * h + i]);
 }
 
+// ------------------------------------------------------------- rmsnorm ----
+// y[t] = x[t] * rsqrt(mean(x[t]^2) + eps) * w, one CTA per token (the
+// stand-alone form of the GEMV prologue; Shaders.metal:97-134).
+__global__ void k_rmsnorm(const void *x, int x_bf16, const uint16_t *w, float eps, float *y, int dim) {
+    __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const size_t base = (size_t)t * dim;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float v = load_act(x, x_bf16, base + i);
+        s = fmaf(v, v, s);
+    }
+    s = warp_sum(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    float ss = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) ss += red[i];
+    const float rms = rsqrtf(ss / (float)dim + eps);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x)
+        y[base + i] = (load_act(x, x_bf16, base + i) * rms) * bf16_bits(w[i]);
+}
+
 // ------------------------------------------------------------ attention ----
 constexpr int kHeadDim = 128;   // dims per head (32 lanes x 4)
 constexpr int kAttnWarps = 4;
@@ -382,16 +406,18 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
     __shared__ int is_last;
     pdl_trigger();
     pdl_wait();
-    const int pos = *p.pos;
+    // a position outside the cache sets the error word; the call then runs on
+    // position 0 without storing, so that every CTA still takes part in the
+    // split merge below (its output is not to be used)
+    const int pos_in = *p.pos;
+    const bool bad = pos_in < 0 || pos_in >= p.max_seq;
+    if (bad && threadIdx.x == 0 && split == 0 && g == 0 && t == 0) atomicOr(p.err, kErrBadExpert);
+    const int pos = bad ? 0 : pos_in;
     const int seq = pos + 1;
     const int hd = kHeadDim, qd = p.nh * hd, kvd = p.nkv * hd;
     // this split's positions: seq cut into nsplit runs of a multiple of 32
     const int slen = ((seq + p.nsplit - 1) / p.nsplit + 31) & ~31;
     const int p0 = split * slen, p1 = min(seq, p0 + slen);
-    if (pos < 0 || pos >= p.max_seq) {
-        if (threadIdx.x == 0 && split == 0 && g == 0 && t == 0) atomicOr(p.err, kErrBadExpert);
-        return;
-    }
     const float *qt = p.qkv + (size_t)t * p.qkv_stride;
     float q[HP][4];
 #pragma unroll
@@ -402,7 +428,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
     }
     const size_t slab = ((size_t)t * p.nkv + g) * p.max_seq * hd;
     uint16_t *kb = p.kc + slab, *vb = p.vc + slab;
-    if (warp == 0 && p0 <= pos && pos < p1) {
+    if (warp == 0 && !bad && p0 <= pos && pos < p1) {
         // the new token's k (QK-norm, RoPE) and v into the cache, as bf16
         float k[4], v[4];
         load4(qt + qd + (size_t)g * hd + 4 * lane, k);

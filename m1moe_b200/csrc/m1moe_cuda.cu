@@ -25,7 +25,8 @@
 #include "prefill.cuh"
 #include "tiled_layout.cuh"
 
-namespace {
+// Error reporting and the launch counter, shared with the dense step (dense.cu).
+namespace m1abi {
 
 thread_local std::string g_last_error;
 std::atomic<long long> g_launches{0};
@@ -44,6 +45,19 @@ m1moe_status cuda_fail(cudaError_t e, const char *what) {
     m1moe_status st = (e == cudaErrorMemoryAllocation) ? M1MOE_ERR_OUT_OF_MEMORY : M1MOE_ERR_CUDA;
     return fail(st, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+m1moe_status moe_compatible(const m1moe_cuda_ctx *moe, int hidden, int layers, int batch, int device);
+
+}  // namespace m1abi
+
+namespace {
+
+using m1abi::cuda_fail;
+using m1abi::fail;
+using m1abi::g_last_error;
+using m1abi::g_launches;
 
 #define M1_CK(call)                                              \
     do {                                                         \
@@ -677,6 +691,20 @@ m1moe_status pf_gemm(m1moe_cuda_ctx *c, const m1::PrefillParams &p, const CUtens
 }
 
 }  // namespace
+
+m1moe_status m1abi::moe_compatible(const m1moe_cuda_ctx *c, int hidden, int layers, int batch,
+                                   int device) {
+    if (!c) return fail(M1MOE_ERR_INVALID_ARG, "MoE ctx is NULL");
+    if (c->cfg.hidden_dim != hidden || c->cfg.num_layers != layers || c->cfg.device != device)
+        return fail(M1MOE_ERR_INVALID_ARG,
+                    "MoE context (hidden %d, %d layers, device %d) does not match the dense one "
+                    "(hidden %d, %d layers, device %d)",
+                    c->cfg.hidden_dim, c->cfg.num_layers, c->cfg.device, hidden, layers, device);
+    if (batch > c->cfg.max_batch)
+        return fail(M1MOE_ERR_INVALID_ARG, "batch %d above the MoE context's max_batch %d", batch,
+                    c->cfg.max_batch);
+    return M1MOE_OK;
+}
 
 extern "C" {
 

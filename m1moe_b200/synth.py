@@ -141,3 +141,64 @@ def layer_image_device(num_experts: int, hidden: int, inter: int, gs: int, *, se
         img[:, s0:s0 + ns] = scale.view(torch.uint8).view(num_experts, ns)
         img[:, b0:b0 + ns] = bias.view(torch.uint8).view(num_experts, ns)
     return img.view(-1)
+
+
+# ------------------------------------------------------------------ dense ----
+
+def dense_weights(seed: int, *, h: int, nh: int, nkv: int, hd: int, layers: int, vocab: int,
+                  qk_norm: bool) -> dict:
+    """Non-expert weights of a decoder (bf16 bit patterns): projections,
+    embedding and LM head ~ N(0, 0.02); norm weights 1 + N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+
+    def mat(rows, cols, std=0.02):
+        return f32_to_bf16(rng.normal(0.0, std, size=(rows, cols)).astype(np.float32))
+
+    def norm(n):
+        return f32_to_bf16((1.0 + rng.normal(0.0, 0.02, size=n)).astype(np.float32))
+
+    qd, kvd = nh * hd, nkv * hd
+    w = {"embed": mat(vocab, h), "lm_head": mat(vocab, h), "final_norm": norm(h),
+         "in_norm": [], "post_norm": [], "wq": [], "wk": [], "wv": [], "wo": [], "qn": [], "kn": []}
+    for _ in range(layers):
+        w["in_norm"].append(norm(h))
+        w["post_norm"].append(norm(h))
+        w["wq"].append(mat(qd, h))
+        w["wk"].append(mat(kvd, h))
+        w["wv"].append(mat(kvd, h))
+        w["wo"].append(mat(h, qd))
+        if qk_norm:
+            w["qn"].append(norm(qd))
+            w["kn"].append(norm(kvd))
+    return w
+
+
+def dense_weights_device(seed: int, *, h: int, nh: int, nkv: int, hd: int, layers: int, vocab: int,
+                         qk_norm: bool, device) -> dict:
+    """The same distributions generated in HBM (torch bf16 tensors), for
+    multi-GB benchmark models; the random stream differs from dense_weights."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def mat(rows, cols, std=0.02):
+        return (torch.randn((rows, cols), generator=g, device=device) * std).to(torch.bfloat16)
+
+    def norm(n):
+        return (1.0 + 0.02 * torch.randn((n,), generator=g, device=device)).to(torch.bfloat16)
+
+    qd, kvd = nh * hd, nkv * hd
+    w = {"embed": mat(vocab, h), "lm_head": mat(vocab, h), "final_norm": norm(h),
+         "in_norm": [], "post_norm": [], "wq": [], "wk": [], "wv": [], "wo": [], "qn": [], "kn": []}
+    for _ in range(layers):
+        w["in_norm"].append(norm(h))
+        w["post_norm"].append(norm(h))
+        w["wq"].append(mat(qd, h))
+        w["wk"].append(mat(kvd, h))
+        w["wv"].append(mat(kvd, h))
+        w["wo"].append(mat(h, qd))
+        if qk_norm:
+            w["qn"].append(norm(qd))
+            w["kn"].append(norm(kvd))
+    return w

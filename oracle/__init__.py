@@ -71,6 +71,13 @@ def lib():
         L.orc_moe_layer.argtypes = [u8p, u16p, f32p, f32p, f32p, c_int, c_int, c_int, c_int,
                                     c_int, c_int, c_int, i32p, f32p, c_int]
         L.orc_moe_layer.restype = c_int
+        L.orc_rmsnorm.argtypes = [f32p, u16p, ctypes.c_float, f32p, c_int]
+        L.orc_matvec_bf16.argtypes = [u16p, f32p, f32p, c_int, c_int, c_int]
+        L.orc_head_rmsnorm.argtypes = [f32p, c_int, c_int, u16p, ctypes.c_float]
+        L.orc_rope.argtypes = [f32p, c_int, c_int, ctypes.c_float, c_int]
+        L.orc_attention.argtypes = [f32p, u16p, u16p, c_int, c_int, c_int, c_int, c_int, f32p]
+        L.orc_argmax.argtypes = [f32p, c_int]
+        L.orc_argmax.restype = c_int
         _lib = L
     return _lib
 
@@ -187,3 +194,109 @@ def moe_layer(table: np.ndarray, router_bf16: np.ndarray, x: np.ndarray, residua
     if rc != 0:
         raise RuntimeError(f"orc_moe_layer failed ({rc})")
     return out, idx, w
+
+
+# ------------------------------------------------------------------ dense ----
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _u16(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint16)
+
+
+def rmsnorm(x: np.ndarray, w_bf16: np.ndarray, eps: float) -> np.ndarray:
+    """Shaders.metal:97-134 for one vector."""
+    x, w = _f32(x), _u16(w_bf16)
+    y = np.empty_like(x)
+    lib().orc_rmsnorm(_p(x, ctypes.c_float), _p(w, ctypes.c_uint16), eps, _p(y, ctypes.c_float), x.size)
+    return y
+
+
+def matvec_bf16(W_bf16: np.ndarray, x: np.ndarray, nthreads: int = 1) -> np.ndarray:
+    """Shaders.metal:328-353: bf16 W [out][in] times f32 x."""
+    W, x = _u16(W_bf16), _f32(x)
+    y = np.empty(W.shape[0], dtype=np.float32)
+    lib().orc_matvec_bf16(_p(W, ctypes.c_uint16), _p(x, ctypes.c_float), _p(y, ctypes.c_float),
+                          W.shape[0], W.shape[1], nthreads)
+    return y
+
+
+def head_rmsnorm(buf: np.ndarray, num_heads: int, head_dim: int, w_bf16: np.ndarray,
+                 eps: float) -> np.ndarray:
+    b, w = _f32(buf).copy(), _u16(w_bf16)
+    lib().orc_head_rmsnorm(_p(b, ctypes.c_float), num_heads, head_dim, _p(w, ctypes.c_uint16), eps)
+    return b
+
+
+def rope(buf: np.ndarray, num_heads: int, head_dim: int, theta: float, pos: int) -> np.ndarray:
+    b = _f32(buf).copy()
+    lib().orc_rope(_p(b, ctypes.c_float), num_heads, head_dim, theta, pos)
+    return b
+
+
+def attention(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, num_heads: int, num_kv_heads: int,
+              head_dim: int, seq_len: int) -> np.ndarray:
+    """Shaders.metal:209-313 for one sequence; kc/vc bf16 [nkv][max_seq][hd]."""
+    q, kc, vc = _f32(q), _u16(kc), _u16(vc)
+    out = np.empty(num_heads * head_dim, dtype=np.float32)
+    lib().orc_attention(_p(q, ctypes.c_float), _p(kc, ctypes.c_uint16), _p(vc, ctypes.c_uint16),
+                        num_heads, num_kv_heads, head_dim, kc.shape[1], seq_len,
+                        _p(out, ctypes.c_float))
+    return out
+
+
+def argmax(logits: np.ndarray) -> int:
+    lg = _f32(logits)
+    return int(lib().orc_argmax(_p(lg, ctypes.c_float), lg.size))
+
+
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """Round to nearest even (the cache store's rounding)."""
+    u = _f32(a).view(np.uint32)
+    return ((u + np.uint32(0x7FFF) + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def decode_step(dense: dict, moe: dict, kv: list, tokens, pos: int, nthreads: int = 1):
+    """InferenceEngine.forward (:124-156) at temperature 0 for a batch of
+    sequences at one position, composed from the restatements above and
+    moe_layer (runLayer, :167-267).
+
+    dense: cfg keys h, nh, nkv, hd, layers, vocab, eps, theta, qk_norm and the
+    bf16 tensors embed, final_norm, lm_head, and per layer (lists) in_norm,
+    post_norm, wq, wk, wv, wo, qn, kn.  moe: tables (layer images), routers,
+    inter, E, K, gs, norm.  kv: per layer (k, v) bf16 arrays
+    [batch][nkv][max_seq][hd], updated in place at `pos` (k and v rounded to
+    bf16 as the B200 cache stores them; the reference keeps f32 rows).
+    Returns (next tokens, logits [batch][vocab])."""
+    h, nh, nkv, hd = dense["h"], dense["nh"], dense["nkv"], dense["hd"]
+    eps, theta = dense["eps"], dense["theta"]
+    toks, all_logits = [], []
+    for b, tok in enumerate(tokens):
+        residual = bf16_to_f32(dense["embed"][tok]).astype(np.float32)
+        for L in range(dense["layers"]):
+            xn = rmsnorm(residual, dense["in_norm"][L], eps)
+            q = matvec_bf16(dense["wq"][L], xn, nthreads)
+            k = matvec_bf16(dense["wk"][L], xn, nthreads)
+            v = matvec_bf16(dense["wv"][L], xn, nthreads)
+            if dense["qk_norm"]:
+                q = head_rmsnorm(q, nh, hd, dense["qn"][L], eps)
+                k = head_rmsnorm(k, nkv, hd, dense["kn"][L], eps)
+            q = rope(q, nh, hd, theta, pos)
+            k = rope(k, nkv, hd, theta, pos)
+            kc, vc = kv[L]
+            kc[b, :, pos, :] = f32_to_bf16_bits(k).reshape(nkv, hd)
+            vc[b, :, pos, :] = f32_to_bf16_bits(v).reshape(nkv, hd)
+            att = attention(q, kc[b], vc[b], nh, nkv, hd, pos + 1)
+            o = matvec_bf16(dense["wo"][L], att, nthreads)
+            residual = (residual + o).astype(np.float32)  # residualAdd
+            h_mid = rmsnorm(residual, dense["post_norm"][L], eps)
+            out, _, _ = moe_layer(moe["tables"][L], moe["routers"][L], h_mid[None, :],
+                                  residual[None, :], h=h, inter=moe["inter"], E=moe["E"],
+                                  K=moe["K"], gs=moe["gs"], norm=moe["norm"], nthreads=nthreads)
+            residual = out[0]
+        xn = rmsnorm(residual, dense["final_norm"], eps)
+        logits = matvec_bf16(dense["lm_head"], xn, nthreads)
+        toks.append(argmax(logits))
+        all_logits.append(logits)
+    return np.array(toks, dtype=np.int32), np.stack(all_logits)

@@ -155,24 +155,16 @@ void orc_matvec4bit(const uint32_t *W, const uint16_t *S, const uint16_t *B,
     orc_matvec4bit_rows_lanes(W, S, B, x, y, out_dim, in_dim, gs, 0, out_dim);
 }
 
+/* A persistent pool of host threads for row-partitioned work (threads are
+ * created once, not per call): the caller publishes `njobs` row ranges of one
+ * function, bumps the generation, runs job 0 itself and waits for the others. */
+typedef void (*orc_rows_fn)(const void *arg, int row0, int row1);
 typedef struct {
-    const uint32_t *W;
-    const uint16_t *S, *B;
-    const float *x;
-    float *y;
-    int out_dim, in_dim, gs, row0, row1;
-} orc_mv_job;
+    orc_rows_fn fn;
+    const void *arg;
+    int row0, row1;
+} orc_job;
 
-static void *orc_mv_worker(void *p) {
-    orc_mv_job *j = (orc_mv_job *)p;
-    orc_matvec4bit_rows_lanes(j->W, j->S, j->B, j->x, j->y, j->out_dim, j->in_dim, j->gs, j->row0,
-                              j->row1);
-    return NULL;
-}
-
-/* A persistent pool of host threads for the row-partitioned matvec (threads
- * are created once, not per matvec): the caller publishes `njobs` jobs,
- * bumps the generation, runs job 0 itself and waits for the others. */
 #define ORC_MAX_THREADS 256
 static struct {
     pthread_mutex_t mu;
@@ -182,7 +174,7 @@ static struct {
     unsigned gen;          /* bumped per batch of jobs */
     int pending;           /* jobs of this batch not finished yet */
     int njobs;
-    orc_mv_job jobs[ORC_MAX_THREADS];
+    orc_job jobs[ORC_MAX_THREADS];
 } orc_pool = {PTHREAD_MUTEX_INITIALIZER, PTHREAD_COND_INITIALIZER, PTHREAD_COND_INITIALIZER};
 static pthread_mutex_t orc_pool_call = PTHREAD_MUTEX_INITIALIZER; /* one batch at a time */
 
@@ -194,9 +186,9 @@ static void *orc_pool_worker(void *arg) {
         while (orc_pool.gen == seen) pthread_cond_wait(&orc_pool.go, &orc_pool.mu);
         seen = orc_pool.gen;
         if (id < orc_pool.njobs) {
-            orc_mv_job j = orc_pool.jobs[id];
+            orc_job j = orc_pool.jobs[id];
             pthread_mutex_unlock(&orc_pool.mu);
-            orc_mv_worker(&j);
+            j.fn(j.arg, j.row0, j.row1);
             pthread_mutex_lock(&orc_pool.mu);
             if (--orc_pool.pending == 0) pthread_cond_signal(&orc_pool.done);
         }
@@ -204,13 +196,10 @@ static void *orc_pool_worker(void *arg) {
     return NULL;
 }
 
-void orc_matvec4bit_mt(const uint32_t *W, const uint16_t *S, const uint16_t *B,
-                       const float *x, float *y, int out_dim, int in_dim, int gs,
-                       int nthreads) {
-    /* The reference dispatches one threadgroup per row (InferenceEngine.swift:463);
-     * here rows are partitioned over host threads. */
-    if (nthreads <= 1 || out_dim < 2 * nthreads) {
-        orc_matvec4bit(W, S, B, x, y, out_dim, in_dim, gs);
+/* Run fn over rows [0, n) split into `nthreads` contiguous ranges. */
+static void orc_parallel_rows(orc_rows_fn fn, const void *arg, int n, int nthreads) {
+    if (nthreads <= 1 || n < 2 * nthreads) {
+        fn(arg, 0, n);
         return;
     }
     if (nthreads > ORC_MAX_THREADS) nthreads = ORC_MAX_THREADS;
@@ -222,26 +211,48 @@ void orc_matvec4bit_mt(const uint32_t *W, const uint16_t *S, const uint16_t *B,
             break;
         ++orc_pool.nthreads;
     }
-    int workers = orc_pool.nthreads + 1 < nthreads ? orc_pool.nthreads + 1 : nthreads;
-    const int per = (out_dim + workers - 1) / workers;
+    const int workers = orc_pool.nthreads + 1 < nthreads ? orc_pool.nthreads + 1 : nthreads;
+    const int per = (n + workers - 1) / workers;
     int njobs = 0;
     for (int t = 0; t < workers; ++t) {
-        const int r0 = t * per, r1 = (t + 1) * per < out_dim ? (t + 1) * per : out_dim;
+        const int r0 = t * per, r1 = (t + 1) * per < n ? (t + 1) * per : n;
         if (r0 >= r1) break;
-        orc_pool.jobs[t] = (orc_mv_job){W, S, B, x, y, out_dim, in_dim, gs, r0, r1};
+        orc_pool.jobs[t] = (orc_job){fn, arg, r0, r1};
         ++njobs;
     }
     orc_pool.njobs = njobs;
     orc_pool.pending = njobs - 1;
     ++orc_pool.gen;
     pthread_cond_broadcast(&orc_pool.go);
-    orc_mv_job j0 = orc_pool.jobs[0];
+    orc_job j0 = orc_pool.jobs[0];
     pthread_mutex_unlock(&orc_pool.mu);
-    orc_mv_worker(&j0);
+    j0.fn(j0.arg, j0.row0, j0.row1);
     pthread_mutex_lock(&orc_pool.mu);
     while (orc_pool.pending > 0) pthread_cond_wait(&orc_pool.done, &orc_pool.mu);
     pthread_mutex_unlock(&orc_pool.mu);
     pthread_mutex_unlock(&orc_pool_call);
+}
+
+typedef struct {
+    const uint32_t *W;
+    const uint16_t *S, *B;
+    const float *x;
+    float *y;
+    int out_dim, in_dim, gs;
+} orc_mv4_arg;
+
+static void orc_mv4_rows(const void *a, int r0, int r1) {
+    const orc_mv4_arg *j = (const orc_mv4_arg *)a;
+    orc_matvec4bit_rows_lanes(j->W, j->S, j->B, j->x, j->y, j->out_dim, j->in_dim, j->gs, r0, r1);
+}
+
+void orc_matvec4bit_mt(const uint32_t *W, const uint16_t *S, const uint16_t *B,
+                       const float *x, float *y, int out_dim, int in_dim, int gs,
+                       int nthreads) {
+    /* The reference dispatches one threadgroup per row (InferenceEngine.swift:463);
+     * here rows are partitioned over host threads. */
+    const orc_mv4_arg a = {W, S, B, x, y, out_dim, in_dim, gs};
+    orc_parallel_rows(orc_mv4_rows, &a, out_dim, nthreads);
 }
 
 void orc_swiglu(const float *gate, const float *up, float *act, int n) {
@@ -357,4 +368,159 @@ int orc_moe_layer(const uint8_t *table, const uint16_t *router_bf16, const float
     free(outs);
     free(scratch);
     return 0;
+}
+
+/* ===================== the dense half of a decode step ===================== */
+
+void orc_rmsnorm(const float *x, const uint16_t *w, float eps, float *y, int dim) {
+    /* Shaders.metal:97-134: rmsNormSum with 256 threads (lane lid sums x[i]^2
+     * for i = lid, lid+256, ...; tree reduction s = 128 .. 1), then
+     * rmsNormApply: out = x * rsqrt(sumSq/dim + eps) * w. */
+    float shared[256];
+    for (int lid = 0; lid < 256; ++lid) {
+        float acc = 0.0f;
+        for (int i = lid; i < dim; i += 256) {
+            const float v = x[i];
+            acc += v * v;
+        }
+        shared[lid] = acc;
+    }
+    for (int s2 = 128; s2 > 0; s2 >>= 1)
+        for (int lid = 0; lid < s2; ++lid) shared[lid] += shared[lid + s2];
+    const float rms = 1.0f / sqrtf(shared[0] / (float)dim + eps);
+    for (int i = 0; i < dim; ++i) y[i] = x[i] * rms * orc_bf16_to_f32(w[i]);
+}
+
+typedef struct {
+    const uint16_t *W;
+    const float *x;
+    float *y;
+    int out_dim, in_dim;
+} orc_mv16_arg;
+
+static void orc_mv16_rows(const void *a, int row0, int row1) {
+    /* Shaders.metal:328-353 (matvecBF16): 64 threads per row, lane lid sums
+     * bf16(w[i]) * x[i] for i = lid, lid+64, ...; tree reduction 32 .. 1.
+     * Lanes innermost (vectorisable); each lane's order is the reference's. */
+    const orc_mv16_arg *j = (const orc_mv16_arg *)a;
+    float acc[64];
+    for (int row = row0; row < row1 && row < j->out_dim; ++row) {
+        const uint16_t *wr = j->W + (size_t)row * j->in_dim;
+        for (int lid = 0; lid < 64; ++lid) acc[lid] = 0.0f;
+        for (int i0 = 0; i0 < j->in_dim; i0 += 64) {
+            const int nl = j->in_dim - i0 < 64 ? j->in_dim - i0 : 64;
+            for (int lid = 0; lid < nl; ++lid)
+                acc[lid] += orc_bf16_to_f32(wr[i0 + lid]) * j->x[i0 + lid];
+        }
+        for (int s2 = 32; s2 > 0; s2 >>= 1)
+            for (int lid = 0; lid < s2; ++lid) acc[lid] += acc[lid + s2];
+        j->y[row] = acc[0];
+    }
+}
+
+void orc_matvec_bf16(const uint16_t *W, const float *x, float *y, int out_dim, int in_dim,
+                     int nthreads) {
+    const orc_mv16_arg a = {W, x, y, out_dim, in_dim};
+    orc_parallel_rows(orc_mv16_rows, &a, out_dim, nthreads);
+}
+
+void orc_head_rmsnorm(float *buf, int num_heads, int head_dim, const uint16_t *w, float eps) {
+    /* InferenceEngine.swift:538-548: every head uses the first head_dim weights. */
+    for (int head = 0; head < num_heads; ++head) {
+        float *b = buf + (size_t)head * head_dim;
+        float ss = 0.0f;
+        for (int d = 0; d < head_dim; ++d) ss += b[d] * b[d];
+        const float rms = 1.0f / sqrtf(ss / (float)head_dim + eps);
+        for (int d = 0; d < head_dim; ++d) b[d] *= rms * orc_bf16_to_f32(w[d]);
+    }
+}
+
+void orc_rope(float *buf, int num_heads, int head_dim, float theta, int pos) {
+    /* InferenceEngine.swift:521-536: half-split pairs (i, i + hd/2). */
+    const int half = head_dim / 2;
+    for (int head = 0; head < num_heads; ++head) {
+        float *b = buf + (size_t)head * head_dim;
+        for (int pair = 0; pair < half; ++pair) {
+            const float freq = 1.0f / powf(theta, (float)(2 * pair) / (float)head_dim);
+            const float angle = (float)pos * freq;
+            const float c = cosf(angle), s = sinf(angle);
+            const float x0 = b[pair], x1 = b[pair + half];
+            b[pair] = x0 * c - x1 * s;
+            b[pair + half] = x0 * s + x1 * c;
+        }
+    }
+}
+
+void orc_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int num_heads,
+                   int num_kv_heads, int head_dim, int max_seq, int seq_len, float *out) {
+    /* Shaders.metal:209-313 (attnScores, attnSoftmax, attnValues) for one
+     * sequence, with the cache in the B200 layout [kv_head][max_seq][head_dim]
+     * (bf16; the reference keeps f32 rows [pos][kvDim]).  scale = 1/sqrt(hd)
+     * (InferenceEngine.swift:358); heads per kv head = num_heads/num_kv_heads. */
+    const int hpkv = num_heads / num_kv_heads;
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    float *scores = (float *)malloc(sizeof(float) * (size_t)seq_len);
+    if (!scores) return;
+    for (int head = 0; head < num_heads; ++head) {
+        const int kvh = head / hpkv;
+        const float *qh = q + (size_t)head * head_dim;
+        const uint16_t *kb = kc + (size_t)kvh * max_seq * head_dim;
+        const uint16_t *vb = vc + (size_t)kvh * max_seq * head_dim;
+        /* scores: 64 threads per (head, pos), strided over head_dim, tree */
+        for (int p = 0; p < seq_len; ++p) {
+            float sh[64];
+            for (int lid = 0; lid < 64; ++lid) {
+                float acc = 0.0f;
+                for (int i = lid; i < head_dim; i += 64)
+                    acc += qh[i] * orc_bf16_to_f32(kb[(size_t)p * head_dim + i]);
+                sh[lid] = acc;
+            }
+            for (int s2 = 32; s2 > 0; s2 >>= 1)
+                for (int lid = 0; lid < s2; ++lid) sh[lid] += sh[lid + s2];
+            scores[p] = sh[0] * scale;
+        }
+        /* softmax: 256 threads, max tree, exp-sum tree, multiply by 1/sum */
+        float sh[256];
+        for (int lid = 0; lid < 256; ++lid) {
+            float mx = -INFINITY;
+            for (int i = lid; i < seq_len; i += 256) mx = scores[i] > mx ? scores[i] : mx;
+            sh[lid] = mx;
+        }
+        for (int s2 = 128; s2 > 0; s2 >>= 1)
+            for (int lid = 0; lid < s2; ++lid) sh[lid] = sh[lid + s2] > sh[lid] ? sh[lid + s2] : sh[lid];
+        const float maxv = sh[0];
+        for (int lid = 0; lid < 256; ++lid) {
+            float sum = 0.0f;
+            for (int i = lid; i < seq_len; i += 256) {
+                const float e = expf(scores[i] - maxv);
+                scores[i] = e;
+                sum += e;
+            }
+            sh[lid] = sum;
+        }
+        for (int s2 = 128; s2 > 0; s2 >>= 1)
+            for (int lid = 0; lid < s2; ++lid) sh[lid] += sh[lid + s2];
+        const float inv = 1.0f / sh[0];
+        for (int i = 0; i < seq_len; ++i) scores[i] *= inv;
+        /* values: one thread per (head, dim), positions in order */
+        for (int d = 0; d < head_dim; ++d) {
+            float acc = 0.0f;
+            for (int p = 0; p < seq_len; ++p)
+                acc += scores[p] * orc_bf16_to_f32(vb[(size_t)p * head_dim + d]);
+            out[(size_t)head * head_dim + d] = acc;
+        }
+    }
+    free(scores);
+}
+
+int orc_argmax(const float *logits, int n) {
+    /* InferenceEngine.swift:552-555: the first maximum wins. */
+    int best = 0;
+    float bv = logits[0];
+    for (int i = 1; i < n; ++i)
+        if (logits[i] > bv) {
+            bv = logits[i];
+            best = i;
+        }
+    return best;
 }

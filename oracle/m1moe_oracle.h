@@ -93,6 +93,31 @@ void orc_matvec4bit_mt(const uint32_t *W, const uint16_t *S, const uint16_t *B,
                        const float *x, float *y, int out_dim, int in_dim, int gs,
                        int nthreads);
 
+/* ---- the dense half of a decode step ---- */
+
+/* Shaders.metal:97-134: 256-lane sum of squares with tree reduction, then
+ * y = x * (1/sqrt(ss/dim + eps)) * w. */
+void orc_rmsnorm(const float *x, const uint16_t *w, float eps, float *y, int dim);
+
+/* Shaders.metal:328-353 (matvecBF16): y = W x, bf16 W [out][in], f32 x;
+ * 64 lanes strided over `in`, tree reduction; rows over nthreads threads. */
+void orc_matvec_bf16(const uint16_t *W, const float *x, float *y, int out_dim, int in_dim,
+                     int nthreads);
+
+/* InferenceEngine.swift:538-548 (per-head RMSNorm, first head_dim weights). */
+void orc_head_rmsnorm(float *buf, int num_heads, int head_dim, const uint16_t *w, float eps);
+
+/* InferenceEngine.swift:521-536 (RoPE, half-split pairs). */
+void orc_rope(float *buf, int num_heads, int head_dim, float theta, int pos);
+
+/* Shaders.metal:209-313 for one sequence over positions [0, seq_len) of a
+ * bf16 cache laid out [num_kv_heads][max_seq][head_dim]; out [num_heads*hd]. */
+void orc_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int num_heads,
+                   int num_kv_heads, int head_dim, int max_seq, int seq_len, float *out);
+
+/* InferenceEngine.swift:552-555: index of the first maximum. */
+int orc_argmax(const float *logits, int n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,283 @@
+"""The dense half of a decode step and the whole step (GPU) vs the CPU oracle.
+
+The oracle restates the reference's dense arithmetic (oracle/m1moe_oracle.c:
+rmsNorm and matvecBF16 of Shaders.metal:97-134 / :328-353, attention of
+:209-313, the CPU QK-norm / RoPE / argmax of InferenceEngine.swift:521-555)
+with the BF16 KV cache of the benchmark configs.  Bars: every output within
+1e-3 of its L2 norm (max |y - ref| / ||ref||_2, fp32 accumulation on both
+sides); greedy tokens equal wherever the oracle's top two logits differ by
+more than 1e-3 of the logits' spread, exact ties to the lower index.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_max_err
+from m1moe_b200 import MoEBlock, synth
+from m1moe_b200.dense import DenseModel, gemv, rmsnorm
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def _dev(a: np.ndarray) -> torch.Tensor:
+    """bf16 bit patterns -> CUDA bf16 tensor."""
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda().view(torch.bfloat16)
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("rows,K", [(6144, 2048), (2048, 4096), (37, 256), (1000, 1024)])
+@pytest.mark.parametrize("B", [1, 3, 8])
+def test_gemv_vs_oracle(oracle_lib, rows, K, B):
+    rng = np.random.default_rng(rows + K + B)
+    W = oracle_lib.f32_to_bf16_bits(rng.normal(0, 0.02, size=(rows, K)))
+    x = rng.normal(0, 1, size=(B, K)).astype(np.float32)
+    y = gemv(_dev(W), torch.from_numpy(x).cuda()).cpu().numpy()
+    for t in range(B):
+        ref = oracle_lib.matvec_bf16(W, x[t], 4)
+        assert rel_max_err(y[t], ref) < TOL, t
+        assert rel_max_err(y[t], ref) < 1e-5, t  # fp32 on both sides
+
+
+@pytest.mark.parametrize("B", [1, 5])
+@pytest.mark.parametrize("xdt", [torch.float32, torch.bfloat16])
+def test_gemv_fused_rmsnorm_and_residual(oracle_lib, B, xdt):
+    """rmsnorm prologue (input_layernorm) and residual epilogue (residualAdd),
+    the residual aliasing the output as in the decode step."""
+    rows, K = 2048, 2048
+    rng = np.random.default_rng(7 + B)
+    W = oracle_lib.f32_to_bf16_bits(rng.normal(0, 0.02, size=(rows, K)))
+    nw = oracle_lib.f32_to_bf16_bits(1 + 0.02 * rng.normal(size=K))
+    xb = synth.hidden_states(8 + B, B, K)
+    xf = synth.bf16_to_f32(xb)
+    res = rng.normal(0, 1, size=(B, rows)).astype(np.float32)
+    x = _dev(xb) if xdt == torch.bfloat16 else torch.from_numpy(xf).cuda()
+    out = torch.from_numpy(res).cuda()
+    gemv(_dev(W), x, norm_w=_dev(nw), eps=1e-5, residual=out, out=out)
+    y = out.cpu().numpy()
+    for t in range(B):
+        ref = oracle_lib.matvec_bf16(W, oracle_lib.rmsnorm(xf[t], nw, 1e-5), 4) + res[t]
+        assert rel_max_err(y[t], ref) < 1e-5, t
+
+
+def test_rmsnorm_vs_oracle(oracle_lib):
+    rng = np.random.default_rng(3)
+    for dim, B in ((2048, 1), (4096, 8), (320, 3)):
+        x = rng.normal(0, 3, size=(B, dim)).astype(np.float32)
+        w = oracle_lib.f32_to_bf16_bits(1 + 0.02 * rng.normal(size=dim))
+        y = rmsnorm(torch.from_numpy(x).cuda(), _dev(w), 1e-5).cpu().numpy()
+        for t in range(B):
+            assert rel_max_err(y[t], oracle_lib.rmsnorm(x[t], w, 1e-5)) < 1e-6
+
+
+def _attn_case(oracle_lib, *, nh, nkv, qk_norm, theta, pos, B, max_seq, seed):
+    hd = 128
+    qd, kvd = nh * hd, nkv * hd
+    rng = np.random.default_rng(seed)
+    dm = DenseModel(hidden_dim=256, num_heads=nh, num_kv_heads=nkv, num_layers=1, vocab_size=16,
+                    qk_norm=qk_norm, rope_theta=theta, max_batch=B, max_seq=max_seq)
+    qn = oracle_lib.f32_to_bf16_bits(1 + 0.05 * rng.normal(size=qd))
+    kn = oracle_lib.f32_to_bf16_bits(1 + 0.05 * rng.normal(size=kvd))
+    if qk_norm:
+        dm.load("qn", qn, 0)
+        dm.load("kn", kn, 0)
+    kc, vc = dm.kv_cache(0)
+    kc.normal_()
+    vc.normal_()
+    dm.set_position(pos)
+    qkv = rng.normal(0, 1, size=(B, qd + 2 * kvd)).astype(np.float32)
+    out = dm.attention(0, torch.from_numpy(qkv).cuda()).cpu().numpy()
+    dm.synchronize()
+    k_gpu, v_gpu = _bits(kc), _bits(vc)
+    errs = []
+    for t in range(B):
+        q = qkv[t, :qd]
+        k = qkv[t, qd:qd + kvd]
+        v = qkv[t, qd + kvd:]
+        if qk_norm:
+            q = oracle_lib.head_rmsnorm(q, nh, hd, qn, 1e-5)
+            k = oracle_lib.head_rmsnorm(k, nkv, hd, kn, 1e-5)
+        q = oracle_lib.rope(q, nh, hd, theta, pos)
+        k = oracle_lib.rope(k, nkv, hd, theta, pos)
+        kref = oracle_lib.f32_to_bf16_bits(k).reshape(nkv, hd)
+        vref = oracle_lib.f32_to_bf16_bits(v).reshape(nkv, hd)
+        # v is stored bit-exactly; k within one bf16 ulp (libm vs CUDA sin/cos/pow)
+        assert np.array_equal(v_gpu[t, :, pos, :], vref), t
+        kd = synth.bf16_to_f32(k_gpu[t, :, pos, :]) - synth.bf16_to_f32(kref)
+        assert np.all(np.abs(kd) <= 2.0 ** -7 * np.abs(synth.bf16_to_f32(kref)) + 1e-30), t
+        kc_t, vc_t = k_gpu[t].copy(), v_gpu[t]
+        ref = oracle_lib.attention(q, kc_t, vc_t, nh, nkv, hd, pos + 1)
+        errs.append(rel_max_err(out[t], ref))
+    dm.close()
+    return max(errs)
+
+
+@pytest.mark.parametrize("pos", [0, 5, 300, 2047])
+@pytest.mark.parametrize("B", [1, 3])
+def test_attention_olmoe_shape(oracle_lib, pos, B):
+    """Config 2's attention: 16 heads of 128, QK-norm, RoPE theta 1e4, context 2048."""
+    assert _attn_case(oracle_lib, nh=16, nkv=16, qk_norm=True, theta=10000.0, pos=pos, B=B,
+                      max_seq=2048, seed=pos + B) < TOL
+
+
+@pytest.mark.parametrize("pos", [0, 77, 4095])
+def test_attention_mixtral_gqa(oracle_lib, pos):
+    """Config 4's attention: 32 query heads over 8 KV heads (GQA), no QK-norm,
+    RoPE theta 1e6, context 4096."""
+    assert _attn_case(oracle_lib, nh=32, nkv=8, qk_norm=False, theta=1e6, pos=pos, B=2,
+                      max_seq=4096, seed=11 + pos) < TOL
+
+
+def test_lm_head_argmax_and_ties(oracle_lib):
+    h, V, B = 2048, 50304, 3
+    rng = np.random.default_rng(5)
+    W = oracle_lib.f32_to_bf16_bits(rng.normal(0, 0.02, size=(V, h)))
+    W[40000] = W[123]  # an exact tie between rows 123 and 40000 for every x
+    fn = oracle_lib.f32_to_bf16_bits(1 + 0.02 * rng.normal(size=h))
+    dm = DenseModel(hidden_dim=h, num_heads=16, num_kv_heads=16, num_layers=1, vocab_size=V,
+                    qk_norm=False, max_batch=B, max_seq=16)
+    dm.load("lm_head", W)
+    dm.load("final_norm", fn)
+    x = rng.normal(0, 1, size=(B, h)).astype(np.float32)
+    # token 2's x points along row 123, so the tied pair is its maximum
+    x[2] = synth.bf16_to_f32(W[123]) * 50.0
+    tok, lg = dm.lm_head(torch.from_numpy(x).cuda())
+    tok, lg = tok.cpu().numpy(), lg.cpu().numpy()
+    for t in range(B):
+        ref = oracle_lib.matvec_bf16(W, oracle_lib.rmsnorm(x[t], fn, 1e-5), 8)
+        assert rel_max_err(lg[t], ref) < 1e-5
+        srt = np.sort(ref)[::-1]
+        if srt[0] - srt[1] > 1e-3 * (srt[0] - srt[-1]):
+            assert tok[t] == oracle_lib.argmax(ref), t
+        assert tok[t] == int(np.argmax(lg[t])), t  # the first maximum of the GPU's own logits
+    assert tok[2] == 123
+    dm.close()
+
+
+def _model(seed, *, h, nh, nkv, layers, vocab, qk_norm, theta, E, K, inter, norm, B, max_seq):
+    dw = synth.dense_weights(seed, h=h, nh=nh, nkv=nkv, hd=128, layers=layers, vocab=vocab,
+                             qk_norm=qk_norm)
+    tables = [synth.layer_image(seed + 100 + L, E, h, inter, 64) for L in range(layers)]
+    routers = [synth.router_weights(seed + 200 + L, E, h) for L in range(layers)]
+    dm = DenseModel(hidden_dim=h, num_heads=nh, num_kv_heads=nkv, num_layers=layers,
+                    vocab_size=vocab, qk_norm=qk_norm, rope_theta=theta, max_batch=B,
+                    max_seq=max_seq)
+    dm.load_all(dw)
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=inter, num_experts=E, top_k=K,
+                   num_layers=layers, norm_topk_prob=norm, max_batch=B)
+    for L in range(layers):
+        blk.load_expert_layer(L, tables[L])
+        blk.load_router(L, routers[L])
+    dense = dict(dw, h=h, nh=nh, nkv=nkv, hd=128, layers=layers, vocab=vocab, eps=1e-5,
+                 theta=theta, qk_norm=qk_norm)
+    moe = dict(tables=tables, routers=routers, inter=inter, E=E, K=K, gs=64, norm=norm)
+    return dm, blk, dense, moe
+
+
+def _check_tokens(oracle_lib, tok, lg, ref_tok, ref_lg):
+    for t in range(len(tok)):
+        assert rel_max_err(lg[t], ref_lg[t]) < TOL, t
+        srt = np.sort(ref_lg[t])[::-1]
+        if srt[0] - srt[1] > 1e-3 * (srt[0] - srt[-1]):
+            assert tok[t] == ref_tok[t], t
+
+
+@pytest.mark.parametrize("arch", ["olmoe", "mixtral"])
+def test_decode_steps_tiny_model(oracle_lib, arch):
+    """Three greedy decode steps from an empty cache for a batch of 2 on a tiny
+    model of each architecture (OLMoE: QK-norm, top-2 of 8 without
+    renormalisation; Mixtral: GQA 4 heads over 2, top-2 renormalised), each
+    step's logits and tokens against the oracle, which keeps its own cache."""
+    olmoe = arch == "olmoe"
+    B, layers, vocab, h = 2, 2, 1000, 256
+    nh, nkv = (2, 2) if olmoe else (4, 2)
+    dm, blk, dense, moe = _model(31 if olmoe else 41, h=h, nh=nh, nkv=nkv, layers=layers,
+                                 vocab=vocab, qk_norm=olmoe, theta=1e4 if olmoe else 1e6, E=8, K=2,
+                                 inter=128, norm=not olmoe, B=B, max_seq=64)
+    kv = [(np.zeros((B, nkv, 64, 128), np.uint16), np.zeros((B, nkv, 64, 128), np.uint16))
+          for _ in range(layers)]
+    tokens = np.array([17, 933], dtype=np.int32)
+    cur = torch.from_numpy(tokens).cuda()
+    lg = torch.empty((B, vocab), dtype=torch.float32, device="cuda")
+    for pos in range(3):
+        nxt = dm.step(blk, cur, logits=lg)
+        dm.synchronize()
+        blk.synchronize()
+        ref_tok, ref_lg = oracle_lib.decode_step(dense, moe, kv, tokens.tolist(), pos, nthreads=4)
+        _check_tokens(oracle_lib, nxt.cpu().numpy(), lg.cpu().numpy(), ref_tok, ref_lg)
+        assert dm.position() == pos + 1
+        tokens = nxt.cpu().numpy()  # follow the GPU's own tokens
+        cur = nxt.clone()
+    dm.close()
+    blk.close()
+
+
+def test_decode_step_config2_shape(oracle_lib):
+    """Config 2's shapes (h 2048, 16 heads + QK-norm, 64 experts top-8, vocab
+    50304) with 2 layers, the KV cache prefilled with N(0,1) to context 2048,
+    batch 2: one step's logits and tokens against the oracle."""
+    B, layers, pos = 2, 2, 2047
+    dm, blk, dense, moe = _model(51, h=2048, nh=16, nkv=16, layers=layers, vocab=50304,
+                                 qk_norm=True, theta=1e4, E=64, K=8, inter=1024, norm=False, B=B,
+                                 max_seq=2048)
+    kv = []
+    for L in range(layers):
+        k, v = dm.kv_cache(L)
+        k.normal_()
+        v.normal_()
+        kv.append((_bits(k), _bits(v)))
+    dm.set_position(pos)
+    tokens = np.array([5, 40000], dtype=np.int32)
+    lg = torch.empty((B, 50304), dtype=torch.float32, device="cuda")
+    nxt = dm.step(blk, torch.from_numpy(tokens).cuda(), logits=lg)
+    dm.synchronize()
+    blk.synchronize()
+    ref_tok, ref_lg = oracle_lib.decode_step(dense, moe, kv, tokens.tolist(), pos, nthreads=8)
+    _check_tokens(oracle_lib, nxt.cpu().numpy(), lg.cpu().numpy(), ref_tok, ref_lg)
+    dm.close()
+    blk.close()
+
+
+def test_decode_step_replays_from_a_cuda_graph(oracle_lib):
+    """A captured step replayed advances the device position each time and
+    gives the tokens that eager steps give."""
+    B, layers, vocab = 2, 2, 1000
+    dm, blk, dense, moe = _model(61, h=256, nh=2, nkv=2, layers=layers, vocab=vocab, qk_norm=True,
+                                 theta=1e4, E=8, K=2, inter=128, norm=False, B=B, max_seq=64)
+    toks = torch.tensor([3, 4], dtype=torch.int32, device="cuda")
+    eager = []
+    cur = toks.clone()
+    for _ in range(4):
+        cur = dm.step(blk, cur).clone()
+        eager.append(cur.cpu().numpy())
+    dm.reset()
+    s = torch.cuda.Stream()
+    buf_in = toks.clone()
+    buf_out = torch.empty_like(buf_in)
+    with torch.cuda.stream(s):
+        dm.step(blk, buf_in, next_tokens=buf_out, stream=s)  # warm-up (position 0 -> 1)
+    torch.cuda.synchronize()
+    dm.reset()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        dm.step(blk, buf_in, next_tokens=buf_out, stream=s)
+        buf_in.copy_(buf_out)
+    torch.cuda.synchronize()
+    dm.reset()
+    buf_in.copy_(toks)
+    got = []
+    for _ in range(4):
+        g.replay()
+        torch.cuda.synchronize()
+        got.append(buf_in.cpu().numpy())
+    assert dm.position() == 4
+    for a, b in zip(eager, got):
+        assert np.array_equal(a, b)
+    del g
+    dm.close()
+    blk.close()

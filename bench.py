@@ -32,6 +32,11 @@ matvec_c0      (1 GPU) config 0: the 1024x2048 int4 matvec over 3072 distinct
 mixtral_decode (1 GPU) config 3 decode at batch 1, 4 and 8 (4 distinct layers).
 mixtral_ep     config 3 decode expert-parallel: 8 experts over N GPUs (one per
            GPU at N=8), one token per rank, with its own oracle parity check.
+decode_step    (1 GPU) configs 2 and 4: whole greedy decode steps (dense
+           attention half + MoE blocks + LM head) through m1moe_cuda_decode_step,
+           tok/s at batch 1 and 8 after the KV cache is prefilled to the
+           context length; the config-2 batch-1 step is checked against the
+           oracle's decode step.
 prefill  = (1 GPU) config 3's prefill mode beside the decode line: one
            Mixtral-shaped layer over 512 tokens through m1moe_cuda_moe_prefill
            (tensor-core grouped GEMMs), TFLOP/s against the measured bf16 peak.
@@ -76,6 +81,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode-step", action="store_true",
+                    help="skip the full decode steps (configs 2 and 4)")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the tensor-core prefill measurement (config 3, 512 tokens)")
     return ap.parse_args()
@@ -575,6 +582,152 @@ def mixtral_ep_measure(dev, world: int, rank: int, steps: int, warmup: int) -> d
             "note": "tok_s_moe_blocks scales the 4-layer time to Mixtral's 32 MoE blocks"}
 
 
+DECODE = {
+    # OLMoE-1B-7B-shaped decode, ctx 2048
+    "olmoe_cfg2": dict(h=2048, nh=16, nkv=16, layers=16, vocab=50304, qk_norm=True, theta=1e4,
+                       E=64, K=8, I=1024, norm=False, ctx=2048),
+    # Mixtral-8x7B-shaped decode, ctx 4096, 128 decode tokens
+    "mixtral_cfg4": dict(h=4096, nh=32, nkv=8, layers=32, vocab=32000, qk_norm=False, theta=1e6,
+                         E=8, K=2, I=14336, norm=True, ctx=4096),
+}
+
+
+def decode_step_measure(dev, name: str, batches=(1, 8), tokens: int = 128, parity: bool = False) -> dict:
+    """Full decode steps (BASELINE configs 2 and 4) through m1moe_cuda_decode_step:
+    embedding, per layer the input RMSNorm + q/k/v GEMV, QK-norm + RoPE + KV
+    store + split-K attention, o_proj + residual + post-norm, the MoE block,
+    then the final norm, LM head and greedy token.  Random-init weights of the
+    named shapes (dense ~ N(0, 0.02), experts as config 0), the bf16 KV cache
+    prefilled with N(0, 1) to the context length, then `tokens` greedy steps
+    replayed from one captured step (the device position advances each
+    replay).  tok/s = batch x steps / device time."""
+    import torch
+
+    from m1moe_b200 import MoEBlock, synth
+    from m1moe_b200.dense import DenseModel
+    c = DECODE[name]
+    h, L, gs, hd = c["h"], c["layers"], 64, 128
+    seed = SEED + (3000 if name == "olmoe_cfg2" else 4000)
+    Bmax = max(batches)
+    max_seq = c["ctx"] + tokens + 1
+    dm = DenseModel(hidden_dim=h, num_heads=c["nh"], num_kv_heads=c["nkv"], num_layers=L,
+                    vocab_size=c["vocab"], qk_norm=c["qk_norm"], rope_theta=c["theta"],
+                    max_batch=Bmax, max_seq=max_seq, device=dev.index)
+    dw = synth.dense_weights_device(seed, h=h, nh=c["nh"], nkv=c["nkv"], hd=hd, layers=L,
+                                    vocab=c["vocab"], qk_norm=c["qk_norm"], device=dev)
+    dm.load_all(dw)
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=c["I"], num_experts=c["E"], top_k=c["K"],
+                   group_size=gs, num_layers=L, norm_topk_prob=c["norm"], max_batch=Bmax,
+                   device=dev.index)
+    for layer in range(L):
+        img = synth.layer_image_device(c["E"], h, c["I"], gs, seed=seed + layer, device=dev)
+        blk.load_expert_layer(layer, img)
+        del img
+        blk.load_router(layer, synth.router_weights(seed + 1000 + layer, c["E"], h))
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 7)
+    for layer in range(L):
+        k, v = dm.kv_cache(layer)
+        k.copy_(torch.randn(k.shape, generator=g, device=dev).to(torch.bfloat16))
+        v.copy_(torch.randn(v.shape, generator=g, device=dev).to(torch.bfloat16))
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    res = {"workload": name, "context": c["ctx"], "steps": tokens, "layers": L,
+           "kernels": "k_embed, then per layer k_dense_gemv (qkv), k_attn_decode, k_dense_gemv "
+                      "(o + post-norm), k_moe_layer; then k_dense_gemv (LM head + argmax)"}
+    peak, kind = measured_peaks()
+    for B in batches:
+        toks = torch.from_numpy(np.random.default_rng(seed + B).integers(
+            0, c["vocab"], size=B).astype(np.int32)).to(dev)
+        buf_in, buf_out = toks.clone(), torch.empty_like(toks)
+        logits = torch.empty((B, c["vocab"]), dtype=torch.float32, device=dev)
+        dm.set_position(c["ctx"])
+        with torch.cuda.stream(stream):
+            dm.step(blk, buf_in, next_tokens=buf_out, logits=logits, stream=stream)
+        torch.cuda.synchronize()
+        dm.synchronize()
+        blk.synchronize()
+        par = None
+        if parity and B == 1:
+            par = decode_parity(dm, blk, dw, c, seed, toks, buf_out, logits)
+        graph = torch.cuda.CUDAGraph()
+        dm.set_position(c["ctx"])
+        with torch.cuda.graph(graph, stream=stream):
+            dm.step(blk, buf_in, next_tokens=buf_out, stream=stream)
+            buf_in.copy_(buf_out)
+        for _ in range(3):  # warm-up replays
+            dm.set_position(c["ctx"])
+            buf_in.copy_(toks)
+            with torch.cuda.stream(stream):
+                graph.replay()
+            torch.cuda.synchronize()
+        dm.set_position(c["ctx"])
+        buf_in.copy_(toks)
+        torch.cuda.synchronize()
+        ms = timed_replays(graph, tokens, stream, 1)
+        dm.synchronize()
+        blk.synchronize()
+        assert dm.position() == c["ctx"] + tokens
+        entry = {"tok_s": B * tokens / (ms * 1e-3), "ms_per_step": ms / tokens}
+        if B == 1:
+            # bytes of one B=1 step: dense weights, LM head, K distinct experts
+            # and the router per layer, the KV rows read (mean position)
+            qd, kvd = c["nh"] * hd, c["nkv"] * hd
+            dense = L * ((qd + 2 * kvd) * h + h * qd) * 2 + c["vocab"] * h * 2
+            experts = L * (c["K"] * expert_bytes(dict(h=h, I=c["I"], gs=gs)) + c["E"] * h * 2)
+            kv = L * 2 * (c["ctx"] + 1 + tokens / 2) * kvd * 2
+            nbytes = dense + experts + kv
+            gbs = nbytes / (ms / tokens * 1e-3) / 1e9
+            entry.update({"algorithmic_bytes_per_step": nbytes, "value": gbs, "unit": "GB/s",
+                          "frac": gbs / peak, "peak_source": kind})
+        if par is not None:
+            entry["parity"] = par
+        res[f"b{B}"] = entry
+        del graph
+    dm.close()
+    blk.close()
+    return res
+
+
+def decode_parity(dm, blk, dw, c, seed, toks, next_tok, logits) -> dict:
+    """Checker (outside the timed region): the first step's logits and token
+    (B = 1, position = context) against the CPU oracle's decode step on the
+    same weights and the same prefilled cache."""
+    import torch
+
+    import oracle
+    oracle.build()
+    from m1moe_b200 import synth
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+    h, L = c["h"], c["layers"]
+    dense = {k: ([bits(x) for x in v] if isinstance(v, list) else bits(v)) for k, v in dw.items()}
+    dense.update(h=h, nh=c["nh"], nkv=c["nkv"], hd=128, layers=L, vocab=c["vocab"], eps=1e-5,
+                 theta=c["theta"], qk_norm=c["qk_norm"])
+    dev = toks.device
+    tables = [synth.layer_image_device(c["E"], h, c["I"], 64, seed=seed + layer, device=dev)
+              .cpu().numpy() for layer in range(L)]
+    routers = [synth.router_weights(seed + 1000 + layer, c["E"], h) for layer in range(L)]
+    moe = dict(tables=tables, routers=routers, inter=c["I"], E=c["E"], K=c["K"], gs=64, norm=c["norm"])
+    kv = []
+    for layer in range(L):
+        k, v = dm.kv_cache(layer)
+        kk, vv = bits(k[:1]), bits(v[:1])
+        kv.append((kk, vv))
+    # the GPU step already stored this position's k and v: the oracle rewrites them
+    ref_tok, ref_lg = oracle.decode_step(dense, moe, kv, toks.cpu().tolist(), c["ctx"],
+                                         nthreads=os.cpu_count() or 1)
+    lg = logits.cpu().numpy()
+    err = float(np.max(np.abs(lg[0] - ref_lg[0])) / max(np.linalg.norm(ref_lg[0]), 1e-30))
+    srt = np.sort(ref_lg[0])[::-1]
+    decisive = bool(srt[0] - srt[1] > 1e-3 * (srt[0] - srt[-1]))
+    same = int(next_tok.cpu().numpy()[0]) == int(ref_tok[0])
+    return {"logits_max_rel_err": err, "token_equal": same, "token_gap_decisive": decisive,
+            "ok": bool(err <= 1e-3 and (same or not decisive)), "tol": 1e-3}
+
+
 def run_gpu(args, wl) -> None:
     import torch
     import torch.distributed as dist
@@ -800,10 +953,13 @@ def run_gpu(args, wl) -> None:
 
     # sub-measurements, each with its own context (the decode tables are freed)
     mixtral_ep = mixtral_ep_measure(dev, world, rank, args.steps, args.warmup)
-    matvec_c0 = mixtral_dec = prefill = None
+    matvec_c0 = mixtral_dec = prefill = decode = None
     if world == 1:
         matvec_c0 = matvec_c0_measure(dev)
         mixtral_dec = mixtral_decode_measure(dev, args.steps, args.warmup)
+        if not args.no_decode_step:
+            decode = {"olmoe_cfg2": decode_step_measure(dev, "olmoe_cfg2", parity=True),
+                      "mixtral_cfg4": decode_step_measure(dev, "mixtral_cfg4")}
         if not args.no_prefill:
             prefill = prefill_measure(dev, args.steps, args.warmup)
 
@@ -838,6 +994,7 @@ def run_gpu(args, wl) -> None:
             "matvec_c0": matvec_c0,
             "mixtral_decode": mixtral_dec,
             "mixtral_ep": mixtral_ep,
+            "decode_step": decode,
             "prefill": prefill,
             "gpu_launches": launches_per_step * (args.steps + 0),
             "clocks": clocks.summary(),
@@ -846,8 +1003,11 @@ def run_gpu(args, wl) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    if not parity["ok"] or not mixtral_ep["parity"]["ok"]:
-        raise SystemExit(f"parity check failed: {parity} {mixtral_ep['parity']}")
+    bad = [] if parity["ok"] and mixtral_ep["parity"]["ok"] else [parity, mixtral_ep["parity"]]
+    if decode and "parity" in decode["olmoe_cfg2"]["b1"] and not decode["olmoe_cfg2"]["b1"]["parity"]["ok"]:
+        bad.append(decode["olmoe_cfg2"]["b1"]["parity"])
+    if bad:
+        raise SystemExit(f"parity check failed: {bad}")
 
 
 def main():

@@ -106,10 +106,15 @@ def _attn_case(oracle_lib, *, nh, nkv, qk_norm, theta, pos, B, max_seq, seed):
         k = oracle_lib.rope(k, nkv, hd, theta, pos)
         kref = oracle_lib.f32_to_bf16_bits(k).reshape(nkv, hd)
         vref = oracle_lib.f32_to_bf16_bits(v).reshape(nkv, hd)
-        # v is stored bit-exactly; k within one bf16 ulp (libm vs CUDA sin/cos/pow)
+        # v is stored bit-exactly; k within one bf16 ulp of itself, or of the
+        # head's largest element near a zero crossing (the rotation angles
+        # differ in the last bits between CUDA's and the C library's
+        # sin/cos/pow)
         assert np.array_equal(v_gpu[t, :, pos, :], vref), t
-        kd = synth.bf16_to_f32(k_gpu[t, :, pos, :]) - synth.bf16_to_f32(kref)
-        assert np.all(np.abs(kd) <= 2.0 ** -7 * np.abs(synth.bf16_to_f32(kref)) + 1e-30), t
+        kf = synth.bf16_to_f32(kref)
+        kd = synth.bf16_to_f32(k_gpu[t, :, pos, :]) - kf
+        bound = 2.0 ** -7 * np.abs(kf) + 2.0 ** -12 * np.abs(kf).max(axis=1, keepdims=True)
+        assert np.all(np.abs(kd) <= bound), (t, float(np.abs(kd).max()))
         kc_t, vc_t = k_gpu[t].copy(), v_gpu[t]
         ref = oracle_lib.attention(q, kc_t, vc_t, nh, nkv, hd, pos + 1)
         errs.append(rel_max_err(out[t], ref))

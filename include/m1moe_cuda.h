@@ -116,6 +116,19 @@ M1MOE_API m1moe_status m1moe_cuda_destroy(m1moe_cuda_ctx *ctx);
 M1MOE_API m1moe_status m1moe_cuda_load_expert_layer(m1moe_cuda_ctx *ctx, int32_t layer,
                                           const void *h_layer_bytes, size_t nbytes);
 
+/* Cold start from the converted model directory: every
+ * <packed_experts_dir>/layer_NN.bin (NN = 00 .. num_layers-1) into the HBM
+ * table, this shard's experts only.  All file sizes are checked first (each
+ * must be num_experts * expert_bytes, the converter's check in
+ * scripts/extract_olmoe.py:340-344); a missing or short file fails the call
+ * with M1MOE_ERR_INVALID_ARG and names it, where the reference would zero the
+ * expert and keep going (InferenceEngine.swift:274-279).  io_threads host
+ * threads pread 32 MB chunks into a ring of pinned buffers while earlier
+ * chunks are copied to the GPU and repacked, the concurrent-read shape of
+ * ExpertCache.prefetch (ExpertCache.swift:126-196); synchronous. */
+M1MOE_API m1moe_status m1moe_cuda_load_expert_files(m1moe_cuda_ctx *ctx, const char *packed_experts_dir,
+                                          int32_t io_threads);
+
 /* Same as above from device memory (stream-ordered), for callers that already
  * hold the layer image in HBM. */
 M1MOE_API m1moe_status m1moe_cuda_load_expert_layer_device(m1moe_cuda_ctx *ctx, int32_t layer,

@@ -60,6 +60,7 @@ _SIGS = [
     ("m1moe_cuda_load_expert_layer", ctypes.c_int, [_vp, _i32, _vp, ctypes.c_size_t]),
     ("m1moe_cuda_load_expert_layer_device", ctypes.c_int, [_vp, _i32, _vp, ctypes.c_size_t, _vp]),
     ("m1moe_cuda_load_router", ctypes.c_int, [_vp, _i32, _vp, ctypes.c_size_t]),
+    ("m1moe_cuda_load_expert_files", ctypes.c_int, [_vp, ctypes.c_char_p, _i32]),
     ("m1moe_cuda_matvec4", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
     ("m1moe_cuda_matvec4_strided", ctypes.c_int,

@@ -15,7 +15,6 @@ from __future__ import annotations
 
 import json
 import mmap
-from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 import numpy as np
@@ -66,17 +65,34 @@ def read_layer(model_dir: str | Path, layer: int, spec: ModelSpec) -> np.ndarray
     return data
 
 
+def check_layer_files(model_dir: str | Path, spec: ModelSpec) -> None:
+    """Every layer file exists with the size the converter guarantees
+    (extract_olmoe.py:340-344), before anything is copied."""
+    want = spec.moe.num_experts * spec.expert_bytes_4bit
+    for L in range(spec.num_layers):
+        p = layer_path(model_dir, L)
+        if not p.exists():
+            raise FileNotFoundError(f"{p}: missing")
+        if p.stat().st_size != want:
+            raise ValueError(f"{p}: {p.stat().st_size} bytes, expected {want}")
+
+
 def load_model_dir(block, spec: ModelSpec, model_dir: str | Path, io_threads: int = 4) -> None:
     """Cold start: fill `block` (a MoEBlock) with every layer's experts and router.
 
+    The expert files go through the library's native loader
+    (MoEBlock.load_expert_files: io_threads threads read 32 MB chunks into
+    pinned buffers while earlier chunks are copied and repacked on the GPU,
+    the concurrent-read shape of ExpertCache.prefetch,
+    ExpertCache.swift:126-196); the routers come from model_weights.bin.
     Unlike the reference, which keeps going with zeroed weights after a short
-    read (InferenceEngine.swift:274-279), a missing or truncated file raises."""
+    read (InferenceEngine.swift:274-279), a missing or wrong-sized file raises
+    before anything is copied."""
+    check_layer_files(model_dir, spec)
     store = WeightStore(model_dir)
     try:
-        with ThreadPoolExecutor(max_workers=max(1, io_threads)) as pool:
-            futs = {L: pool.submit(read_layer, model_dir, L, spec) for L in range(spec.num_layers)}
-            for L in range(spec.num_layers):
-                block.load_expert_layer(L, futs[L].result())
-                block.load_router(L, store.tensor(spec.router_key(L)))
+        block.load_expert_files(Path(model_dir) / "packed_experts", io_threads=io_threads)
+        for L in range(spec.num_layers):
+            block.load_router(L, store.tensor(spec.router_key(L)))
     finally:
         store.close()

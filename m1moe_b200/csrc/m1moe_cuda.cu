@@ -8,13 +8,19 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <algorithm>
 #include <atomic>
+#include <condition_variable>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "m1moe_cuda.h"
@@ -216,6 +222,11 @@ struct m1moe_cuda_ctx {
     uint8_t *pf_xg = nullptr, *pf_act = nullptr;
     bool pf_maps = false;
     CUtensorMap pf_map_gu{}, pf_map_dn{};
+    // native cold-start loader (m1moe_cuda_load_expert_files): two device
+    // staging buffers, a ring of pinned chunk buffers and their copy events
+    void *ld_stage[2] = {nullptr, nullptr};
+    void *ld_pinned[8] = {};
+    cudaEvent_t ld_ev[8] = {};
     // expert parallelism over peer memory (moe_layer.cuh EpLayout)
     int ep_world = 1, ep_rank = 0, ep_b = 0;
     uint8_t *ep_region = nullptr;              // this rank's exchange region
@@ -260,6 +271,11 @@ void free_ctx(m1moe_cuda_ctx *c) {
     for (int i = 0; i < 2; ++i) {
         if (c->pinned[i]) cudaFreeHost(c->pinned[i]);
         if (c->staged[i]) cudaEventDestroy(c->staged[i]);
+    }
+    for (int i = 0; i < 2; ++i) cudaFree(c->ld_stage[i]);
+    for (int i = 0; i < 8; ++i) {
+        if (c->ld_pinned[i]) cudaFreeHost(c->ld_pinned[i]);
+        if (c->ld_ev[i]) cudaEventDestroy(c->ld_ev[i]);
     }
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -862,6 +878,168 @@ m1moe_status m1moe_cuda_load_expert_layer(m1moe_cuda_ctx *c, int32_t layer, cons
         M1_CK(cudaStreamSynchronize(c->stream));  // staging is reused by the next experts
     }
     c->layer_loaded[layer] = 1;
+    return M1MOE_OK;
+}
+
+m1moe_status m1moe_cuda_load_expert_files(m1moe_cuda_ctx *c, const char *dir, int32_t io_threads) {
+    if (!c || !dir) return fail(M1MOE_ERR_INVALID_ARG, "ctx/dir is NULL");
+    const m1moe_cuda_cfg &g = c->cfg;
+    const size_t eb = c->expert_bytes, want = (size_t)g.num_experts * eb;
+    const int nthr = std::max(1, std::min<int>(io_threads, 64));
+    // every file is checked before any copy: a missing or short file fails the
+    // whole load (the converter's size check, extract_olmoe.py:340-344; the
+    // reference engine would silently zero the expert, InferenceEngine.swift
+    // :274-279)
+    std::vector<int> fds(g.num_layers, -1);
+    auto close_all = [&]() {
+        for (int fd : fds)
+            if (fd >= 0) close(fd);
+    };
+    for (int L = 0; L < g.num_layers; ++L) {
+        char path[4096];
+        snprintf(path, sizeof(path), "%s/layer_%02d.bin", dir, L);
+        fds[L] = open(path, O_RDONLY);
+        struct stat st;
+        if (fds[L] < 0 || fstat(fds[L], &st) != 0) {
+            close_all();
+            return fail(M1MOE_ERR_INVALID_ARG, "%s: cannot open (%s)", path, strerror(errno));
+        }
+        if ((size_t)st.st_size != want) {
+            close_all();
+            return fail(M1MOE_ERR_INVALID_ARG, "%s: %lld bytes, expected %zu (= %d experts x %zu)", path,
+                        (long long)st.st_size, want, g.num_experts, eb);
+        }
+#ifdef POSIX_FADV_SEQUENTIAL
+        posix_fadvise(fds[L], 0, 0, POSIX_FADV_SEQUENTIAL);
+#endif
+    }
+    DeviceGuard dg(g.device);
+    // Work list: per layer, groups of `per` experts of this shard (one device
+    // staging buffer each, two buffers alternating), each group cut into
+    // chunks read by the io threads into a ring of pinned buffers.  Copies and
+    // repacks go on one stream, so a staging buffer is reused only after the
+    // repack that read it.
+    const size_t chunk = 32u << 20;
+    constexpr int R = 8;  // pinned ring slots
+    const int per = (int)std::max<size_t>(1, (kStagingBytes / 2) / eb);
+    struct Chunk {
+        int layer, group, e;  // group's first expert (shard-relative) and experts in it
+        int ng;
+        size_t file_off, stage_off, bytes;
+        bool last;
+    };
+    std::vector<Chunk> work;
+    int ngroups = 0;
+    for (int L = 0; L < g.num_layers; ++L)
+        for (int e = 0; e < c->ne; e += per, ++ngroups) {
+            const int n = std::min(per, c->ne - e);
+            const size_t total = (size_t)n * eb, base = (size_t)(c->e0 + e) * eb;
+            for (size_t off = 0; off < total; off += chunk)
+                work.push_back({L, ngroups, e, n, base + off, off, std::min(chunk, total - off),
+                                off + chunk >= total});
+        }
+    if (!c->ld_stage[0]) {
+        const size_t sb = (size_t)std::min(per, c->ne) * eb;
+        M1_CK(cudaMalloc(&c->ld_stage[0], sb));
+        M1_CK(cudaMalloc(&c->ld_stage[1], sb));
+    }
+    if (!c->ld_pinned[0]) {
+        for (int i = 0; i < R; ++i) {
+            M1_CK(cudaHostAlloc(&c->ld_pinned[i], chunk, cudaHostAllocDefault));
+            M1_CK(cudaEventCreateWithFlags(&c->ld_ev[i], cudaEventDisableTiming));
+        }
+    }
+    const long long nwork = (long long)work.size();
+    std::mutex mu;
+    std::condition_variable cv;
+    std::vector<uint8_t> ready(nwork, 0);
+    long long consumed = 0;           // chunks whose copy the main thread has issued
+    std::atomic<long long> next{0};   // next chunk for an io thread
+    std::atomic<bool> stop{false};
+    std::string io_err;
+    auto worker = [&]() {
+        for (;;) {
+            const long long k = next.fetch_add(1);
+            if (k >= nwork || stop.load()) return;
+            const int slot = (int)(k % R);
+            {
+                // the slot's previous chunk (k - R) must have been handed to the GPU ...
+                std::unique_lock<std::mutex> lk(mu);
+                cv.wait(lk, [&] { return consumed > k - R || stop.load(); });
+            }
+            if (stop.load()) return;
+            // ... and copied out of the slot
+            if (k >= R && cudaEventSynchronize(c->ld_ev[slot]) != cudaSuccess) {
+                std::lock_guard<std::mutex> lk(mu);
+                io_err = "waiting for a pinned buffer's copy failed";
+                stop = true;
+                cv.notify_all();
+                return;
+            }
+            const Chunk &w = work[k];
+            uint8_t *dst = static_cast<uint8_t *>(c->ld_pinned[slot]);
+            size_t got = 0;
+            while (got < w.bytes) {
+                const ssize_t r = pread(fds[w.layer], dst + got, w.bytes - got, (off_t)(w.file_off + got));
+                if (r <= 0) break;
+                got += (size_t)r;
+            }
+            std::lock_guard<std::mutex> lk(mu);
+            if (got != w.bytes) {
+                char buf[256];
+                snprintf(buf, sizeof(buf), "layer_%02d.bin: short read at byte %zu", w.layer,
+                         w.file_off + got);
+                io_err = buf;
+                stop = true;
+            }
+            ready[k] = 1;
+            cv.notify_all();
+        }
+    };
+    std::vector<std::thread> pool;
+    for (int i = 0; i < nthr; ++i) pool.emplace_back(worker);
+    m1moe_status st = M1MOE_OK;
+    for (long long k = 0; k < nwork && st == M1MOE_OK; ++k) {
+        {
+            std::unique_lock<std::mutex> lk(mu);
+            cv.wait(lk, [&] { return ready[k] || stop.load(); });
+            if (stop.load() && !io_err.empty()) {
+                st = fail(M1MOE_ERR_INVALID_ARG, "%s", io_err.c_str());
+                break;
+            }
+        }
+        const Chunk &w = work[k];
+        const int slot = (int)(k % R);
+        uint8_t *stage = static_cast<uint8_t *>(c->ld_stage[w.group & 1]);
+        cudaError_t e = cudaMemcpyAsync(stage + w.stage_off, c->ld_pinned[slot], w.bytes,
+                                        cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(c->ld_ev[slot], c->stream);
+        if (e != cudaSuccess) {
+            st = cuda_fail(e, "expert file copy");
+            break;
+        }
+        if (w.last) {
+            uint8_t *dst = c->table + ((size_t)w.layer * c->ne + w.e) * c->tl.block;
+            st = repack_experts(c, stage, dst, w.ng, c->stream);
+        }
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            consumed = k + 1;
+        }
+        cv.notify_all();
+    }
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (st != M1MOE_OK) stop = true;
+        consumed = nwork + R;
+    }
+    cv.notify_all();
+    for (auto &t : pool) t.join();
+    close_all();
+    const cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (st != M1MOE_OK) return st;
+    if (e != cudaSuccess) return cuda_fail(e, "expert file load");
+    for (int L = 0; L < g.num_layers; ++L) c->layer_loaded[L] = 1;
     return M1MOE_OK;
 }
 

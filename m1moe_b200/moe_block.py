@@ -81,6 +81,14 @@ class MoEBlock:
         _lib.call("m1moe_cuda_load_expert_layer", self._ctx, layer,
                   buf.ctypes.data, buf.nbytes)
 
+    def load_expert_files(self, packed_experts_dir, io_threads: int = 4) -> None:
+        """Cold start: every packed_experts/layer_NN.bin of the converted model
+        directory, read by `io_threads` native threads while earlier chunks are
+        copied and repacked (m1moe_cuda_load_expert_files).  Raises
+        M1MoECudaError (INVALID_ARG) naming a missing or wrong-sized file."""
+        _lib.call("m1moe_cuda_load_expert_files", self._ctx, str(packed_experts_dir).encode(),
+                  io_threads)
+
     def load_router(self, layer: int, router_bf16) -> None:
         """router_bf16: bf16 bit patterns [num_experts][hidden_dim] (numpy uint16)."""
         if isinstance(router_bf16, torch.Tensor):

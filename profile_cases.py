@@ -4,6 +4,8 @@
     python profile_cases.py layer mixtral 1   # k_moe_layer, Mixtral shapes
     python profile_cases.py matvec 1          # k_matvec4_ring over 2048 matrices
     python profile_cases.py prefill mixtral 512  # k_prefill_gemm, 512 tokens
+    python profile_cases.py decode olmoe 1    # whole decode steps, config-2 shapes, 2 layers
+    python profile_cases.py trace olmoe 1     # k_moe_layer phase trace summary (no profiler)
 
 Each case builds synthetic weights (m1moe_b200.synth), runs the kernel a few
 times and exits 0; the device footprint stays at a few GB so that a profiler
@@ -94,11 +96,124 @@ def prefill_case(workload: str, tokens: int) -> None:
     print("ok")
 
 
+def decode_case(workload: str, batch: int, layers: int = 2, steps: int = 4) -> None:
+    """Whole decode steps (m1moe_cuda_decode_step) at config 2 or 4 shapes with
+    `layers` layers, the KV cache at the full context: for a launch list of
+    every kernel of a step."""
+    import torch
+
+    from m1moe_b200 import MoEBlock, synth
+    from m1moe_b200.dense import DenseModel
+
+    if workload == "olmoe":
+        h, nh, nkv, V, qk, th, E, K, I, norm, ctx = 2048, 16, 16, 50304, True, 1e4, 64, 8, 1024, False, 2048
+    elif workload == "mixtral":
+        h, nh, nkv, V, qk, th, E, K, I, norm, ctx = 4096, 32, 8, 32000, False, 1e6, 8, 2, 14336, True, 4096
+    else:
+        raise SystemExit(f"unknown workload {workload!r}")
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    dm = DenseModel(hidden_dim=h, num_heads=nh, num_kv_heads=nkv, num_layers=layers, vocab_size=V,
+                    qk_norm=qk, rope_theta=th, max_batch=batch, max_seq=ctx + steps + 1)
+    dm.load_all(synth.dense_weights_device(1, h=h, nh=nh, nkv=nkv, hd=128, layers=layers, vocab=V,
+                                           qk_norm=qk, device=dev))
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, num_layers=layers,
+                   max_batch=batch, norm_topk_prob=norm)
+    for layer in range(layers):
+        img = synth.layer_image_device(E, h, I, 64, seed=layer, device=dev)
+        blk.load_expert_layer(layer, img)
+        del img
+        blk.load_router(layer, synth.router_weights(100 + layer, E, h))
+        k, v = dm.kv_cache(layer)
+        k.normal_()
+        v.normal_()
+    dm.set_position(ctx)
+    tok = torch.arange(batch, dtype=torch.int32, device=dev)
+    for _ in range(steps):
+        tok = dm.step(blk, tok).clone()
+    torch.cuda.synchronize()
+    dm.synchronize()
+    blk.synchronize()
+    dm.close()
+    blk.close()
+    print("ok")
+
+
+def trace_case(workload: str, batch: int, layers: int = 4, calls: int = 20) -> None:
+    """Phase trace of k_moe_layer (m1moe_cuda_set_trace) over `calls` calls of
+    `layers` distinct layers, launched back to back; prints, per phase event,
+    the median over CTAs and calls of its time after the call's first CTA
+    start (us), and the spread of the end event."""
+    import numpy as np
+    import torch
+
+    from m1moe_b200 import MoEBlock, _lib, synth
+
+    if workload == "olmoe":
+        h, inter, e, k, norm = 2048, 1024, 64, 8, False
+    elif workload == "mixtral":
+        h, inter, e, k, norm = 4096, 14336, 8, 2, True
+    else:
+        raise SystemExit(f"unknown workload {workload!r}")
+    torch.cuda.set_device(0)
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=inter, num_experts=e, top_k=k,
+                   num_layers=layers, max_batch=8, norm_topk_prob=norm)
+    for layer in range(layers):
+        img = synth.layer_image_device(e, h, inter, 64, seed=layer, device="cuda")
+        blk.load_expert_layer(layer, img)
+        del img
+        blk.load_router(layer, synth.router_weights(100 + layer, e, h))
+    x = torch.randn(batch, h, device="cuda")
+    out = torch.empty(batch, h, device="cuda")
+    trace = torch.zeros((160, 24), dtype=torch.int64, device="cuda")
+    names = {0: "start", 1: "out rows init", 2: "logits published", 12: "all logits seen",
+             13: "ranks counted", 3: "top-K ranked", 19: "producer saw routing",
+             16: "geometry", 11: "first tile issued", 4: "consumers released", 5: "first tile landed",
+             9: "all tiles issued", 17: "gate/up done", 6: "activations quantised",
+             18: "first down item", 22: "first down tile", 23: "last down tile", 7: "epochs seen",
+             8: "down items done", 10: "end"}
+    rows = {ev: [] for ev in names}
+    for it in range(calls + 3):
+        for layer in range(layers):
+            rec = it >= 3 and layer == layers - 1
+            _lib.call("m1moe_cuda_set_trace", blk._ctx, trace.data_ptr() if rec else 0)
+            _lib.call("m1moe_cuda_moe_layer", blk._ctx, layer, x.data_ptr(), 0, x.data_ptr(), 0,
+                      out.data_ptr(), 0, batch, 0, 0, 0)
+            if rec:
+                torch.cuda.synchronize()
+                t = trace.cpu().numpy().astype(np.int64)
+                G = min(148, 160)
+                ns0, ns1 = t[:G, 20], t[:G, 21]
+                c0, c1 = t[:G, 0], t[:G, 10]
+                # cycles -> ns per CTA from its own start/end pair
+                scale = (ns1 - ns0) / np.maximum(c1 - c0, 1)
+                t0 = ns0.min()
+                for ev in names:
+                    vals = ns0 + (t[:G, ev] - c0) * scale - t0
+                    ok = t[:G, ev] != 0
+                    if ok.any():
+                        rows[ev].append(np.median(vals[ok]) / 1e3)
+                trace.zero_()
+    _lib.call("m1moe_cuda_set_trace", blk._ctx, 0)
+    blk.synchronize()
+    print(f"k_moe_layer phase trace: {workload}, batch {batch}, median over CTAs and {calls} calls")
+    print("| event | us after the first CTA's start |")
+    print("|---|---|")
+    order = sorted((float(np.median(v)), ev) for ev, v in rows.items() if v)
+    for med, ev in order:
+        print(f"| {names[ev]} | {med:.2f} |")
+    blk.close()
+
+
 def main(argv: list[str]) -> None:
     if len(argv) >= 1 and argv[0] == "layer":
         layer_case(argv[1] if len(argv) > 1 else "olmoe", int(argv[2]) if len(argv) > 2 else 1)
     elif len(argv) >= 1 and argv[0] == "prefill":
         prefill_case(argv[1] if len(argv) > 1 else "mixtral", int(argv[2]) if len(argv) > 2 else 512)
+    elif len(argv) >= 1 and argv[0] == "decode":
+        decode_case(argv[1] if len(argv) > 1 else "olmoe", int(argv[2]) if len(argv) > 2 else 1)
+    elif len(argv) >= 1 and argv[0] == "trace":
+        trace_case(argv[1] if len(argv) > 1 else "olmoe", int(argv[2]) if len(argv) > 2 else 1)
     elif len(argv) >= 1 and argv[0] == "matvec":
         matvec_case(int(argv[1]) if len(argv) > 1 else 1)
     else:

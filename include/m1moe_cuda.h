@@ -253,6 +253,20 @@ M1MOE_API m1moe_status m1moe_cuda_ep_region(m1moe_cuda_ctx *ctx, int32_t world,
 M1MOE_API m1moe_status m1moe_cuda_ep_connect(m1moe_cuda_ctx *ctx, int32_t rank,
                                    const void *h_handles);
 
+/* Single-process form of m1moe_cuda_ep_connect, for one process that drives
+ * several GPUs (or, in tests, several contexts on one GPU): ctxs[r] is rank
+ * r's context (ctxs[rank] == ctx), each with its exchange region already made
+ * by m1moe_cuda_ep_region with the same world and tokens_per_rank; peer access
+ * between different devices is enabled here. */
+M1MOE_API m1moe_status m1moe_cuda_ep_connect_local(m1moe_cuda_ctx *ctx, int32_t rank,
+                                         m1moe_cuda_ctx *const *ctxs);
+
+/* How many polls an expert-parallel flag wait makes before it gives up, sets
+ * the device error word and lets the call unwind (0 = the default, 2^22
+ * polls with back-off, about a second).  A short limit lets failure drills
+ * and tests see a missing rank within milliseconds. */
+M1MOE_API m1moe_status m1moe_cuda_set_wait_limit(m1moe_cuda_ctx *ctx, uint32_t polls);
+
 /* One expert-parallel MoE step for this rank's tokens (stream-ordered):
  * d_x, d_residual and d_out hold this rank's tokens_per_rank tokens; out =
  * residual + sum over ALL ranks' experts.  Every rank must make the same

@@ -75,6 +75,8 @@ _SIGS = [
      [_vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp]),
     ("m1moe_cuda_ep_region", ctypes.c_int, [_vp, _i32, _i32, _vp]),
     ("m1moe_cuda_ep_connect", ctypes.c_int, [_vp, _i32, _vp]),
+    ("m1moe_cuda_ep_connect_local", ctypes.c_int, [_vp, _i32, _vp]),
+    ("m1moe_cuda_set_wait_limit", ctypes.c_int, [_vp, ctypes.c_uint32]),
     ("m1moe_cuda_moe_layer_ep", ctypes.c_int,
      [_vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp, _vp]),
     ("m1moe_cuda_moe_layer_host", ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp]),

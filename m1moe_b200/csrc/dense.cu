@@ -166,7 +166,7 @@ m1moe_status gemv_nt(const m1::GemvParams &p, int num_sms, cudaStream_t st) {
     D_CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;
     D_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nw * 32, smem));
-    per_sm = std::max(1, std::min(per_sm, 2));
+    per_sm = std::max(1, std::min(per_sm, 4));
     // rows per CTA at least one round
     const int grid = std::max(1, std::min(per_sm * num_sms, (p.rows + m1::GemvRound<NT>::U - 1) /
                                                                m1::GemvRound<NT>::U));
@@ -190,6 +190,13 @@ m1moe_status check_gemv_shape(int rows, int K, int B) {
     return M1MOE_OK;
 }
 
+// Position splits per (token, KV head): about four CTAs per SM over the
+// batch's (token, KV head) pairs, each split at least 32 positions.
+int attn_splits(int num_sms, int nkv, int B, int max_seq) {
+    const int want = (4 * num_sms + nkv * B - 1) / (nkv * B);
+    return std::max(1, std::min(std::min(want, m1::kAttnMaxSplit), (max_seq + 31) / 32));
+}
+
 m1::AttnParams attn_params(m1moe_dense_ctx *c, int layer, const float *qkv, int B, float *out) {
     const m1moe_dense_cfg &g = c->cfg;
     m1::AttnParams p{};
@@ -208,7 +215,7 @@ m1::AttnParams attn_params(m1moe_dense_ctx *c, int layer, const float *qkv, int 
     const size_t cache_layer = (size_t)g.max_batch * g.num_kv_heads * g.max_seq * c->hd;
     p.kc = c->kc + (size_t)layer * cache_layer;
     p.vc = c->vc + (size_t)layer * cache_layer;
-    p.nsplit = c->nsplit;
+    p.nsplit = attn_splits(c->num_sms, g.num_kv_heads, B, g.max_seq);
     p.part = c->part;
     p.cnt = c->attn_cnt;
     p.out = out;
@@ -218,7 +225,7 @@ m1::AttnParams attn_params(m1moe_dense_ctx *c, int layer, const float *qkv, int 
 
 m1moe_status launch_attn(m1moe_dense_ctx *c, const m1::AttnParams &p, int B, cudaStream_t st) {
     const int hp = c->cfg.num_heads / c->cfg.num_kv_heads;
-    const dim3 grid(c->nsplit, c->cfg.num_kv_heads, B), block(m1::kAttnThreads);
+    const dim3 grid(p.nsplit, c->cfg.num_kv_heads, B), block(m1::kAttnThreads);
     switch (hp) {
     case 1: return launch_pdl(m1::k_attn_decode<1>, grid, block, 0, st, "k_attn_decode launch", p);
     case 2: return launch_pdl(m1::k_attn_decode<2>, grid, block, 0, st, "k_attn_decode launch", p);
@@ -276,9 +283,9 @@ m1moe_status m1moe_cuda_dense_create(const m1moe_dense_cfg *cfg, m1moe_dense_ctx
     int nsm = 0;
     if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, g.device) == cudaSuccess && nsm > 0)
         c->num_sms = nsm;
-    // position splits: about two CTAs per SM over (max_batch x KV heads)
-    c->nsplit = std::max(1, std::min((2 * c->num_sms + g.num_kv_heads - 1) / g.num_kv_heads,
-                                     (g.max_seq + 31) / 32));
+    // position splits (chosen per call by attn_splits); the partials are
+    // sized for the most, at batch 1
+    c->nsplit = attn_splits(c->num_sms, g.num_kv_heads, 1, g.max_seq);
     c->loaded.assign(kNumTensors, std::vector<uint8_t>(g.num_layers, 0));
     const size_t h = g.hidden_dim, V = g.vocab_size, L = g.num_layers, B = g.max_batch;
     const size_t cache = L * B * g.num_kv_heads * (size_t)g.max_seq * c->hd;
@@ -408,7 +415,7 @@ m1moe_status m1moe_cuda_dense_synchronize(m1moe_dense_ctx *c) {
     D_CK(cudaMemcpy(&word, c->err, 4, cudaMemcpyDeviceToHost));
     if (word) {
         D_CK(cudaMemset(c->err, 0, 4));
-        return fail(M1MOE_ERR_DEVICE, "dense error word 0x%x (2: a token id or position out of range)", word);
+        return fail(M1MOE_ERR_DEVICE, "dense error word 0x%x (2: a token id or KV position was out of range)", word);
     }
     return M1MOE_OK;
 }

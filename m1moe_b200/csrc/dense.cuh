@@ -260,11 +260,27 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) k_dense_gemv(const GemvPar
     if (!is_last) return;
     __threadfence();
     if constexpr (EPI == kEpiPostNorm) {
-        const int n = p.rows;
-        for (int i = tid; i < p.ntok * n; i += blockDim.x) {
-            const int t = i / n, c = i - t * n;
-            const float rms = rsqrtf(__ldcg(p.ss_acc + t) / (float)n + p.eps);
-            p.post_out[i] = (__ldcg(p.y + i) * rms) * bf16_bits(p.post_w[c]);
+        __shared__ float rms_s[kDenseMaxTok];
+        const int n = p.rows, total = p.ntok * n, nth = blockDim.x;
+        if (tid < p.ntok) rms_s[tid] = rsqrtf(__ldcg(p.ss_acc + tid) / (float)n + p.eps);
+        __syncthreads();
+        // eight independent loads in flight per thread and round (a loop of
+        // dependent L2 round trips would dominate this tail)
+        for (int base = tid; base < total; base += 8 * nth) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * nth;
+                v[j] = i < total ? __ldcg(p.y + i) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * nth;
+                if (i < total) {
+                    const int t = i / n, c = i - t * n;
+                    p.post_out[i] = (v[j] * rms_s[t]) * bf16_bits(p.post_w[c]);
+                }
+            }
         }
         __syncthreads();
         if (tid < kDenseMaxTok) p.ss_acc[tid] = 0.f;
@@ -299,7 +315,7 @@ __global__ void k_embed(const uint16_t *embed, const int32_t *tokens, int vocab,
     if (t >= ntok) return;
     int tok = tokens[t];
     if (tok < 0 || tok >= vocab) {
-        if (threadIdx.x == 0 && err) atomicOr(err, kErrBadExpert);
+        if (threadIdx.x == 0 && err) atomicOr(err, kErrBadIndex);
         tok = 0;
     }
     for (int i = threadIdx.x; i < h; i += blockDim.x)
@@ -334,6 +350,7 @@ __global__ void k_rmsnorm(const void *x, int x_bf16, const uint16_t *w, float ep
 constexpr int kHeadDim = 128;   // dims per head (32 lanes x 4)
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kAttnMaxSplit = 128;  // position splits per (token, KV head)
 
 struct AttnParams {
     const float *qkv;   // [ntok][qkv_stride]: q [nh*hd] | k [nkv*hd] | v [nkv*hd]
@@ -411,7 +428,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
     // split merge below (its output is not to be used)
     const int pos_in = *p.pos;
     const bool bad = pos_in < 0 || pos_in >= p.max_seq;
-    if (bad && threadIdx.x == 0 && split == 0 && g == 0 && t == 0) atomicOr(p.err, kErrBadExpert);
+    if (bad && threadIdx.x == 0 && split == 0 && g == 0 && t == 0) atomicOr(p.err, kErrBadIndex);
     const int pos = bad ? 0 : pos_in;
     const int seq = pos + 1;
     const int hd = kHeadDim, qd = p.nh * hd, kvd = p.nkv * hd;
@@ -540,20 +557,47 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    // merge: every split's max and sum into shared memory (one load per
+    // thread), per head the global max, the splits' factors and the total,
+    // then each output dimension sums its splits with eight loads in flight
+    __shared__ float sm_f[HP][kAttnMaxSplit];
+    __shared__ float sm_L[HP];
+    const int ns = p.nsplit;
+    const float *base = p.part + ((size_t)t * p.nh + g * HP) * ns * hd2;
+    for (int i = threadIdx.x; i < HP * ns; i += kAttnThreads) {
+        const int hh = i / ns, s2 = i - hh * ns;
+        sm_f[hh][s2] = __ldcg(base + ((size_t)hh * ns + s2) * hd2 + hd);
+    }
+    __syncthreads();
+    for (int hh = warp; hh < HP; hh += kAttnWarps) {
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, sm_f[hh][s2]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.f;
+        for (int s2 = lane; s2 < ns; s2 += 32) {
+            const float ms = sm_f[hh][s2];
+            const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+            L = fmaf(__ldcg(base + ((size_t)hh * ns + s2) * hd2 + hd + 1), f, L);
+            sm_f[hh][s2] = f;
+        }
+        L = warp_sum(L);
+        if (lane == 0) sm_L[hh] = L;
+    }
+    __syncthreads();
     for (int i = threadIdx.x; i < HP * hd; i += kAttnThreads) {
         const int hh = i / hd, d = i - hh * hd;
-        const float *src = p.part + ((size_t)t * p.nh + g * HP + hh) * p.nsplit * hd2;
-        float M = -INFINITY;
-        for (int s2 = 0; s2 < p.nsplit; ++s2) M = fmaxf(M, __ldcg(src + (size_t)s2 * hd2 + hd));
-        float L = 0.f, O = 0.f;
-        for (int s2 = 0; s2 < p.nsplit; ++s2) {
-            const float ms = __ldcg(src + (size_t)s2 * hd2 + hd);
-            if (ms == -INFINITY) continue;
-            const float f = expf(ms - M);
-            L = fmaf(__ldcg(src + (size_t)s2 * hd2 + hd + 1), f, L);
-            O = fmaf(__ldcg(src + (size_t)s2 * hd2 + d), f, O);
+        const float *src = base + (size_t)hh * ns * hd2 + d;
+        float O = 0.f;
+        for (int s0 = 0; s0 < ns; s0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = s0 + j < ns ? __ldcg(src + (size_t)(s0 + j) * hd2) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (s0 + j < ns) O = fmaf(v[j], sm_f[hh][s0 + j], O);
         }
-        p.out[(size_t)t * p.nh * hd + (size_t)(g * HP + hh) * hd + d] = O / L;
+        p.out[(size_t)t * p.nh * hd + (size_t)(g * HP + hh) * hd + d] = O / sm_L[hh];
     }
 }
 

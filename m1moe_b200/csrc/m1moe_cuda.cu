@@ -232,6 +232,7 @@ struct m1moe_cuda_ctx {
     uint8_t *ep_region = nullptr;              // this rank's exchange region
     uint8_t *ep_peer[m1::kMaxRanks] = {};      // every rank's region as mapped here
     bool ep_ready = false;                     // every peer mapped
+    uint32_t ep_wait_limit = m1::kWaitLimit;   // polls of an expert-parallel flag wait
 };
 
 namespace {
@@ -337,6 +338,7 @@ m1::LayerParams layer_params(m1moe_cuda_ctx *c, int layer, int B) {
     p.done = c->done;
     p.epochs = c->epochs;
     p.err = c->err;
+    p.ep_wait_limit = c->ep_wait_limit;
     p.trace = c->trace;
     return p;
 }
@@ -1392,6 +1394,40 @@ m1moe_status m1moe_cuda_ep_connect(m1moe_cuda_ctx *c, int32_t rank, const void *
     }
     c->ep_rank = rank;
     c->ep_ready = true;
+    return M1MOE_OK;
+}
+
+m1moe_status m1moe_cuda_ep_connect_local(m1moe_cuda_ctx *c, int32_t rank, m1moe_cuda_ctx *const *ctxs) {
+    if (!c || !ctxs) return fail(M1MOE_ERR_INVALID_ARG, "ctx/ctxs is NULL");
+    if (!c->ep_region) return fail(M1MOE_ERR_INVALID_ARG, "no exchange region (m1moe_cuda_ep_region)");
+    if (rank < 0 || rank >= c->ep_world)
+        return fail(M1MOE_ERR_INVALID_ARG, "rank %d outside [0,%d)", rank, c->ep_world);
+    if (ctxs[rank] != c) return fail(M1MOE_ERR_INVALID_ARG, "ctxs[rank] must be this context");
+    DeviceGuard dg(c->cfg.device);
+    for (int o = 0; o < c->ep_world; ++o) {
+        const m1moe_cuda_ctx *q = ctxs[o];
+        if (!q || !q->ep_region || q->ep_world != c->ep_world || q->ep_b != c->ep_b)
+            return fail(M1MOE_ERR_INVALID_ARG, "rank %d's context has no matching exchange region", o);
+        if (q->cfg.device != c->cfg.device) {
+            int can = 0;
+            M1_CK(cudaDeviceCanAccessPeer(&can, c->cfg.device, q->cfg.device));
+            if (!can)
+                return fail(M1MOE_ERR_UNSUPPORTED, "device %d cannot access device %d", c->cfg.device,
+                            q->cfg.device);
+            const cudaError_t e = cudaDeviceEnablePeerAccess(q->cfg.device, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+            else if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceEnablePeerAccess");
+        }
+        c->ep_peer[o] = q->ep_region;
+    }
+    c->ep_rank = rank;
+    c->ep_ready = true;
+    return M1MOE_OK;
+}
+
+m1moe_status m1moe_cuda_set_wait_limit(m1moe_cuda_ctx *c, uint32_t polls) {
+    if (!c) return fail(M1MOE_ERR_INVALID_ARG, "ctx is NULL");
+    c->ep_wait_limit = polls ? polls : m1::kWaitLimit;
     return M1MOE_OK;
 }
 

@@ -161,6 +161,7 @@ struct LayerParams {
     float *user_w;    // optional [ntok][K]
     float *user_scores;  // optional [ntok][E]
     int *err;         // device error word
+    uint32_t ep_wait_limit;     // polls before an expert-parallel flag wait gives up
     unsigned long long *trace;  // optional phase timestamps
     // expert parallelism (ep_world > 1): tokens [ep_rank*ep_b, +ep_b) of the
     // ntok = ep_world*ep_b are this rank's (x, residual and out point at them);
@@ -1108,7 +1109,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         if (tid < p.ep_world) {
             const unsigned *fl = reinterpret_cast<const unsigned *>(mine) + tid * 32;
             bool ok = false;
-            for (uint32_t it = 0, nap = 32; it < kWaitLimit; ++it) {
+            for (uint32_t it = 0, nap = 32; it < p.ep_wait_limit; ++it) {
                 if (ld_acquire_sys_u32(fl) == ep_tag) {
                     ok = true;
                     break;
@@ -1781,7 +1782,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 if (tid < W && tid != me && !ctl.abort) {
                     const unsigned *fl = reinterpret_cast<const unsigned *>(mine + (size_t)W * 128) + tid * 32;
                     bool ok = false;
-                    for (uint32_t it = 0, nap = 32; it < kWaitLimit; ++it) {
+                    for (uint32_t it = 0, nap = 32; it < p.ep_wait_limit; ++it) {
                         if (ld_acquire_sys_u32(fl) == ep_tag) {
                             ok = true;
                             break;

@@ -13,7 +13,7 @@ namespace m1 {
 
 // Device error word bits (m1moe_cuda_synchronize reports them as M1MOE_ERR_DEVICE).
 constexpr int kErrWaitTimeout = 1;   // an mbarrier wait exceeded its iteration limit
-constexpr int kErrBadExpert = 2;     // a routed expert index was out of range
+constexpr int kErrBadIndex = 2;      // a token id or a KV position was out of range (dense step)
 constexpr int kErrRange = 4;         // a value left the fp16 range of the tensor-core operands
 
 // A wait gives up after this many try_wait polls (each poll may suspend the

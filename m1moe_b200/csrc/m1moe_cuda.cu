@@ -231,6 +231,7 @@ struct m1moe_cuda_ctx {
     int ep_world = 1, ep_rank = 0, ep_b = 0;
     uint8_t *ep_region = nullptr;              // this rank's exchange region
     uint8_t *ep_peer[m1::kMaxRanks] = {};      // every rank's region as mapped here
+    bool ep_ipc[m1::kMaxRanks] = {};           // mapped by cudaIpcOpenMemHandle (closed at destroy)
     bool ep_ready = false;                     // every peer mapped
     uint32_t ep_wait_limit = m1::kWaitLimit;   // polls of an expert-parallel flag wait
 };
@@ -267,7 +268,7 @@ void free_ctx(m1moe_cuda_ctx *c) {
                     (void *)c->pf_xg, (void *)c->pf_act})
         cudaFree(q);
     for (int r = 0; r < m1::kMaxRanks; ++r)
-        if (c->ep_peer[r] && c->ep_peer[r] != c->ep_region) cudaIpcCloseMemHandle(c->ep_peer[r]);
+        if (c->ep_ipc[r]) cudaIpcCloseMemHandle(c->ep_peer[r]);
     cudaFree(c->ep_region);
     for (int i = 0; i < 2; ++i) {
         if (c->pinned[i]) cudaFreeHost(c->pinned[i]);
@@ -280,6 +281,7 @@ void free_ctx(m1moe_cuda_ctx *c) {
     }
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
+    cudaGetLastError();  // a failed free above must not surface in a later call
 }
 
 #ifndef M1_BOX_SHARE
@@ -1391,6 +1393,7 @@ m1moe_status m1moe_cuda_ep_connect(m1moe_cuda_ctx *c, int32_t rank, const void *
         void *ptr = nullptr;
         M1_CK(cudaIpcOpenMemHandle(&ptr, hnd, cudaIpcMemLazyEnablePeerAccess));
         c->ep_peer[o] = static_cast<uint8_t *>(ptr);
+        c->ep_ipc[o] = true;
     }
     c->ep_rank = rank;
     c->ep_ready = true;

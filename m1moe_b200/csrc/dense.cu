@@ -158,19 +158,23 @@ m1moe_status launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sm
     return M1MOE_OK;
 }
 
+constexpr size_t kGemvSmemCap = 227 * 1024 - 2048;  // dynamic shared memory (static use aside)
+
 template <int NT, int EPI>
-m1moe_status gemv_nt(const m1::GemvParams &p, int num_sms, cudaStream_t st) {
+m1moe_status gemv_nt(m1::GemvParams p, int num_sms, cudaStream_t st) {
     const int nw = p.K / m1::kGemvColsPerWarp;
-    const size_t smem = m1::gemv_smem(nw, NT);
+    // one CTA per SM (the ring takes most of its shared memory), at least a
+    // stage of rows per CTA
+    const int sr = p.K <= 2048 ? 16 : 8;
+    const int grid = std::max(1, std::min(num_sms, (p.rows + sr - 1) / sr));
+    const m1::GemvPlan g = m1::gemv_plan(p.K, NT, (p.rows + grid - 1) / grid, kGemvSmemCap);
+    p.stage_rows = g.stage_rows;
+    p.nstages = g.nstages;
+    p.off_bars = g.off_bars;
+    p.off_part = g.off_part;
     auto kern = m1::k_dense_gemv<NT, EPI>;
-    D_CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    int per_sm = 0;
-    D_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nw * 32, smem));
-    per_sm = std::max(1, std::min(per_sm, 4));
-    // rows per CTA at least one round
-    const int grid = std::max(1, std::min(per_sm * num_sms, (p.rows + m1::GemvRound<NT>::U - 1) /
-                                                               m1::GemvRound<NT>::U));
-    return launch_pdl(kern, dim3(grid), dim3(nw * 32), smem, st, "k_dense_gemv launch", p);
+    D_CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, g.smem));
+    return launch_pdl(kern, dim3(grid), dim3((nw + 1) * 32), (size_t)g.smem, st, "k_dense_gemv launch", p);
 }
 
 template <int EPI>
@@ -440,6 +444,7 @@ m1moe_status m1moe_cuda_dense_gemv(const uint16_t *d_w, int32_t rows, int32_t in
     p.y = d_y;
     p.res = d_res;
     p.ntok = batch;
+    p.err = nullptr;
     int dev = 0, nsm = 148;
     D_CK(cudaGetDevice(&dev));
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
@@ -491,6 +496,7 @@ m1moe_status m1moe_cuda_dense_lm_head(m1moe_dense_ctx *c, const float *d_x, int3
     p.done = c->done;
     p.keys = c->keys;
     p.tokens = d_tokens;
+    p.err = c->err;
     return gemv<m1::kEpiArgmax>(p, c->num_sms, as_stream(stream));
 }
 
@@ -523,6 +529,7 @@ m1moe_status m1moe_cuda_decode_step(m1moe_dense_ctx *c, m1moe_cuda_ctx *moe, con
         q.eps = g.rms_norm_eps;
         q.y = c->qkv;
         q.ntok = batch;
+        q.err = c->err;
         if (m1moe_status s = gemv<m1::kEpiStore>(q, c->num_sms, st)) return s;
         // 3. QK-norm, RoPE, KV store (:194-220) and attention (CMD2, :225)
         if (m1moe_status s = launch_attn(c, attn_params(c, L, c->qkv, batch, c->attn_out), batch, st))
@@ -541,6 +548,7 @@ m1moe_status m1moe_cuda_decode_step(m1moe_dense_ctx *c, m1moe_cuda_ctx *moe, con
         o.post_out = c->h_mid;
         o.ss_acc = c->ss_acc;
         o.done = c->done;
+        o.err = c->err;
         if (m1moe_status s = gemv<m1::kEpiPostNorm>(o, c->num_sms, st)) return s;
         // 5. the MoE block: residual += sum_k w_k Expert_k(h_mid) (:240-266)
         if (m1moe_status s = m1moe_cuda_moe_layer(moe, L, c->h_mid, M1MOE_DTYPE_F32, c->residual,
@@ -562,6 +570,7 @@ m1moe_status m1moe_cuda_decode_step(m1moe_dense_ctx *c, m1moe_cuda_ctx *moe, con
     lm.keys = c->keys;
     lm.tokens = d_next_tokens;
     lm.pos = c->pos;
+    lm.err = c->err;
     return gemv<m1::kEpiArgmax>(lm, c->num_sms, st);
 }
 

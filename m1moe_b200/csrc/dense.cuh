@@ -74,6 +74,9 @@ struct GemvParams {
     float *embed_out;
     int embed_dim;
     int *pos;           // device position, advanced by the argmax's last CTA (or null)
+    int *err;           // device error word (a bounded ring wait gave up)
+    // ring geometry (gemv_plan)
+    int stage_rows, nstages, off_bars, off_part;
 };
 
 __device__ __forceinline__ float dot8_bf16(const uint4 w, const float (&x)[8], float acc) {
@@ -120,33 +123,87 @@ struct GemvRound {
     static constexpr int U = NT <= 4 ? 8 : 4;
 };
 
-// Dynamic shared memory of k_dense_gemv: the warps' partials of one chunk.
-__host__ __device__ inline size_t gemv_smem(int nwarps, int nt) {
-    return (size_t)nwarps * kGemvChunkRows * nt * 4;
+// Shared-memory map of k_dense_gemv (host-planned, gemv_plan): the weight
+// ring [nstages][stage_rows][K] bf16, its full/empty barriers, the warps'
+// partials of one 64-row chunk [nw][kGemvChunkRows][NT] f32.
+struct GemvPlan {
+    int stage_rows, nstages, off_bars, off_part, smem;
+};
+
+__host__ __device__ inline GemvPlan gemv_plan(int K, int nt, int rows_per_cta, size_t smem_cap) {
+    GemvPlan g{};
+    const int nw = K / kGemvColsPerWarp;
+    g.stage_rows = K <= 2048 ? 16 : 8;  // 64 KB stages
+    const size_t stage = (size_t)g.stage_rows * K * 2;
+    const size_t part = (size_t)nw * kGemvChunkRows * nt * 4;
+    const int need = (rows_per_cta + g.stage_rows - 1) / g.stage_rows;
+    int nst = (int)((smem_cap - part - 256) / stage);
+    nst = nst < need ? nst : need;
+    g.nstages = nst < 1 ? 1 : (nst > 4 ? 4 : nst);
+    g.off_bars = (int)(g.nstages * stage);
+    g.off_part = g.off_bars + 2 * 8 * 4;  // room for 4 full + 4 empty barriers
+    g.smem = g.off_part + (int)part;
+    return g;
 }
 
+// One CTA per SM: warps 0..nw-1 own 256 columns each (x in registers), warp
+// nw is the producer.  The CTA's rows are one contiguous block of W, copied
+// stage by stage into the ring with bulk copies; the first stages are
+// requested before waiting on the previous kernel (weights are constants),
+// so the whole block can be in flight while that kernel finishes.
 template <int NT, int EPI>
-__global__ void __launch_bounds__(kGemvMaxWarps * 32) k_dense_gemv(const GemvParams p) {
+__global__ void __launch_bounds__((kGemvMaxWarps + 1) * 32) k_dense_gemv(const GemvParams p) {
     constexpr int U = GemvRound<NT>::U, NV = U * NT, kS = 32 / NV;
-    extern __shared__ __align__(16) float part[];  // [nw][kGemvChunkRows][NT]
+    extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[kGemvMaxWarps][NT];
     __shared__ unsigned long long kred[NT];
     __shared__ int is_last;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const int G = gridDim.x, K = p.K;
-    const int c0 = warp * kGemvColsPerWarp + lane * 8;
+    __shared__ int abort_flag;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nw = (int)(blockDim.x >> 5) - 1, nct = nw * 32;  // consumer warps / threads
+    const int G = gridDim.x, K = p.K, SR = p.stage_rows, NST = p.nstages;
+    const size_t stage_bytes = (size_t)SR * K * 2;
+    uint8_t *ring = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.off_bars);
+    uint64_t *empty = full + 4;
+    float *part = reinterpret_cast<float *>(smem + p.off_part);
     const int r0 = (int)((long long)p.rows * blockIdx.x / G);
     const int r1 = (int)((long long)p.rows * (blockIdx.x + 1) / G);
+    const int nstg = (r1 - r0 + SR - 1) / SR;  // stages of this CTA
+    if (tid == 0) {
+        for (int i = 0; i < NST; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], nw);
+        }
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
     pdl_trigger();
-    uint4 wv[U];
-    auto load_round = [&](int r) {
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-            wv[u] = (r + u < r1) ? ld_stream16(p.w + (size_t)(r + u) * K + c0) : make_uint4(0, 0, 0, 0);
-    };
-    // the weights are constants: the first round goes out before the wait
-    if (r0 < r1) load_round(r0);
+    if (warp == nw) {
+        // ================= producer =================
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            int n = 0;
+            for (; n < nstg; ++n) {
+                const int s = n % NST;
+                if (n >= NST && !mbar_wait(&empty[s], ((n / NST) - 1) & 1, &abort_flag, p.err)) break;
+                const int rs = r0 + n * SR, nr = min(SR, r1 - rs);
+                const uint32_t bytes = (uint32_t)nr * K * 2;
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_g2s(ring + (size_t)s * stage_bytes, p.w + (size_t)rs * K, bytes, &full[s], pol);
+            }
+            // the last stages' copies land before this warp exits (a consumer
+            // that gave up may not be waiting for them)
+            volatile int never = 0;
+            for (int m = n > NST ? n - NST : 0; m < n; ++m)
+                mbar_wait(&full[m % NST], (m / NST) & 1, &never, nullptr);
+        }
+        return;
+    }
+    // ================= consumers =================
     pdl_wait();
+    const int c0 = warp * kGemvColsPerWarp + lane * 8;
     float xr[NT][8];
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
@@ -161,13 +218,13 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) k_dense_gemv(const GemvPar
         // RMSNorm (Shaders.metal:97-134): x * rsqrt(mean(x^2) + eps) * w
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-            float s = 0.f;
+            float s2 = 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) s = fmaf(xr[t][j], xr[t][j], s);
-            s = warp_sum(s);
-            if (lane == 0) red[warp][t] = s;
+            for (int j = 0; j < 8; ++j) s2 = fmaf(xr[t][j], xr[t][j], s2);
+            s2 = warp_sum(s2);
+            if (lane == 0) red[warp][t] = s2;
         }
-        __syncthreads();
+        named_sync(1, nct);
         float nwv[8];
         {
             const uint4 r = *reinterpret_cast<const uint4 *>(p.norm_w + c0);
@@ -194,25 +251,39 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) k_dense_gemv(const GemvPar
         ssl[t] = 0.f;
         kmax[t] = 0ull;
     }
+    bool ok = true;
     for (int cr = r0; cr < r1; cr += kGemvChunkRows) {
         const int ce = min(cr + kGemvChunkRows, r1);
-        for (int r = cr; r < ce; r += U) {
-            float acc[NV];
+        // the chunk's stages (SR divides the chunk's 64 rows)
+        for (int rs = cr; ok && rs < ce; rs += SR) {
+            const int n = (rs - r0) / SR, s = n % NST, nr = min(SR, r1 - rs);
+            ok = mbar_wait(&full[s], (n / NST) & 1, &abort_flag, p.err);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            const uint8_t *st = ring + (size_t)s * stage_bytes + (size_t)c0 * 2;
+            for (int r = 0; r < nr; r += U) {
+                float acc[NV];
 #pragma unroll
-            for (int u = 0; u < U; ++u)
+                for (int u = 0; u < U; ++u) {
+                    const uint4 wv = (r + u < nr) ? *reinterpret_cast<const uint4 *>(st + (size_t)(r + u) * K * 2)
+                                                  : make_uint4(0, 0, 0, 0);
 #pragma unroll
-                for (int t = 0; t < NT; ++t) acc[u * NT + t] = dot8_bf16(wv[u], xr[t], 0.f);
-            // the next round's loads are in flight during the reduction
-            if (r + U < r1) load_round(r + U);
-            const float tot = warp_reduce_multi(acc);
-            if (lane % kS == 0) {
-                const int v = lane / kS, u = v / NT, t = v - u * NT;
-                if (r + u < ce) part[((size_t)warp * kGemvChunkRows + (r + u - cr)) * NT + t] = tot;
+                    for (int t = 0; t < NT; ++t) acc[u * NT + t] = dot8_bf16(wv, xr[t], 0.f);
+                }
+                const float tot = warp_reduce_multi(acc);
+                if (lane % kS == 0) {
+                    const int v = lane / kS, u = v / NT, t = v - u * NT;
+                    if (r + u < nr)
+                        part[((size_t)warp * kGemvChunkRows + (rs + r + u - cr)) * NT + t] = tot;
+                }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        __syncthreads();
+        named_sync(1, nct);
+        if (abort_flag) break;
         const int nrow = ce - cr;
-        for (int i = tid; i < nrow * NT; i += blockDim.x) {
+        for (int i = tid; i < nrow * NT; i += nct) {
             const int rr = i / NT, t = i - rr * NT, row = cr + rr;
             float v = 0.f;
             for (int w = 0; w < nw; ++w) v += part[((size_t)w * kGemvChunkRows + rr) * NT + t];
@@ -226,63 +297,64 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) k_dense_gemv(const GemvPar
                 kmax[t] = k > kmax[t] ? k : kmax[t];
             }
         }
-        __syncthreads();
+        named_sync(1, nct);
     }
+    if (abort_flag) return;  // the producer drains its copies; the error word is set
     if constexpr (EPI == kEpiStore) return;
     // ---- the CTA's contribution, then the last CTA finishes the call ----
     if constexpr (EPI == kEpiPostNorm) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-            const float s = warp_sum(ssl[t]);
-            if (lane == 0) red[warp][t] = s;
+            const float s2 = warp_sum(ssl[t]);
+            if (lane == 0) red[warp][t] = s2;
         }
-        __syncthreads();
+        named_sync(1, nct);
         if (tid < p.ntok) {
-            float s = 0.f;
-            for (int w = 0; w < nw; ++w) s += red[w][tid];
-            atomicAdd(p.ss_acc + tid, s);
+            float s2 = 0.f;
+            for (int w = 0; w < nw; ++w) s2 += red[w][tid];
+            atomicAdd(p.ss_acc + tid, s2);
         }
     } else {
         if (tid < NT) kred[tid] = 0ull;
-        __syncthreads();
+        named_sync(1, nct);
 #pragma unroll
         for (int t = 0; t < NT; ++t)
             if (kmax[t]) atomicMax(&kred[t], kmax[t]);
-        __syncthreads();
+        named_sync(1, nct);
         if (tid < p.ntok) atomicMax(p.keys + tid, kred[tid]);
     }
-    __syncthreads();
+    named_sync(1, nct);
     if (tid == 0) {
         __threadfence();
         is_last = atomicAdd(p.done, 1u) == (unsigned)G - 1u;
     }
-    __syncthreads();
+    named_sync(1, nct);
     if (!is_last) return;
     __threadfence();
     if constexpr (EPI == kEpiPostNorm) {
         __shared__ float rms_s[kDenseMaxTok];
-        const int n = p.rows, total = p.ntok * n, nth = blockDim.x;
+        const int n = p.rows, total = p.ntok * n;
         if (tid < p.ntok) rms_s[tid] = rsqrtf(__ldcg(p.ss_acc + tid) / (float)n + p.eps);
-        __syncthreads();
+        named_sync(1, nct);
         // eight independent loads in flight per thread and round (a loop of
         // dependent L2 round trips would dominate this tail)
-        for (int base = tid; base < total; base += 8 * nth) {
+        for (int base = tid; base < total; base += 8 * nct) {
             float v[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const int i = base + j * nth;
+                const int i = base + j * nct;
                 v[j] = i < total ? __ldcg(p.y + i) : 0.f;
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const int i = base + j * nth;
+                const int i = base + j * nct;
                 if (i < total) {
                     const int t = i / n, c = i - t * n;
                     p.post_out[i] = (v[j] * rms_s[t]) * bf16_bits(p.post_w[c]);
                 }
             }
         }
-        __syncthreads();
+        named_sync(1, nct);
         if (tid < kDenseMaxTok) p.ss_acc[tid] = 0.f;
     } else {
         __shared__ int tok[kDenseMaxTok];
@@ -291,13 +363,13 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) k_dense_gemv(const GemvPar
             tok[tid] = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
             if (p.tokens) p.tokens[tid] = tok[tid];
         }
-        __syncthreads();
+        named_sync(1, nct);
         if (p.embed)
-            for (int i = tid; i < p.ntok * p.embed_dim; i += blockDim.x) {
+            for (int i = tid; i < p.ntok * p.embed_dim; i += nct) {
                 const int t = i / p.embed_dim, c = i - t * p.embed_dim;
                 p.embed_out[i] = bf16_bits(p.embed[(size_t)tok[t] * p.embed_dim + c]);
             }
-        __syncthreads();
+        named_sync(1, nct);
         if (tid < kDenseMaxTok) p.keys[tid] = 0ull;
         if (tid == 0 && p.pos) *p.pos += 1;
     }

@@ -194,10 +194,11 @@ m1moe_status check_gemv_shape(int rows, int K, int B) {
     return M1MOE_OK;
 }
 
-// Position splits per (token, KV head): about four CTAs per SM over the
-// batch's (token, KV head) pairs, each split at least 32 positions.
+// Position splits per (token, KV head): about one CTA per SM over the
+// batch's (token, KV head) pairs (each CTA streams its rows through a
+// two-stage ring; fewer splits keep the final merge short).
 int attn_splits(int num_sms, int nkv, int B, int max_seq) {
-    const int want = (4 * num_sms + nkv * B - 1) / (nkv * B);
+    const int want = (num_sms + nkv * B / 2) / (nkv * B);
     return std::max(1, std::min(std::min(want, m1::kAttnMaxSplit), (max_seq + 31) / 32));
 }
 
@@ -227,14 +228,21 @@ m1::AttnParams attn_params(m1moe_dense_ctx *c, int layer, const float *qkv, int 
     return p;
 }
 
+template <int HP>
+m1moe_status launch_attn_hp(dim3 grid, dim3 block, size_t smem, cudaStream_t st, const m1::AttnParams &p) {
+    D_CK(cudaFuncSetAttribute(m1::k_attn_decode<HP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    return launch_pdl(m1::k_attn_decode<HP>, grid, block, smem, st, "k_attn_decode launch", p);
+}
+
 m1moe_status launch_attn(m1moe_dense_ctx *c, const m1::AttnParams &p, int B, cudaStream_t st) {
     const int hp = c->cfg.num_heads / c->cfg.num_kv_heads;
     const dim3 grid(p.nsplit, c->cfg.num_kv_heads, B), block(m1::kAttnThreads);
+    const size_t smem = m1::attn_smem();
     switch (hp) {
-    case 1: return launch_pdl(m1::k_attn_decode<1>, grid, block, 0, st, "k_attn_decode launch", p);
-    case 2: return launch_pdl(m1::k_attn_decode<2>, grid, block, 0, st, "k_attn_decode launch", p);
-    case 4: return launch_pdl(m1::k_attn_decode<4>, grid, block, 0, st, "k_attn_decode launch", p);
-    case 8: return launch_pdl(m1::k_attn_decode<8>, grid, block, 0, st, "k_attn_decode launch", p);
+    case 1: return launch_attn_hp<1>(grid, block, smem, st, p);
+    case 2: return launch_attn_hp<2>(grid, block, smem, st, p);
+    case 4: return launch_attn_hp<4>(grid, block, smem, st, p);
+    case 8: return launch_attn_hp<8>(grid, block, smem, st, p);
     default: return fail(M1MOE_ERR_UNSUPPORTED, "heads per KV head %d: 1, 2, 4 or 8", hp);
     }
 }

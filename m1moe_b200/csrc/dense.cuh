@@ -420,8 +420,9 @@ __global__ void k_rmsnorm(const void *x, int x_bf16, const uint16_t *w, float ep
 
 // ------------------------------------------------------------ attention ----
 constexpr int kHeadDim = 128;   // dims per head (32 lanes x 4)
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 8;
 constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kAttnStage = 128;     // positions per shared-memory stage (K and V: 64 KB)
 constexpr int kAttnMaxSplit = 128;  // position splits per (token, KV head)
 
 struct AttnParams {
@@ -483,16 +484,39 @@ __device__ __forceinline__ uint2 pack4_bf16(const float (&v)[4]) {
     return r;
 }
 
-// HP: q heads per KV head (the GQA group size), 1..8.
+// Dynamic shared memory of k_attn_decode: two stages of K and V rows.
+__host__ __device__ constexpr size_t attn_smem() {
+    return 2 * 2 * (size_t)kAttnStage * kHeadDim * 2 + 64;
+}
+
+// HP: q heads per KV head (the GQA group size), 1..8.  One CTA per (split,
+// KV head, token); about one CTA per SM in all.  Thread 0 bulk-copies the
+// split's cached K and V rows (positions before `pos`) stage by stage into a
+// two-stage shared-memory ring; 8 warps score 16 positions of a stage each
+// from shared memory; the new token's own k and v (position `pos`) come from
+// registers.
 template <int HP>
-__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnParams p) {
     constexpr int P = HP <= 4 ? 8 : 4;  // positions per warp round (P*HP <= 32)
     constexpr int NV = P * HP, kS = 32 / NV;
+    constexpr int kPerWarp = kAttnStage / kAttnWarps;  // positions of a stage per warp
+    extern __shared__ __align__(128) uint8_t smem[];
     const int split = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int hd = kHeadDim;
+    uint16_t *sk = reinterpret_cast<uint16_t *>(smem);                 // [2][kAttnStage][hd]
+    uint16_t *sv = sk + 2 * (size_t)kAttnStage * hd;                    // [2][kAttnStage][hd]
+    uint64_t *full = reinterpret_cast<uint64_t *>(sv + 2 * (size_t)kAttnStage * hd);
     __shared__ float sm_m[kAttnWarps][HP], sm_l[kAttnWarps][HP];
     __shared__ __align__(16) float sm_o[kAttnWarps][HP][kHeadDim];
-    __shared__ int is_last;
+    __shared__ int is_last, abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
     pdl_trigger();
     pdl_wait();
     // a position outside the cache sets the error word; the call then runs on
@@ -503,10 +527,25 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
     if (bad && threadIdx.x == 0 && split == 0 && g == 0 && t == 0) atomicOr(p.err, kErrBadIndex);
     const int pos = bad ? 0 : pos_in;
     const int seq = pos + 1;
-    const int hd = kHeadDim, qd = p.nh * hd, kvd = p.nkv * hd;
-    // this split's positions: seq cut into nsplit runs of a multiple of 32
-    const int slen = ((seq + p.nsplit - 1) / p.nsplit + 31) & ~31;
-    const int p0 = split * slen, p1 = min(seq, p0 + slen);
+    const int qd = p.nh * hd, kvd = p.nkv * hd;
+    const int slen = (seq + p.nsplit - 1) / p.nsplit;
+    const int p0 = min(seq, split * slen), p1 = min(seq, p0 + slen);
+    const int c1 = min(p1, pos);             // cached rows [p0, c1)
+    const int nst = c1 > p0 ? (c1 - p0 + kAttnStage - 1) / kAttnStage : 0;
+    const bool has_pos = p0 <= pos && pos < p1;
+    const size_t slab = ((size_t)t * p.nkv + g) * p.max_seq * hd;
+    uint16_t *kb = p.kc + slab, *vb = p.vc + slab;
+    auto issue = [&](int j) {  // stage j -> buffer j & 1
+        const int a = p0 + j * kAttnStage, n = min(kAttnStage, c1 - a);
+        const uint32_t bytes = (uint32_t)n * hd * 2;
+        const int b = j & 1;
+        mbar_arrive_expect_tx(&full[b], 2 * bytes);
+        bulk_g2s(sk + (size_t)b * kAttnStage * hd, kb + (size_t)a * hd, bytes, &full[b], 0ull);
+        bulk_g2s(sv + (size_t)b * kAttnStage * hd, vb + (size_t)a * hd, bytes, &full[b], 0ull);
+    };
+    int issued = 0;  // stages issued (thread 0's count)
+    if (threadIdx.x == 0)
+        for (; issued < nst && issued < 2; ++issued) issue(issued);
     const float *qt = p.qkv + (size_t)t * p.qkv_stride;
     float q[HP][4];
 #pragma unroll
@@ -515,19 +554,23 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
         if (p.qn_w) head_rmsnorm(q[hh], p.qn_w, p.eps);
         head_rope(q[hh], pos, p.theta);
     }
-    const size_t slab = ((size_t)t * p.nkv + g) * p.max_seq * hd;
-    uint16_t *kb = p.kc + slab, *vb = p.vc + slab;
-    if (warp == 0 && !bad && p0 <= pos && pos < p1) {
-        // the new token's k (QK-norm, RoPE) and v into the cache, as bf16
-        float k[4], v[4];
-        load4(qt + qd + (size_t)g * hd + 4 * lane, k);
-        load4(qt + qd + kvd + (size_t)g * hd + 4 * lane, v);
-        if (p.kn_w) head_rmsnorm(k, p.kn_w, p.eps);
-        head_rope(k, pos, p.theta);
-        *reinterpret_cast<uint2 *>(kb + (size_t)pos * hd + 4 * lane) = pack4_bf16(k);
-        *reinterpret_cast<uint2 *>(vb + (size_t)pos * hd + 4 * lane) = pack4_bf16(v);
+    float kp[4], vp[4];  // the new token's k and v (warp 0 of the split holding pos)
+    if (warp == 0 && has_pos) {
+        load4(qt + qd + (size_t)g * hd + 4 * lane, kp);
+        load4(qt + qd + kvd + (size_t)g * hd + 4 * lane, vp);
+        if (p.kn_w) head_rmsnorm(kp, p.kn_w, p.eps);
+        head_rope(kp, pos, p.theta);
+        // the cache keeps them as bf16; this step uses the same rounded values
+        const uint2 kq = pack4_bf16(kp), vq = pack4_bf16(vp);
+        if (!bad) {
+            *reinterpret_cast<uint2 *>(kb + (size_t)pos * hd + 4 * lane) = kq;
+            *reinterpret_cast<uint2 *>(vb + (size_t)pos * hd + 4 * lane) = vq;
+        }
+        kp[0] = __uint_as_float(kq.x << 16), kp[1] = __uint_as_float(kq.x & 0xFFFF0000u);
+        kp[2] = __uint_as_float(kq.y << 16), kp[3] = __uint_as_float(kq.y & 0xFFFF0000u);
+        vp[0] = __uint_as_float(vq.x << 16), vp[1] = __uint_as_float(vq.x & 0xFFFF0000u);
+        vp[2] = __uint_as_float(vq.y << 16), vp[3] = __uint_as_float(vq.y & 0xFFFF0000u);
     }
-    __syncthreads();  // the stores above reach this CTA's loads below
     float m[HP], l[HP], o[HP][4];
 #pragma unroll
     for (int hh = 0; hh < HP; ++hh) {
@@ -536,18 +579,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
 #pragma unroll
         for (int i = 0; i < 4; ++i) o[hh][i] = 0.f;
     }
-    for (int pb = p0 + warp * P; pb < p1; pb += kAttnWarps * P) {
-        uint2 kw[P], vw[P];
-#pragma unroll
-        for (int j = 0; j < P; ++j) {
-            const int pp = pb + j;
-            if (pp < p1) {
-                kw[j] = *reinterpret_cast<const uint2 *>(kb + (size_t)pp * hd + 4 * lane);
-                vw[j] = *reinterpret_cast<const uint2 *>(vb + (size_t)pp * hd + 4 * lane);
-            } else {
-                kw[j] = vw[j] = make_uint2(0, 0);
-            }
-        }
+    // online softmax over P positions whose K/V rows (4 dims per lane) are in kw/vw
+    auto consume = [&](const uint2 (&kw)[P], const uint2 (&vw)[P], int nvalid) {
         float acc[NV];
 #pragma unroll
         for (int j = 0; j < P; ++j) {
@@ -560,13 +593,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
         const float tot = warp_reduce_multi(acc);  // lane holds value lane / kS
 #pragma unroll
         for (int hh = 0; hh < HP; ++hh) {
-            float s[P];
+            float sc[P];
             float mx = m[hh];
 #pragma unroll
             for (int j = 0; j < P; ++j) {
-                s[j] = __shfl_sync(0xffffffffu, tot, (j * HP + hh) * kS) * p.scale;
-                if (pb + j >= p1) s[j] = -INFINITY;
-                mx = fmaxf(mx, s[j]);
+                sc[j] = __shfl_sync(0xffffffffu, tot, (j * HP + hh) * kS) * p.scale;
+                if (j >= nvalid) sc[j] = -INFINITY;
+                mx = fmaxf(mx, sc[j]);
             }
             const float corr = expf(m[hh] - mx);  // 0 on the first round (m = -inf)
             l[hh] *= corr;
@@ -574,7 +607,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
             for (int i = 0; i < 4; ++i) o[hh][i] *= corr;
 #pragma unroll
             for (int j = 0; j < P; ++j) {
-                const float e = expf(s[j] - mx);
+                const float e = expf(sc[j] - mx);
                 l[hh] += e;
                 const float v0 = __uint_as_float(vw[j].x << 16), v1 = __uint_as_float(vw[j].x & 0xFFFF0000u);
                 const float v2 = __uint_as_float(vw[j].y << 16), v3 = __uint_as_float(vw[j].y & 0xFFFF0000u);
@@ -585,6 +618,45 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
             }
             m[hh] = mx;
         }
+    };
+    for (int j = 0; j < nst; ++j) {
+        const int b = j & 1, a = p0 + j * kAttnStage, n = min(kAttnStage, c1 - a);
+        bool ok = mbar_wait(&full[b], (j >> 1) & 1, &abort_flag, p.err);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+            const uint16_t *kst = sk + (size_t)b * kAttnStage * hd, *vst = sv + (size_t)b * kAttnStage * hd;
+            for (int i0 = warp * kPerWarp; i0 < min(n, (warp + 1) * kPerWarp); i0 += P) {
+                uint2 kw[P], vw[P];
+                const int nv = min(P, n - i0);
+#pragma unroll
+                for (int jj = 0; jj < P; ++jj) {
+                    const int i = i0 + (jj < nv ? jj : 0);
+                    kw[jj] = *reinterpret_cast<const uint2 *>(kst + (size_t)i * hd + 4 * lane);
+                    vw[jj] = *reinterpret_cast<const uint2 *>(vst + (size_t)i * hd + 4 * lane);
+                }
+                consume(kw, vw, nv);
+            }
+        }
+        __syncthreads();  // every warp is done with buffer b (and saw the abort flag)
+        if (abort_flag) {
+            // a wait gave up: the copies still in flight land before the CTA exits
+            if (threadIdx.x == 0)
+                for (int k = j + 1; k < issued; ++k)
+                    for (uint32_t it = 0; it < kWaitLimit; ++it)
+                        if (mbar_try_wait(&full[k & 1], (k >> 1) & 1)) break;
+            break;
+        }
+        if (threadIdx.x == 0 && j + 2 < nst) issue(issued++);
+    }
+    if (warp == 0 && has_pos) {
+        uint2 kw[P], vw[P];
+        const uint2 kq = pack4_bf16(kp), vq = pack4_bf16(vp);
+#pragma unroll
+        for (int jj = 0; jj < P; ++jj) {
+            kw[jj] = kq;
+            vw[jj] = vq;
+        }
+        consume(kw, vw, 1);
     }
     // merge the warps, then write this split's partial
 #pragma unroll
@@ -629,9 +701,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    // merge: every split's max and sum into shared memory (one load per
-    // thread), per head the global max, the splits' factors and the total,
-    // then each output dimension sums its splits with eight loads in flight
+    // every split's max into shared memory (one load per thread), per head
+    // the global max, the splits' factors and the total, then each output
+    // dimension sums its splits with eight loads in flight
     __shared__ float sm_f[HP][kAttnMaxSplit];
     __shared__ float sm_L[HP];
     const int ns = p.nsplit;
@@ -645,7 +717,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
         float M = -INFINITY;
         for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, sm_f[hh][s2]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
         float L = 0.f;
         for (int s2 = lane; s2 < ns; s2 += 32) {
             const float ms = sm_f[hh][s2];
@@ -664,10 +736,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnParams p
         for (int s0 = 0; s0 < ns; s0 += 8) {
             float v[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = s0 + j < ns ? __ldcg(src + (size_t)(s0 + j) * hd2) : 0.f;
+            for (int jj = 0; jj < 8; ++jj) v[jj] = s0 + jj < ns ? __ldcg(src + (size_t)(s0 + jj) * hd2) : 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (s0 + j < ns) O = fmaf(v[j], sm_f[hh][s0 + j], O);
+            for (int jj = 0; jj < 8; ++jj)
+                if (s0 + jj < ns) O = fmaf(v[jj], sm_f[hh][s0 + jj], O);
         }
         p.out[(size_t)t * p.nh * hd + (size_t)(g * HP + hh) * hd + d] = O / sm_L[hh];
     }

@@ -198,7 +198,7 @@ m1moe_status check_gemv_shape(int rows, int K, int B) {
 // batch's (token, KV head) pairs (each CTA streams its rows through a
 // two-stage ring; fewer splits keep the final merge short).
 int attn_splits(int num_sms, int nkv, int B, int max_seq) {
-    const int want = (num_sms + nkv * B / 2) / (nkv * B);
+    const int want = num_sms / (nkv * B);  // one wave: at most one CTA per SM
     return std::max(1, std::min(std::min(want, m1::kAttnMaxSplit), (max_seq + 31) / 32));
 }
 

@@ -454,18 +454,27 @@ __device__ __forceinline__ void head_rmsnorm(float (&v)[4], const uint16_t *w, f
     for (int i = 0; i < 4; ++i) v[i] *= rms * bf16_bits(w[4 * lane + i]);
 }
 
-// RoPE on a head held 4 per lane (InferenceEngine.swift:521-536): pairs
-// (i, i + hd/2) -- lanes l and l ^ 16 -- rotate by pos * theta^(-2i/hd).
-__device__ __forceinline__ void head_rope(float (&v)[4], int pos, float theta) {
+// The rotation of pair i at position pos (InferenceEngine.swift:521-536):
+// angle = pos * theta^(-2i/hd); rc/rs[i] = cos/sin of it, for the hd/2 pairs.
+__device__ __forceinline__ void rope_table(float *rc, float *rs, int pos, float theta) {
+    for (int i = threadIdx.x; i < kHeadDim / 2; i += blockDim.x) {
+        const float freq = 1.0f / powf(theta, (float)(2 * i) / (float)kHeadDim);
+        const float ang = (float)pos * freq;
+        rc[i] = cosf(ang);
+        rs[i] = sinf(ang);
+    }
+}
+
+// RoPE on a head held 4 per lane: pairs (i, i + hd/2) -- lanes l and l ^ 16
+// -- rotate by the table's angle of pair i.
+__device__ __forceinline__ void head_rope(float (&v)[4], const float *rc, const float *rs) {
     const int lane = threadIdx.x & 31;
     const bool lo = lane < 16;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const float other = __shfl_xor_sync(0xffffffffu, v[i], 16);
         const int pair = 4 * (lane & 15) + i;
-        const float freq = 1.0f / powf(theta, (float)(2 * pair) / (float)kHeadDim);
-        const float ang = (float)pos * freq;
-        const float c = cosf(ang), s = sinf(ang);
+        const float c = rc[pair], s = rs[pair];
         // lo: x0' = x0 c - x1 s; hi: x1' = x0 s + x1 c
         v[i] = lo ? (v[i] * c - other * s) : (other * s + v[i] * c);
     }
@@ -510,14 +519,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnParam
     __shared__ float sm_m[kAttnWarps][HP], sm_l[kAttnWarps][HP];
     __shared__ __align__(16) float sm_o[kAttnWarps][HP][kHeadDim];
     __shared__ int is_last, abort_flag;
+    __shared__ float rope_c[kHeadDim / 2], rope_s[kHeadDim / 2];
     if (threadIdx.x == 0) {
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
         abort_flag = 0;
         mbar_fence_init();
     }
-    __syncthreads();
     pdl_trigger();
+    {
+        // warm L2 with this split's cached rows while the previous kernel
+        // finishes: the position read here may be a step old, which only
+        // makes the hint less exact (a prefetch consumes no data)
+        const int pq = *reinterpret_cast<const volatile int *>(p.pos);
+        if (threadIdx.x == 0 && pq > 0 && pq < p.max_seq) {
+            const int sl = (pq + p.nsplit) / p.nsplit, a = min(pq, split * sl), e = min(pq, a + sl);
+            if (e > a) {
+                const size_t off = (((size_t)t * p.nkv + g) * p.max_seq + a) * kHeadDim;
+                const uint32_t bytes = (uint32_t)(e - a) * kHeadDim * 2;
+                bulk_prefetch_l2(p.kc + off, bytes);
+                bulk_prefetch_l2(p.vc + off, bytes);
+            }
+        }
+    }
     pdl_wait();
     // a position outside the cache sets the error word; the call then runs on
     // position 0 without storing, so that every CTA still takes part in the
@@ -544,6 +568,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnParam
         bulk_g2s(sv + (size_t)b * kAttnStage * hd, vb + (size_t)a * hd, bytes, &full[b], 0ull);
     };
     int issued = 0;  // stages issued (thread 0's count)
+    rope_table(rope_c, rope_s, pos, p.theta);
+    __syncthreads();  // barriers initialised, rotation table written
     if (threadIdx.x == 0)
         for (; issued < nst && issued < 2; ++issued) issue(issued);
     const float *qt = p.qkv + (size_t)t * p.qkv_stride;
@@ -552,14 +578,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnParam
     for (int hh = 0; hh < HP; ++hh) {
         load4(qt + (size_t)(g * HP + hh) * hd + 4 * lane, q[hh]);
         if (p.qn_w) head_rmsnorm(q[hh], p.qn_w, p.eps);
-        head_rope(q[hh], pos, p.theta);
+        head_rope(q[hh], rope_c, rope_s);
     }
     float kp[4], vp[4];  // the new token's k and v (warp 0 of the split holding pos)
     if (warp == 0 && has_pos) {
         load4(qt + qd + (size_t)g * hd + 4 * lane, kp);
         load4(qt + qd + kvd + (size_t)g * hd + 4 * lane, vp);
         if (p.kn_w) head_rmsnorm(kp, p.kn_w, p.eps);
-        head_rope(kp, pos, p.theta);
+        head_rope(kp, rope_c, rope_s);
         // the cache keeps them as bf16; this step uses the same rounded values
         const uint2 kq = pack4_bf16(kp), vq = pack4_bf16(vp);
         if (!bad) {

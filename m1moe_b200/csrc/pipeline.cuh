@@ -85,6 +85,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (no data is consumed, so it
+// is safe ahead of any dependency wait).  src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Programmatic Dependent Launch: wait until the preceding grid in the stream
 // has completed and its memory is visible (a no-op without a PDL predecessor);
 // allow the following grid to start launching.

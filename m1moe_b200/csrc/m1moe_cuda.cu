@@ -233,6 +233,8 @@ struct m1moe_cuda_ctx {
     uint8_t *ep_peer[m1::kMaxRanks] = {};      // every rank's region as mapped here
     bool ep_ipc[m1::kMaxRanks] = {};           // mapped by cudaIpcOpenMemHandle (closed at destroy)
     bool ep_ready = false;                     // every peer mapped
+    int *ep_own_idx = nullptr;                 // this rank's tokens' top-K [b][K] (route-only call)
+    float *ep_own_w = nullptr;
     uint32_t ep_wait_limit = m1::kWaitLimit;   // polls of an expert-parallel flag wait
 };
 
@@ -270,6 +272,8 @@ void free_ctx(m1moe_cuda_ctx *c) {
     for (int r = 0; r < m1::kMaxRanks; ++r)
         if (c->ep_ipc[r]) cudaIpcCloseMemHandle(c->ep_peer[r]);
     cudaFree(c->ep_region);
+    cudaFree(c->ep_own_idx);
+    cudaFree(c->ep_own_w);
     for (int i = 0; i < 2; ++i) {
         if (c->pinned[i]) cudaFreeHost(c->pinned[i]);
         if (c->staged[i]) cudaEventDestroy(c->staged[i]);
@@ -1368,6 +1372,8 @@ m1moe_status m1moe_cuda_ep_region(m1moe_cuda_ctx *c, int32_t world, int32_t toke
     const m1::EpLayout el = m1::ep_layout(world, tokens_per_rank, c->cfg.hidden_dim);
     M1_CK(cudaMalloc((void **)&c->ep_region, (size_t)el.bytes));
     M1_CK(cudaMemset(c->ep_region, 0, (size_t)el.bytes));
+    M1_CK(cudaMalloc((void **)&c->ep_own_idx, (size_t)tokens_per_rank * c->cfg.top_k * 4));
+    M1_CK(cudaMalloc((void **)&c->ep_own_w, (size_t)tokens_per_rank * c->cfg.top_k * 4));
     cudaIpcMemHandle_t hnd;
     M1_CK(cudaIpcGetMemHandle(&hnd, c->ep_region));
     std::memcpy(h_handle, &hnd, sizeof(hnd));
@@ -1446,8 +1452,24 @@ m1moe_status m1moe_cuda_moe_layer_ep(m1moe_cuda_ctx *c, int32_t layer, const voi
     if (!c->router_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "router of layer %d not loaded", layer);
     if (!c->layer_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "experts of layer %d not loaded", layer);
     DeviceGuard dg(c->cfg.device);
+    // 1. route this rank's own tokens once, here (a route-only call at the
+    //    cheap batch of ep_b tokens); the routing travels with the tokens
+    {
+        m1::LayerParams r = layer_params(c, layer, c->ep_b);
+        r.x = d_x;
+        r.x_bf16 = x_dtype == M1MOE_DTYPE_BF16;
+        r.user_idx = c->ep_own_idx;
+        r.user_w = c->ep_own_w;
+        r.route_only = 1;
+        if (m1moe_status st = dispatch_layer(c, r, as_stream(stream))) return st;
+    }
+    // 2. gather every rank's tokens and routing, apply the local experts,
+    //    return each rank its own tokens' sums
     const int B = c->ep_world * c->ep_b;
     m1::LayerParams p = layer_params(c, layer, B);
+    p.ep_pre = 1;
+    p.ep_own_idx = c->ep_own_idx;
+    p.ep_own_w = c->ep_own_w;
     p.x = d_x;
     p.x_bf16 = x_dtype == M1MOE_DTYPE_BF16;
     p.res = d_res;

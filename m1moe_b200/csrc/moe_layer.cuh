@@ -80,15 +80,18 @@ constexpr int kMaxRanks = 8;      // expert-parallel ranks joined over peer memo
 //   [world*128]           done flags, one 128-byte line per source rank
 //   [2*world*128]         the call counter (one line)
 //   [xs_off]              gathered x, f32 [2][world*b][h] (by call parity)
+//   [rt_off]              gathered routing: idx int32 [2][world*b][kMaxTopK], then
+//                         weights f32 [2][world*b][kMaxTopK]
 //   [recv_off]            partial sums received, f32 [2][world][b][h]
 struct EpLayout {
-    long long xs_off, recv_off, bytes;
+    long long xs_off, rt_off, recv_off, bytes;
 };
 
 __host__ __device__ inline EpLayout ep_layout(int world, int b, int h) {
     EpLayout l;
     l.xs_off = (2LL * world + 1) * 128;
-    l.recv_off = l.xs_off + 2LL * world * b * h * 4;
+    l.rt_off = l.xs_off + 2LL * world * b * h * 4;
+    l.recv_off = l.rt_off + 2LL * 2 * world * b * 16 * 4;
     l.bytes = l.recv_off + 2LL * world * b * h * 4;
     return l;
 }
@@ -168,6 +171,11 @@ struct LayerParams {
     // ep_base[r] is rank r's exchange region as mapped here
     int ep_world, ep_rank, ep_b;
     uint8_t *ep_base[kMaxRanks];
+    // routing made at each token's owner (ep_pre): this rank's own tokens'
+    // top-K [ep_b][K] (a route-only call just before), pushed with the tokens
+    int ep_pre;
+    const int *ep_own_idx;
+    const float *ep_own_w;
     // geometry (host-planned)
     int stage_bytes;       // largest tile (bytes)
     int ring_bytes;        // bytes of the tile ring
@@ -346,9 +354,21 @@ __device__ __forceinline__ unsigned long long logit_key(float v, int e) {
 
 template <int NT, bool SL>
 __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, Slots &sl, int *range, float *rlog,
-                          unsigned long long *keys, float *parts, unsigned tag, const volatile int *abort) {
+                          unsigned long long *keys, float *parts, unsigned tag, const volatile int *abort,
+                          bool pre = false) {
     const int tid = threadIdx.x;
     const int E = p.E, K = p.K, ntok = p.ntok, nel = ntok * E;
+    // marks of token t's k-th expert: the caller's index output, and for a
+    // local expert its token mask and the token's k
+    auto mark = [&](int t, int k) {
+        const int e = rs.idx[t][k];
+        if (p.user_idx && blockIdx.x == 0) p.user_idx[t * K + k] = e;
+        if (is_local(p, e)) {
+            atomicOr(&rs.tmask[e], 1u << t);
+            rs.kof[e][t] = (unsigned char)k;
+        }
+    };
+    if (!pre) {
     // a. collect the tagged (partial) logits: all of this thread's loads in
     //    flight at once.  Slot path: word (e, part, t) at (e*LP + part)*NT + t,
     //    t < ntok; otherwise word (t, e) at t*E + e.  nw <= kMaxTok * kMaxExperts.
@@ -420,16 +440,6 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, Slots &sl, int *r
     }
     if (!named_sync_and(2, 256, ok)) return false;
     if (tid == 0) trace_event(p.trace, 0, 12);
-    // marks of token t's k-th expert: the caller's index output, and for a
-    // local expert its token mask and the token's k
-    auto mark = [&](int t, int k) {
-        const int e = rs.idx[t][k];
-        if (p.user_idx && blockIdx.x == 0) p.user_idx[t * K + k] = e;
-        if (is_local(p, e)) {
-            atomicOr(&rs.tmask[e], 1u << t);
-            rs.kof[e][t] = (unsigned char)k;
-        }
-    };
     // b. rank of every (token, expert).  Many tokens over at most 64 experts
     //    (slot path, more than 256 elements): a warp per token holds its keys
     //    in registers, two per lane, and counts the larger ones over 32
@@ -480,6 +490,7 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, Slots &sl, int *r
     }
     named_sync(2, 256);
     if (tid == 0) trace_event(p.trace, 0, 13);
+    }  // !pre (with pre, rs.idx holds the owners' routing and tmask is zero)
     // c. local-expert marks
     for (int i = tid; i < ntok * K; i += 256) {
         int t = 0, k = i;
@@ -1087,23 +1098,33 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         // (advanced by the last CTA at the end of a call) names the call
         ep_tag = ld_acquire_sys_u32(reinterpret_cast<const unsigned *>(mine + 2LL * p.ep_world * 128)) + 1u;
         ep_par = ep_tag & 1;
-        // CTA 0 writes this rank's tokens into every rank's gathered-x slot
-        // for this call's parity, then raises one tagged flag per rank (148
-        // CTAs adding to one counter over NVLink serialise for ~10 us)
+        // CTA o writes this rank's tokens (and, with ep_pre, their routing)
+        // into rank o's gathered slots for this call's parity, then raises
+        // one tagged flag there (148 CTAs adding to one counter over NVLink
+        // serialise for ~10 us; one CTA per destination runs in parallel)
         const int nb = p.ep_b;
-        if (blk == 0) {
-            for (int q = tid; q < p.ep_world * nb * h; q += kLayerThreads) {
-                const int o = q / (nb * h), rem = q - o * nb * h;
-                float *xs = reinterpret_cast<float *>(p.ep_base[o] + el.xs_off) +
-                            ((size_t)ep_par * p.ep_world + p.ep_rank) * nb * h;
-                xs[rem] = load_act(p.x, p.x_bf16, rem);
+        if (blk < p.ep_world) {
+            const int o = blk;
+            float *xs = reinterpret_cast<float *>(p.ep_base[o] + el.xs_off) +
+                        ((size_t)ep_par * p.ep_world + p.ep_rank) * nb * h;
+            for (int q = tid; q < nb * h; q += kLayerThreads) xs[q] = load_act(p.x, p.x_bf16, q);
+            if (p.ep_pre) {
+                const size_t slot = ((size_t)ep_par * p.ep_world + p.ep_rank) * nb * kMaxTopK;
+                int *ri = reinterpret_cast<int *>(p.ep_base[o] + el.rt_off) + slot;
+                float *rw = reinterpret_cast<float *>(p.ep_base[o] + el.rt_off) +
+                            2LL * p.ep_world * nb * kMaxTopK + slot;
+                for (int q = tid; q < nb * p.K; q += kLayerThreads) {
+                    const int j = q / p.K, k = q - j * p.K;
+                    ri[j * kMaxTopK + k] = p.ep_own_idx[q];
+                    rw[j * kMaxTopK + k] = p.ep_own_w[q];
+                }
             }
             // the barrier orders every thread's stores before the release
-            // stores of the flags (release is cumulative): one system-scope
-            // release per rank instead of a system fence in every thread
+            // store of the flag (release is cumulative): one system-scope
+            // release instead of a system fence in every thread
             __syncthreads();
-            if (tid < p.ep_world)
-                st_release_sys_u32(reinterpret_cast<unsigned *>(p.ep_base[tid]) + p.ep_rank * 32, ep_tag);
+            if (tid == 0)
+                st_release_sys_u32(reinterpret_cast<unsigned *>(p.ep_base[o]) + p.ep_rank * 32, ep_tag);
         }
         // every rank's tokens have arrived
         if (tid < p.ep_world) {
@@ -1124,7 +1145,38 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         Xbf16 = 0;
     }
     const int nrows = i1 - i0;
-    if (warp < 8) {
+    const bool pre = ep && p.ep_pre;
+    if (warp < 8 && pre) {
+        // ---- phases 2-3 with the owners' routing (made by their route-only
+        // calls, gathered with the tokens): no logits, no exchange ----
+        const EpLayout el = ep_layout(p.ep_world, p.ep_b, h);
+        const uint8_t *mine = p.ep_base[p.ep_rank];
+        const int *gi = reinterpret_cast<const int *>(mine + el.rt_off) + (size_t)ep_par * p.ntok * kMaxTopK;
+        const float *gw = reinterpret_cast<const float *>(mine + el.rt_off) +
+                          2LL * p.ntok * kMaxTopK + (size_t)ep_par * p.ntok * kMaxTopK;
+        for (int e = tid; e < p.E; e += 256) rs.tmask[e] = 0u;
+        for (int q = tid; q < p.ntok * p.K; q += 256) {
+            const int t = q / p.K, k = q - t * p.K;
+            int e = __ldcv(gi + t * kMaxTopK + k);
+            if (e < 0 || e >= p.E) {  // cannot happen; never index out of the tables
+                set_abort(ctl, p.err);
+                e = 0;
+            }
+            rs.idx[t][k] = e;
+            const float wk = __ldcv(gw + t * kMaxTopK + k);
+            rs.w[t][k] = wk;
+            if (p.user_w && blk == 0) p.user_w[q] = wk;
+        }
+        named_sync(2, 256);
+        named_arrive(6, kLayerThreads);
+        const bool ok = route_cta<NT, SL>(p, rs, sl, ctl.range, rlog, keys, reinterpret_cast<float *>(ring), tag,
+                                          vabort, true);
+        if (tid == 0) {
+            if (ok) ctl.route_ok = 1;
+            else set_abort(ctl, p.err);
+        }
+        named_arrive(3, 256 + 32);
+    } else if (warp < 8) {
         if constexpr (SL) {
             // ---- phase 2: partial logits, straight from global memory ----
             // Work item (e, part): W_r[e] . x[t] over the part's 8-column blocks
@@ -1348,7 +1400,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     }
     // the routing weights: needed only by the caller's outputs and the final
     // atomics, so warps 1..7 compute them while the first copies are in flight
-    if (warp >= 1 && warp < 8 && ctl.route_ok)
+    if (warp >= 1 && warp < 8 && ctl.route_ok && !pre)
         for (int t = warp - 1; t < p.ntok; t += 7) route_weights(p, rs, rlog, t);
     if (!go) {
         if (p.route_only) __syncthreads();  // user outputs complete before the epoch advances

@@ -394,7 +394,7 @@ __device__ bool route_cta(const LayerParams &p, RouteInfo &rs, Slots &sl, int *r
         }
         if (*abort) break;
         __nanosleep(nap);
-        nap = min(nap * 2, 256u);
+        nap = min(nap * 2, 64u);  // the wait is short: keep the wake-up lag small
     }
     // b. the logit of (token, expert) element t*E + e (its parts summed in
     //    order) and its ranking key
@@ -1070,6 +1070,25 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     // scheduled now, and touch nothing until the previous grid has completed
     // and its memory is visible (no-ops without a dependent launch)
     pdl_trigger();
+    // The router is a constant: warps 0..7 load their first block of it
+    // before waiting on the previous kernel, so that the logits need only x
+    // (one L2 round trip) once the wait returns.
+    uint4 wpre = make_uint4(0u, 0u, 0u, 0u);
+    if (warp < 8) {
+        if constexpr (SL) {
+            const int P = p.lparts, n8 = h / 8;
+            constexpr int LT0 = NT == 1 ? 0 : (NT == 2 ? 1 : (NT == 4 ? 2 : 3));
+            if (blk < p.E * P) {
+                const int e = blk / P, part = blk - e * P;
+                const int g8 = n8 * part / P + (tid >> LT0);
+                if (g8 < n8 * (part + 1) / P)
+                    wpre = __ldg(reinterpret_cast<const uint4 *>(p.router + (size_t)e * h) + g8);
+            }
+        } else {
+            if (blk < p.E && tid < h / 8)
+                wpre = __ldg(reinterpret_cast<const uint4 *>(p.router + (size_t)blk * h) + tid);
+        }
+    }
     pdl_wait();
     if (tid == 0) {
         trace_event(p.trace, 0, 0);
@@ -1195,7 +1214,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 float acc = 0.f;
                 if (tt < p.ntok) {
                     for (int g8 = g0 + (tid >> LT); g8 < g1; g8 += 256 >> LT) {
-                        const uint4 wv = __ldg(row + g8);
+                        const uint4 wv = (m == 0 && g8 == g0 + (tid >> LT)) ? wpre : __ldg(row + g8);
                         float xv[8];
                         if (Xbf16) {
                             const uint4 r = *(reinterpret_cast<const uint4 *>(
@@ -1256,7 +1275,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
     #pragma unroll
                 for (int t = 0; t < NT; ++t) acc[t] = 0.f;
                 for (int g8 = tid; g8 < h / 8; g8 += 256) {
-                    const uint4 wv = __ldg(row + g8);
+                    const uint4 wv = (m == 0 && g8 == tid) ? wpre : __ldg(row + g8);
                     const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
                     float wf[8];
     #pragma unroll

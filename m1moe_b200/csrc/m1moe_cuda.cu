@@ -236,6 +236,12 @@ struct m1moe_cuda_ctx {
     int *ep_own_idx = nullptr;                 // this rank's tokens' top-K [b][K] (route-only call)
     float *ep_own_w = nullptr;
     uint32_t ep_wait_limit = m1::kWaitLimit;   // polls of an expert-parallel flag wait
+    // dynamic shared memory last set per k_moe_layer variant (a driver call
+    // per launch otherwise): index by NT (1, 2, 4, 8) and the slot flag
+    int layer_smem_set[4][2] = {};
+    // the synchronous host call as one CUDA graph per (layer, batch, residual
+    // given): copy in, the layer, copy out (m1moe_cuda_moe_layer_host)
+    std::vector<cudaGraphExec_t> host_graphs;
 };
 
 namespace {
@@ -283,6 +289,8 @@ void free_ctx(m1moe_cuda_ctx *c) {
         if (c->ld_pinned[i]) cudaFreeHost(c->ld_pinned[i]);
         if (c->ld_ev[i]) cudaEventDestroy(c->ld_ev[i]);
     }
+    for (cudaGraphExec_t g : c->host_graphs)
+        if (g) cudaGraphExecDestroy(g);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
     cudaGetLastError();  // a failed free above must not surface in a later call
@@ -498,8 +506,14 @@ m1moe_status launch_layer(m1moe_cuda_ctx *c, m1::LayerParams p, cudaStream_t st)
     const size_t smem = plan_layer(p, grid, NT, SL);
     if (smem == 0 || smem > kMaxDynSmem)
         return fail(M1MOE_ERR_UNSUPPORTED, "shape needs more shared memory than an SM has");
-    M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT, SL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem));
+    {
+        int &set = c->layer_smem_set[NT == 1 ? 0 : (NT == 2 ? 1 : (NT == 4 ? 2 : 3))][SL ? 1 : 0];
+        if (set < (int)smem) {
+            M1_CK(cudaFuncSetAttribute(m1::k_moe_layer<NT, SL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem));
+            set = (int)smem;
+        }
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(m1::kLayerThreads);
@@ -1504,17 +1518,42 @@ m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *c, int32_t layer, const f
     // copy costs a few microseconds of its own on the stream)
     float *pin_in = static_cast<float *>(c->hpin);
     float *pin_out = pin_in + 2 * n;
+    if (!c->router_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "router of layer %d not loaded", layer);
+    if (!c->layer_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "experts of layer %d not loaded", layer);
+    // the copies and the layer launch go out as one CUDA graph (captured on
+    // the first call of this layer, batch and residual flag), which costs one
+    // launch instead of three stream operations
+    const size_t key = ((size_t)layer * m1::kMaxTok + (B - 1)) * 2 + (h_res ? 1 : 0);
+    if (c->host_graphs.empty()) c->host_graphs.assign((size_t)c->cfg.num_layers * m1::kMaxTok * 2, nullptr);
+    if (!c->host_graphs[key]) {
+        float *d_out = c->hio;
+        int32_t *d_idx = reinterpret_cast<int32_t *>(d_out + n);
+        float *d_w = reinterpret_cast<float *>(d_idx) + (size_t)B * c->cfg.top_k;
+        M1_CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        cudaError_t e = cudaMemcpyAsync(c->hin, pin_in, h_res ? 2 * hb : hb, cudaMemcpyHostToDevice, c->stream);
+        m1moe_status st = M1MOE_OK;
+        if (e == cudaSuccess)
+            st = m1moe_cuda_moe_layer(c, layer, c->hin, M1MOE_DTYPE_F32, h_res ? c->hin + n : nullptr,
+                                      M1MOE_DTYPE_F32, d_out, M1MOE_DTYPE_F32, B, d_idx, d_w, c->stream);
+        if (e == cudaSuccess && st == M1MOE_OK)
+            e = cudaMemcpyAsync(pin_out, d_out, hb + 2 * kb, cudaMemcpyDeviceToHost, c->stream);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+        if (st != M1MOE_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return st;
+        }
+        if (e == cudaSuccess) e = e2;
+        cudaGraphExec_t exec = nullptr;
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return cuda_fail(e, "host-call graph");
+        c->host_graphs[key] = exec;
+    }
     memcpy(pin_in, h_x, hb);
     if (h_res) memcpy(pin_in + n, h_res, hb);
-    M1_CK(cudaMemcpyAsync(c->hin, pin_in, h_res ? 2 * hb : hb, cudaMemcpyHostToDevice, c->stream));
-    float *d_out = c->hio;
-    int32_t *d_idx = reinterpret_cast<int32_t *>(d_out + n);
-    float *d_w = reinterpret_cast<float *>(d_idx) + (size_t)B * c->cfg.top_k;
-    m1moe_status st = m1moe_cuda_moe_layer(c, layer, c->hin, M1MOE_DTYPE_F32,
-                                           h_res ? c->hin + n : nullptr, M1MOE_DTYPE_F32, d_out,
-                                           M1MOE_DTYPE_F32, B, d_idx, d_w, c->stream);
-    if (st) return st;
-    M1_CK(cudaMemcpyAsync(pin_out, d_out, hb + 2 * kb, cudaMemcpyDeviceToHost, c->stream));
+    M1_CK(cudaGraphLaunch(c->host_graphs[key], c->stream));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     M1_CK(cudaStreamSynchronize(c->stream));
     memcpy(h_out, pin_out, hb);
     if (h_idx) memcpy(h_idx, pin_out + n, kb);

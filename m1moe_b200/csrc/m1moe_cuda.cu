@@ -197,7 +197,7 @@ struct m1moe_cuda_ctx {
     int nbox = 0;                        // logit boxes (CTA c polls box c % nbox)
     int box_words = 0;                   // logit_box_words(grid, E, h)
     float *acc = nullptr;                // [max_batch][h] fp32 sums for bf16 output
-    int *done = nullptr;                 // CTAs finished with their atomics (bf16 output)
+    int *done = nullptr;                 // [2] CTAs finished / past the exchange (accumulator output)
     unsigned *epochs = nullptr;          // per-CTA call counters (moe_layer.cuh)
     int *err = nullptr;           // device error word (pipeline.cuh kErr*)
     unsigned long long *trace = nullptr;  // optional phase timestamps (caller-owned)
@@ -325,7 +325,7 @@ int logit_box_words(int grid, int E, int h) {
 // so no stale word can match after this).
 cudaError_t clear_exchange(m1moe_cuda_ctx *c) {
     cudaError_t e = cudaMemset(c->epochs, 0, kEpochBytes);
-    if (e == cudaSuccess) e = cudaMemset(c->done, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(c->done, 0, 8);
     if (e == cudaSuccess) e = cudaMemset(c->xlog, 0, (size_t)c->nbox * c->box_words * 8);
     return e;
 }
@@ -822,7 +822,7 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     M1_ALLOC(c->router, (size_t)g.num_layers * E * g.hidden_dim * 2);
     M1_ALLOC(c->xlog, (size_t)c->nbox * c->box_words * 8);
     M1_ALLOC(c->acc, B * g.hidden_dim * 4);
-    M1_ALLOC(c->done, 4);
+    M1_ALLOC(c->done, 8);
     M1_ALLOC(c->epochs, kEpochBytes);
     M1_ALLOC(c->err, 4);
     M1_ALLOC(c->hin, 2 * B * g.hidden_dim * 4);

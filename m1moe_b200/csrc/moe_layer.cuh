@@ -79,17 +79,21 @@ constexpr int kMaxRanks = 8;      // expert-parallel ranks joined over peer memo
 //   [0]                   x-ready flags, one 128-byte line per source rank
 //   [world*128]           done flags, one 128-byte line per source rank
 //   [2*world*128]         the call counter (one line)
+//   [sf_off]              slice flags, u32 [world][kMaxCtas]
 //   [xs_off]              gathered x, f32 [2][world*b][h] (by call parity)
 //   [rt_off]              gathered routing: idx int32 [2][world*b][kMaxTopK], then
 //                         weights f32 [2][world*b][kMaxTopK]
 //   [recv_off]            partial sums received, f32 [2][world][b][h]
 struct EpLayout {
-    long long xs_off, rt_off, recv_off, bytes;
+    long long sf_off, xs_off, rt_off, recv_off, bytes;
 };
 
 __host__ __device__ inline EpLayout ep_layout(int world, int b, int h) {
     EpLayout l;
-    l.xs_off = (2LL * world + 1) * 128;
+    // [sf_off] slice flags u32 [world][kMaxCtas]: source rank r's CTA c has
+    // written its slice of this rank's tokens' partial sums
+    l.sf_off = (2LL * world + 1) * 128;
+    l.xs_off = l.sf_off + (long long)world * kMaxCtas * 4;
     l.rt_off = l.xs_off + 2LL * world * b * h * 4;
     l.recv_off = l.rt_off + 2LL * 2 * world * b * 16 * 4;
     l.bytes = l.recv_off + 2LL * world * b * h * 4;
@@ -268,6 +272,12 @@ __device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned l
 __device__ __forceinline__ void st_relaxed_v2_u64(unsigned long long *p, unsigned long long a,
                                                   unsigned long long b) {
     asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 __device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p) {
@@ -1831,27 +1841,44 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 ctl.last = atomicAdd(p.done, 1) == G - 1;
             }
             named_sync(1, kConsumerThreads);
-            if (ctl.last && ep) {
-                __threadfence();
-                // expert parallel: send each rank the partial sums of its tokens,
-                // then add those received to this rank's own, in rank order
+            if (ep) {
+                // expert parallel, spread over every CTA: once all CTAs' sums
+                // are in the accumulator (a grid-wide arrival count: the
+                // launch is cooperative), CTA c sends each peer its slice
+                // [i0, i1) of h for that peer's tokens and raises one flag
+                // there, waits for its slice of this rank's tokens from every
+                // peer, and writes residual + the ranks' sums in rank order
                 const EpLayout el = ep_layout(p.ep_world, p.ep_b, h);
                 const int W = p.ep_world, nb = p.ep_b, me = p.ep_rank;
                 uint8_t *mine = p.ep_base[me];
-                for (int q = tid; q < W * nb * h; q += kConsumerThreads) {
-                    const int o = q / (nb * h);
-                    if (o == me) continue;
-                    const int rem = q - o * nb * h;
-                    float *rv = reinterpret_cast<float *>(p.ep_base[o] + el.recv_off) +
-                                ((size_t)ep_par * W + me) * nb * h;
-                    rv[rem] = __ldcg(p.acc + (size_t)o * nb * h + rem);
+                if (tid == 0) {
+                    bool ok = ctl.abort == 0;
+                    for (uint32_t it = 0, nap = 32; ok && it < kWaitLimit; ++it) {
+                        if (ld_acquire_gpu_s32(p.done) >= G) break;
+                        if (it + 1 == kWaitLimit || *vabort) ok = false;
+                        __nanosleep(nap);
+                        nap = min(nap * 2, 64u);
+                    }
+                    if (!ok && !*vabort) set_abort(ctl, p.err);
+                }
+                named_sync(1, kConsumerThreads);
+                const int sr = i1 - i0;
+                if (!ctl.abort) {
+                    for (int q = tid; q < W * nb * sr; q += kConsumerThreads) {
+                        const int o = q / (nb * sr);
+                        if (o == me) continue;
+                        const int rem = q - o * nb * sr, t = rem / sr, i = i0 + (rem - t * sr);
+                        float *rv = reinterpret_cast<float *>(p.ep_base[o] + el.recv_off) +
+                                    ((size_t)ep_par * W + me) * nb * h;
+                        rv[(size_t)t * h + i] = __ldcg(p.acc + ((size_t)o * nb + t) * h + i);
+                    }
                 }
                 named_sync(1, kConsumerThreads);  // then the release stores below
-                if (tid < W && tid != me)
-                    st_release_sys_u32(reinterpret_cast<unsigned *>(p.ep_base[tid] + (size_t)W * 128) + me * 32,
+                if (tid < W && tid != me && !ctl.abort)
+                    st_release_sys_u32(reinterpret_cast<unsigned *>(p.ep_base[tid] + el.sf_off) + (size_t)me * kMaxCtas + blk,
                                        ep_tag);
                 if (tid < W && tid != me && !ctl.abort) {
-                    const unsigned *fl = reinterpret_cast<const unsigned *>(mine + (size_t)W * 128) + tid * 32;
+                    const unsigned *fl = reinterpret_cast<const unsigned *>(mine + el.sf_off) + (size_t)tid * kMaxCtas + blk;
                     bool ok = false;
                     for (uint32_t it = 0, nap = 32; it < p.ep_wait_limit; ++it) {
                         if (ld_acquire_sys_u32(fl) == ep_tag) {
@@ -1859,24 +1886,31 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                             break;
                         }
                         __nanosleep(nap);
-                        nap = min(nap * 2, 256u);
+                        nap = min(nap * 2, 64u);
                     }
                     if (!ok) set_abort(ctl, p.err);
                 }
                 named_sync(1, kConsumerThreads);
                 const float *rv = reinterpret_cast<const float *>(mine + el.recv_off) + (size_t)ep_par * W * nb * h;
-                for (int q = tid; q < nb * h; q += kConsumerThreads) {
-                    float v = p.res ? load_act(p.res, p.res_bf16, q) : 0.f;
+                for (int q = tid; q < nb * sr; q += kConsumerThreads) {
+                    const int t = q / sr, i = i0 + (q - t * sr);
+                    const size_t oi = (size_t)t * h + i;
+                    float v = p.res ? load_act(p.res, p.res_bf16, oi) : 0.f;
                     for (int o = 0; o < W; ++o)
-                        v += o == me ? __ldcg(p.acc + (size_t)me * nb * h + q) : __ldcg(rv + (size_t)o * nb * h + q);
+                        v += o == me ? __ldcg(p.acc + (size_t)me * nb * h + oi) : __ldcv(rv + (size_t)o * nb * h + oi);
                     if (p.out_bf16)
-                        reinterpret_cast<__nv_bfloat16 *>(p.out)[q] = __float2bfloat16_rn(v);
+                        reinterpret_cast<__nv_bfloat16 *>(p.out)[oi] = __float2bfloat16_rn(v);
                     else
-                        reinterpret_cast<float *>(p.out)[q] = v;
+                        reinterpret_cast<float *>(p.out)[oi] = v;
                 }
-                // the call is complete on this rank: advance its call counter
-                if (tid == 0) st_release_sys_u32(reinterpret_cast<unsigned *>(mine + 2LL * W * 128), ep_tag);
-                if (tid == 0) *p.done = 0;
+                // the last CTA through resets the counts and advances the
+                // region's call counter, which names the next call
+                named_sync(1, kConsumerThreads);
+                if (tid == 0 && atomicAdd(p.done + 1, 1) == G - 1) {
+                    p.done[0] = 0;
+                    p.done[1] = 0;
+                    st_release_sys_u32(reinterpret_cast<unsigned *>(mine + 2LL * W * 128), ep_tag);
+                }
             } else if (ctl.last) {
                 __threadfence();
                 if (p.out_bf16) {

@@ -173,6 +173,8 @@ def trace_case(workload: str, batch: int, layers: int = 4, calls: int = 20) -> N
              18: "first down item", 22: "first down tile", 23: "last down tile", 7: "epochs seen",
              8: "down items done", 10: "end"}
     rows = {ev: [] for ev in names}
+    spread = {ev: [] for ev in names}
+    tiles = []
     for it in range(calls + 3):
         for layer in range(layers):
             rec = it >= 3 and layer == layers - 1
@@ -193,15 +195,22 @@ def trace_case(workload: str, batch: int, layers: int = 4, calls: int = 20) -> N
                     ok = t[:G, ev] != 0
                     if ok.any():
                         rows[ev].append(np.median(vals[ok]) / 1e3)
+                        spread[ev].append((np.percentile(vals[ok], 10) / 1e3, np.percentile(vals[ok], 90) / 1e3))
+                tiles.append(t[:G, 15].copy())
                 trace.zero_()
     _lib.call("m1moe_cuda_set_trace", blk._ctx, 0)
     blk.synchronize()
     print(f"k_moe_layer phase trace: {workload}, batch {batch}, median over CTAs and {calls} calls")
-    print("| event | us after the first CTA's start |")
-    print("|---|---|")
+    print("| event | us after the first CTA's start (median CTA) | 10th / 90th percentile CTA |")
+    print("|---|---|---|")
     order = sorted((float(np.median(v)), ev) for ev, v in rows.items() if v)
     for med, ev in order:
-        print(f"| {names[ev]} | {med:.2f} |")
+        lo = float(np.median([a for a, _ in spread[ev]]))
+        hi = float(np.median([b for _, b in spread[ev]]))
+        print(f"| {names[ev]} | {med:.2f} | {lo:.2f} / {hi:.2f} |")
+    tt = np.concatenate(tiles)
+    ntg, ntd = tt & 0xFFFFFFFF, tt >> 32
+    print(f"\ntiles per CTA: gate/up {np.median(ntg):.0f} (max {ntg.max()}), down {np.median(ntd):.0f} (max {ntd.max()})")
     blk.close()
 
 

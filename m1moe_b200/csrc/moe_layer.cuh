@@ -226,7 +226,6 @@ struct Ctl {
     int range[2];          // cost-weighted split: this CTA's units [range[0], range[1])
     int ntg, ntd;          // gate/up and down tiles of this CTA
     int nsub;              // down tiles per row chunk (ntd = nsub * nic)
-    int dn_first;          // the down tiles come first in tile order (all tiles fit the ring)
     int last;              // this CTA finished last (bf16 output)
     int epochs_seen;       // every CTA's output rows are initialised (1)
     int stage_tile[kMaxStages];  // tile whose copy was last issued into each slot
@@ -738,20 +737,6 @@ __device__ void route_geometry(const LayerParams &p, Ctl &ctl, int blk) {
         for (int cb = a >> 3; cb < (b >> 3); cb = dn_run_end(p, cb, b >> 3)) ++nsub;
         ctl.nsub = nsub;
         ctl.ntd = nsub * p.nic;
-        // When every tile of this CTA fits the ring at once, the down tiles go
-        // out first: the copy engine serves a CTA's copies roughly in issue
-        // order, and the down weights are needed only after the activations,
-        // so they should not be the last bytes to land.  (With less room
-        // than that the order stays gate/up first: down tiles are released
-        // only after gate/up is done, and must not hold ring space that the
-        // gate/up tiles are waiting for.)  An upper bound of the bytes:
-        // gate/up rows, down column blocks and the scale/bias rows of at most
-        // dn_max_cb/gcb + 1 groups per run, 128 bytes of rounding per tile.
-        const int gcb = p.gs >> 3, RC = p.tl.rc;
-        const long long gu = (long long)(b - a) * p.tl.pr;
-        const long long dn = (long long)p.nic * (((b - a) >> 3) + (long long)nsub * (p.dn_max_cb / gcb + 1)) * RC * 4;
-        const long long tot = gu + dn + 128LL * (ctl.ntg + ctl.ntd);
-        ctl.dn_first = (tot <= p.ring_bytes && ctl.ntg + ctl.ntd <= kLayerSlots) ? 1 : 0;
     }
     __syncwarp();
 }
@@ -768,18 +753,12 @@ struct Producer {
 };
 
 // The copies of tile k.  Tile order: gate/up tiles, then the down tiles row
-// chunk by row chunk, runs within a chunk in column order -- or, with
-// dn_first, the down tiles first (gu_tile / dn_tile give a tile's index).
-__device__ __forceinline__ int gu_tile(const Ctl &ctl, int k) { return ctl.dn_first ? ctl.ntd + k : k; }
-__device__ __forceinline__ int dn_tile(const Ctl &ctl, int j) { return ctl.dn_first ? j : ctl.ntg + j; }
-
-__device__ void describe_tile(const LayerParams &p, const Ctl &ctl, int kk, TileCopy &c) {
+// chunk by row chunk, runs within a chunk in column order.
+__device__ void describe_tile(const LayerParams &p, const Ctl &ctl, int k, TileCopy &c) {
     const TiledLayout &tl = p.tl;
     const RouteInfo &rs = ctl.route;
     const int a = ctl.a, b = ctl.b, ntg = ctl.ntg, ntd = ctl.ntd, nsub = ctl.nsub;
     const int GT = p.gu_tile_rows, RC = tl.rc, ncbE = p.I >> 3;
-    // k in the gate/up-first order
-    const int k = !ctl.dn_first ? kk : (kk < ntd ? ntg + kk : kk - ntd);
     if (k < ntg) {
         // gate/up: [a, b) cut at multiples of GT (GT | I, so a tile never
         // crosses experts)
@@ -1492,8 +1471,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             for (;;) {
                 const int q = grab(&ctl.next_gu);
                 if (q >= ng_items) break;
-                const int ng = fdiv(q, p.fd_iptg), rr = q - ng * ipt_g;
-                const int n = gu_tile(ctl, ng), s = n % NSL;
+                const int n = fdiv(q, p.fd_iptg), rr = q - n * ipt_g;
+                const int s = n % NSL;
                 if (!wait_tile(full, ctl, s, n, NSL, p.err)) break;
                 if (q == 0 && lane == 0) trace_event(p.trace, 0, 5);
                 const StageGeo g = ctl.geo[s];
@@ -1508,9 +1487,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             for (;;) {
                 const int q = grab(&ctl.next_gu);
                 if (q >= ng_items) break;
-                const int ng = fdiv(q, p.fd_iptg), rem = q - ng * ipt_g, pg = fdiv(rem, p.fd_nslg),
+                const int n = fdiv(q, p.fd_iptg), rem = q - n * ipt_g, pg = fdiv(rem, p.fd_nslg),
                           j = rem - pg * nslg;
-                const int n = gu_tile(ctl, ng), s = n % NSL;
+                const int s = n % NSL;
                 if (!wait_tile(full, ctl, s, n, NSL, p.err)) break;
                 if (q == 0 && lane == 0) trace_event(p.trace, 0, 5);
                 const StageGeo g = ctl.geo[s];
@@ -1735,13 +1714,13 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 };
                 bool ok = true;
                 for (int jt = 0; jt < nsub; ++jt) {
-                    const int n = dn_tile(ctl, ic * nsub + jt), s = n % NSL;
+                    const int n = ntg + ic * nsub + jt, s = n % NSL;
                     if (!wait_tile(full, ctl, s, n, NSL, p.err)) {
                         ok = false;
                         break;
                     }
-                    if (lane == 0 && wi == 0 && n == dn_tile(ctl, 0)) trace_event(p.trace, 0, 22);
-                    if (lane == 0 && wi == 0 && n == dn_tile(ctl, ntd - 1)) trace_event(p.trace, 0, 23);
+                    if (lane == 0 && wi == 0 && n == ntg) trace_event(p.trace, 0, 22);
+                    if (lane == 0 && wi == 0 && n == ntg + ntd - 1) trace_event(p.trace, 0, 23);
                     const StageGeo g = ctl.geo[s];
                     if (g.u != cur) {
                         if (cur >= 0 && !flush_expert()) {
@@ -1772,13 +1751,13 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 unsigned any = 0u;
                 bool ok = true;
                 for (int jt = 0; jt < nsub; ++jt) {
-                    const int n = dn_tile(ctl, ic * nsub + jt), s = n % NSL;
+                    const int n = ntg + ic * nsub + jt, s = n % NSL;
                     if (!wait_tile(full, ctl, s, n, NSL, p.err)) {
                         ok = false;
                         break;
                     }
-                    if (lane == 0 && wi == 0 && n == dn_tile(ctl, 0)) trace_event(p.trace, 0, 22);
-                    if (lane == 0 && wi == 0 && n == dn_tile(ctl, ntd - 1)) trace_event(p.trace, 0, 23);
+                    if (lane == 0 && wi == 0 && n == ntg) trace_event(p.trace, 0, 22);
+                    if (lane == 0 && wi == 0 && n == ntg + ntd - 1) trace_event(p.trace, 0, 23);
                     const StageGeo g = ctl.geo[s];
                     const int e = rs.ulist[g.u];
                     const unsigned mask = rs.tmask[e];

@@ -437,6 +437,23 @@ M1MOE_API m1moe_status m1moe_cuda_decode_step(m1moe_dense_ctx *ctx, m1moe_cuda_c
                                     const int32_t *d_tokens, int32_t batch, int32_t *d_next_tokens,
                                     float *d_logits, void *stream);
 
+/* Token-parallel prefill of one sequence (sequence slot 0): the T prompt
+ * tokens d_tokens [T] at positions pos .. pos+T-1 (pos = the context's
+ * device position) go through every layer together -- embedding, input
+ * RMSNorm and the q|k|v projection as one bf16 GEMM (cuBLAS, fp32
+ * accumulation), QK-norm + RoPE + the KV store of all T positions, causal
+ * attention, the o projection added to the residual, the post-attention
+ * RMSNorm and the MoE block on the tensor cores (m1moe_cuda_moe_prefill) --
+ * then the last token's final norm, LM head and greedy next token
+ * (d_next_token [1]; d_logits [vocab] may be NULL); the position advances by
+ * T.  The reference runs the prompt token by token through forward()
+ * (bench/main.swift:139-141); this gives the same cache and next token
+ * within the tolerance of its bf16/fp16 GEMM operands.  Buffers for T tokens
+ * are allocated on the first call that needs them (synchronously). */
+M1MOE_API m1moe_status m1moe_cuda_prefill_step(m1moe_dense_ctx *ctx, m1moe_cuda_ctx *moe,
+                                     const int32_t *d_tokens, int32_t tokens,
+                                     int32_t *d_next_token, float *d_logits, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -100,6 +100,7 @@ _SIGS = [
     ("m1moe_cuda_dense_attention", ctypes.c_int, [_vp, _i32, _vp, _i32, _vp, _vp]),
     ("m1moe_cuda_dense_lm_head", ctypes.c_int, [_vp, _vp, _i32, _vp, _vp, _vp]),
     ("m1moe_cuda_decode_step", ctypes.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _vp]),
+    ("m1moe_cuda_prefill_step", ctypes.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _vp]),
 ]
 
 

@@ -22,6 +22,8 @@ LIB = LIBDIR / "libm1moe_cuda.so"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-fvisibility=hidden", "-shared"]
+# cuBLAS for the plain bf16 GEMMs of the token-parallel dense prefill
+LINK_FLAGS = ["-lcublas", "-Xlinker", "-rpath", "-Xlinker", "/usr/local/cuda/lib64"]
 
 
 def _nvcc() -> str:
@@ -49,7 +51,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     cus = sorted(CSRC.glob("*.cu"))
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [_nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}",
-           *[str(c) for c in cus], "-o", str(tmp)]
+           *[str(c) for c in cus], "-o", str(tmp), *LINK_FLAGS]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)

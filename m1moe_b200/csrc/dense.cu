@@ -7,6 +7,7 @@
 // WeightStore.swift:47-126) and MetalContext (f32 scratch and KV buffers,
 // MetalContext.swift:134-152) do.  A decode step joins it with an MoE
 // context (m1moe_cuda.cu) for the expert blocks.
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -56,6 +57,12 @@ struct m1moe_dense_ctx {
     int *err = nullptr;                  // device error word
     int nsplit = 1;
     int num_sms = 148;
+    // token-parallel prefill (m1moe_cuda_prefill_step): buffers for pf_cap
+    // tokens (grown on demand) and the cuBLAS handle of its projections
+    int pf_cap = 0;
+    float *pf_res = nullptr, *pf_qkv = nullptr, *pf_hmid = nullptr;
+    __nv_bfloat16 *pf_xn = nullptr, *pf_attn = nullptr;
+    cublasHandle_t blas = nullptr;
     // which tensors are loaded: [tensor][layer]
     std::vector<std::vector<uint8_t>> loaded;
 };
@@ -132,8 +139,11 @@ void free_dense(m1moe_dense_ctx *c) {
                     (void *)c->post_norm, (void *)c->wqkv, (void *)c->wo, (void *)c->qn, (void *)c->kn,
                     (void *)c->kc, (void *)c->vc, (void *)c->residual, (void *)c->h_mid, (void *)c->qkv,
                     (void *)c->attn_out, (void *)c->part, (void *)c->ss_acc, (void *)c->done,
-                    (void *)c->keys, (void *)c->attn_cnt, (void *)c->pos, (void *)c->err})
+                    (void *)c->keys, (void *)c->attn_cnt, (void *)c->pos, (void *)c->err,
+                    (void *)c->pf_res, (void *)c->pf_qkv, (void *)c->pf_hmid, (void *)c->pf_xn,
+                    (void *)c->pf_attn})
         cudaFree(q);
+    if (c->blas) cublasDestroy(c->blas);
     delete c;
 }
 
@@ -254,6 +264,43 @@ m1moe_status check_loaded(m1moe_dense_ctx *c) {
         for (int L = 0; L < n; ++L)
             if (!c->loaded[t][L]) return fail(M1MOE_ERR_NOT_LOADED, "dense tensor %d of layer %d not loaded", t, L);
     }
+    return M1MOE_OK;
+}
+
+// Buffers for T prefill tokens (grown, never shrunk; a synchronous reallocation).
+m1moe_status pf_dense_reserve(m1moe_dense_ctx *c, int T) {
+    if (!c->blas) {
+        if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS)
+            return fail(M1MOE_ERR_CUDA, "cublasCreate failed");
+    }
+    if (T <= c->pf_cap) return M1MOE_OK;
+    D_CK(cudaDeviceSynchronize());
+    for (void *q : {(void *)c->pf_res, (void *)c->pf_qkv, (void *)c->pf_hmid, (void *)c->pf_xn,
+                    (void *)c->pf_attn})
+        cudaFree(q);
+    c->pf_res = c->pf_qkv = c->pf_hmid = nullptr;
+    c->pf_xn = c->pf_attn = nullptr;
+    c->pf_cap = 0;
+    const size_t h = c->cfg.hidden_dim;
+    D_CK(cudaMalloc((void **)&c->pf_res, (size_t)T * h * 4));
+    D_CK(cudaMalloc((void **)&c->pf_hmid, (size_t)T * h * 4));
+    D_CK(cudaMalloc((void **)&c->pf_qkv, (size_t)T * c->qkv_rows * 4));
+    D_CK(cudaMalloc((void **)&c->pf_xn, (size_t)T * h * 2));
+    D_CK(cudaMalloc((void **)&c->pf_attn, (size_t)T * c->qd * 2));
+    c->pf_cap = T;
+    return M1MOE_OK;
+}
+
+// Y[T][N] = X[T][K] . W[N][K]^T (+ Y if accumulate): a plain bf16 GEMM with
+// fp32 accumulation and output (cuBLAS; column-major view: Y^T = W . X^T).
+m1moe_status gemm_bf16(m1moe_dense_ctx *c, const uint16_t *W, const __nv_bfloat16 *X, float *Y, int N, int K,
+                       int T, bool accumulate, cudaStream_t st) {
+    if (cublasSetStream(c->blas, st) != CUBLAS_STATUS_SUCCESS) return fail(M1MOE_ERR_CUDA, "cublasSetStream");
+    const float alpha = 1.f, beta = accumulate ? 1.f : 0.f;
+    const cublasStatus_t r = cublasGemmEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &alpha, W, CUDA_R_16BF, K, X,
+                                          CUDA_R_16BF, K, &beta, Y, CUDA_R_32F, N, CUBLAS_COMPUTE_32F,
+                                          CUBLAS_GEMM_DEFAULT);
+    if (r != CUBLAS_STATUS_SUCCESS) return fail(M1MOE_ERR_CUDA, "cublasGemmEx failed (%d)", (int)r);
     return M1MOE_OK;
 }
 
@@ -578,6 +625,82 @@ m1moe_status m1moe_cuda_decode_step(m1moe_dense_ctx *c, m1moe_cuda_ctx *moe, con
     lm.keys = c->keys;
     lm.tokens = d_next_tokens;
     lm.pos = c->pos;
+    lm.pos_add = 1;
+    lm.err = c->err;
+    return gemv<m1::kEpiArgmax>(lm, c->num_sms, st);
+}
+
+m1moe_status m1moe_cuda_prefill_step(m1moe_dense_ctx *c, m1moe_cuda_ctx *moe, const int32_t *d_tokens,
+                                     int32_t T, int32_t *d_next_token, float *d_logits, void *stream) {
+    if (!c || !moe || !d_tokens || !d_next_token) return fail(M1MOE_ERR_INVALID_ARG, "NULL pointer");
+    const m1moe_dense_cfg &g = c->cfg;
+    if (T < 1 || T > g.max_seq) return fail(M1MOE_ERR_INVALID_ARG, "tokens %d outside [1,%d]", T, g.max_seq);
+    if (m1moe_status st = check_loaded(c)) return st;
+    if (m1moe_status st = m1abi::moe_compatible(moe, g.hidden_dim, g.num_layers, 1, g.device)) return st;
+    DevGuard dg(g.device);
+    if (m1moe_status st = pf_dense_reserve(c, T)) return st;
+    cudaStream_t st = as_stream(stream);
+    const int h = g.hidden_dim, hd = c->hd;
+    const size_t cache_layer = (size_t)g.max_batch * g.num_kv_heads * g.max_seq * hd;
+    // 1. embed the prompt (InferenceEngine.swift:482-488, per token in the reference)
+    if (m1moe_status s = launch_pdl(m1::k_embed, dim3(T), dim3(256), 0, st, "k_embed launch",
+                                    (const uint16_t *)c->embed, d_tokens, (int)g.vocab_size, h, c->pf_res,
+                                    (int)T, c->err))
+        return s;
+    for (int L = 0; L < g.num_layers; ++L) {
+        // 2. input RMSNorm (bf16 operand) and the q|k|v projection of all tokens
+        if (m1moe_status s = launch_pdl(m1::k_rmsnorm_bf16, dim3(T), dim3(256), 0, st, "k_rmsnorm_bf16 launch",
+                                        (const float *)c->pf_res, (const uint16_t *)(c->in_norm + (size_t)L * h),
+                                        (float)g.rms_norm_eps, c->pf_xn, h))
+            return s;
+        if (m1moe_status s = gemm_bf16(c, c->wqkv + (size_t)L * c->qkv_rows * h, c->pf_xn, c->pf_qkv,
+                                       c->qkv_rows, h, T, false, st))
+            return s;
+        // 3. QK-norm, RoPE, KV store at positions pos .. pos+T-1, then causal attention
+        uint16_t *kc = c->kc + (size_t)L * cache_layer, *vc = c->vc + (size_t)L * cache_layer;
+        const uint16_t *qn = g.qk_norm ? c->qn + (size_t)L * hd : nullptr;
+        const uint16_t *kn = g.qk_norm ? c->kn + (size_t)L * hd : nullptr;
+        if (m1moe_status s = launch_pdl(m1::k_qk_rope_store, dim3(T, g.num_heads + g.num_kv_heads), dim3(32), 0, st,
+                                        "k_qk_rope_store launch", c->pf_qkv, c->qkv_rows, (int)g.num_heads,
+                                        (int)g.num_kv_heads, (const int *)c->pos, (int)g.max_seq, qn, kn,
+                                        (float)g.rms_norm_eps, (float)g.rope_theta, kc, vc, c->err))
+            return s;
+        if (m1moe_status s = launch_pdl(m1::k_attn_prefill, dim3(T, g.num_heads), dim3(128), 0, st,
+                                        "k_attn_prefill launch", (const float *)c->pf_qkv, c->qkv_rows,
+                                        (int)g.num_heads, (int)g.num_kv_heads, (const int *)c->pos, (int)g.max_seq,
+                                        1.0f / sqrtf((float)hd), (const uint16_t *)kc, (const uint16_t *)vc,
+                                        c->pf_attn))
+            return s;
+        // 4. o projection added to the residual, then the post-attention RMSNorm
+        if (m1moe_status s = gemm_bf16(c, c->wo + (size_t)L * h * c->qd, c->pf_attn, c->pf_res, h, c->qd, T,
+                                       true, st))
+            return s;
+        if (m1moe_status s = launch_pdl(m1::k_rmsnorm, dim3(T), dim3(256), 0, st, "k_rmsnorm launch",
+                                        (const void *)c->pf_res, 0, (const uint16_t *)(c->post_norm + (size_t)L * h),
+                                        (float)g.rms_norm_eps, c->pf_hmid, h))
+            return s;
+        // 5. the MoE block of all tokens on the tensor cores
+        if (m1moe_status s = m1moe_cuda_moe_prefill(moe, L, c->pf_hmid, M1MOE_DTYPE_F32, c->pf_res,
+                                                    M1MOE_DTYPE_F32, c->pf_res, M1MOE_DTYPE_F32, T, nullptr,
+                                                    nullptr, stream))
+            return s;
+    }
+    // 6. the last token's final norm, LM head and greedy token; the position
+    //    advances past the prompt
+    m1::GemvParams lm{};
+    lm.w = c->lm_head;
+    lm.rows = g.vocab_size;
+    lm.K = h;
+    lm.x = c->pf_res + (size_t)(T - 1) * h;
+    lm.norm_w = c->final_norm;
+    lm.eps = g.rms_norm_eps;
+    lm.y = d_logits;
+    lm.ntok = 1;
+    lm.done = c->done;
+    lm.keys = c->keys;
+    lm.tokens = d_next_token;
+    lm.pos = c->pos;
+    lm.pos_add = T;
     lm.err = c->err;
     return gemv<m1::kEpiArgmax>(lm, c->num_sms, st);
 }

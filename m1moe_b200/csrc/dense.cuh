@@ -73,7 +73,8 @@ struct GemvParams {
     const uint16_t *embed;     // bf16 [vocab][embed_dim], or null
     float *embed_out;
     int embed_dim;
-    int *pos;           // device position, advanced by the argmax's last CTA (or null)
+    int *pos;           // device position, advanced by pos_add by the argmax's last CTA (or null)
+    int pos_add;
     int *err;           // device error word (a bounded ring wait gave up)
     // ring geometry (gemv_plan)
     int stage_rows, nstages, off_bars, off_part;
@@ -371,7 +372,7 @@ __global__ void __launch_bounds__((kGemvMaxWarps + 1) * 32) k_dense_gemv(const G
             }
         named_sync(1, nct);
         if (tid < kDenseMaxTok) p.keys[tid] = 0ull;
-        if (tid == 0 && p.pos) *p.pos += 1;
+        if (tid == 0 && p.pos) *p.pos += p.pos_add;
     }
     if (tid == 0) *p.done = 0u;
 }
@@ -769,6 +770,146 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnParam
         }
         p.out[(size_t)t * p.nh * hd + (size_t)(g * HP + hh) * hd + d] = O / sm_L[hh];
     }
+}
+
+// --------------------------------------------------- prefill (T tokens) ----
+// Token-parallel prefill of one sequence: T prompt tokens at positions
+// pos0 .. pos0+T-1 go through each layer together.
+
+// y[t] = bf16(x[t] * rsqrt(mean(x[t]^2) + eps) * w): the GEMM operand of the
+// next projection, one CTA per token.
+__global__ void k_rmsnorm_bf16(const float *x, const uint16_t *w, float eps, __nv_bfloat16 *y, int dim) {
+    __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const size_t base = (size_t)t * dim;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) s = fmaf(x[base + i], x[base + i], s);
+    s = warp_sum(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    float ss = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) ss += red[i];
+    const float rms = rsqrtf(ss / (float)dim + eps);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x)
+        y[base + i] = __float2bfloat16_rn((x[base + i] * rms) * bf16_bits(w[i]));
+}
+
+// Per (token, head): QK-norm and RoPE of q in place, and for the KV heads
+// k (norm, RoPE) and v stored as bf16 in the cache at the token's position.
+// grid (T, nh + nkv), one warp (hd = 128, 4 dims per lane).
+__global__ void k_qk_rope_store(float *qkv, int qkv_stride, int nh, int nkv, const int *pos0p, int max_seq,
+                                const uint16_t *qn_w, const uint16_t *kn_w, float eps, float theta,
+                                uint16_t *kc, uint16_t *vc, int *err) {
+    __shared__ float rc[kHeadDim / 2], rs[kHeadDim / 2];
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x, hh = blockIdx.y, lane = threadIdx.x;
+    const int pos = *pos0p + t;
+    if (pos < 0 || pos >= max_seq) {
+        if (lane == 0 && hh == 0) atomicOr(err, kErrBadIndex);
+        return;
+    }
+    rope_table(rc, rs, pos, theta);
+    __syncwarp();
+    const int hd = kHeadDim, qd = nh * hd, kvd = nkv * hd;
+    float *row = qkv + (size_t)t * qkv_stride;
+    float v4[4];
+    if (hh < nh) {
+        load4(row + (size_t)hh * hd + 4 * lane, v4);
+        if (qn_w) head_rmsnorm(v4, qn_w, eps);
+        head_rope(v4, rc, rs);
+        *reinterpret_cast<float4 *>(row + (size_t)hh * hd + 4 * lane) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+    } else {
+        const int g = hh - nh;
+        load4(row + qd + (size_t)g * hd + 4 * lane, v4);
+        if (kn_w) head_rmsnorm(v4, kn_w, eps);
+        head_rope(v4, rc, rs);
+        const size_t at = ((size_t)g * max_seq + pos) * hd + 4 * lane;  // sequence slot 0
+        *reinterpret_cast<uint2 *>(kc + at) = pack4_bf16(v4);
+        load4(row + qd + kvd + (size_t)g * hd + 4 * lane, v4);
+        *reinterpret_cast<uint2 *>(vc + at) = pack4_bf16(v4);
+    }
+}
+
+// Causal attention of the T prompt tokens over the cache (sequence slot 0):
+// token t (position pos0 + t) attends positions 0 .. pos0 + t.  One CTA per
+// (token, q head), four warps over the positions with an online softmax,
+// merged in shared memory; bf16 output (the o-projection GEMM's operand).
+__global__ void __launch_bounds__(128) k_attn_prefill(const float *qkv, int qkv_stride, int nh, int nkv,
+                                                      const int *pos0p, int max_seq, float scale,
+                                                      const uint16_t *kc, const uint16_t *vc,
+                                                      __nv_bfloat16 *out) {
+    constexpr int P = 8, NW = 4;
+    __shared__ float sm_m[NW], sm_l[NW];
+    __shared__ __align__(16) float sm_o[NW][kHeadDim];
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x, head = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int hd = kHeadDim, g = head / (nh / nkv);
+    const int seq = max(1, min(*pos0p + t + 1, max_seq));
+    float q[4];
+    load4(qkv + (size_t)t * qkv_stride + (size_t)head * hd + 4 * lane, q);
+    const uint16_t *kb = kc + (size_t)g * max_seq * hd, *vb = vc + (size_t)g * max_seq * hd;
+    float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int pb = warp * P; pb < seq; pb += NW * P) {
+        uint2 kw[P], vw[P];
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+            const int pp = min(pb + j, seq - 1);
+            kw[j] = __ldcg(reinterpret_cast<const uint2 *>(kb + (size_t)pp * hd + 4 * lane));
+            vw[j] = __ldcg(reinterpret_cast<const uint2 *>(vb + (size_t)pp * hd + 4 * lane));
+        }
+        float acc[P];
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+            const float k0 = __uint_as_float(kw[j].x << 16), k1 = __uint_as_float(kw[j].x & 0xFFFF0000u);
+            const float k2 = __uint_as_float(kw[j].y << 16), k3 = __uint_as_float(kw[j].y & 0xFFFF0000u);
+            acc[j] = fmaf(q[3], k3, fmaf(q[2], k2, fmaf(q[1], k1, q[0] * k0)));
+        }
+        const float tot = warp_reduce_multi(acc);
+        float sc[P], mx = m;
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+            sc[j] = __shfl_sync(0xffffffffu, tot, j * (32 / P)) * scale;
+            if (pb + j >= seq) sc[j] = -INFINITY;
+            mx = fmaxf(mx, sc[j]);
+        }
+        const float corr = expf(m - mx);
+        l *= corr;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] *= corr;
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+            const float e = expf(sc[j] - mx);
+            l += e;
+            o[0] = fmaf(e, __uint_as_float(vw[j].x << 16), o[0]);
+            o[1] = fmaf(e, __uint_as_float(vw[j].x & 0xFFFF0000u), o[1]);
+            o[2] = fmaf(e, __uint_as_float(vw[j].y << 16), o[2]);
+            o[3] = fmaf(e, __uint_as_float(vw[j].y & 0xFFFF0000u), o[3]);
+        }
+        m = mx;
+    }
+    if (lane == 0) {
+        sm_m[warp] = m;
+        sm_l[warp] = l;
+    }
+    *reinterpret_cast<float4 *>(&sm_o[warp][4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
+    __syncthreads();
+    const int d = threadIdx.x;  // 128 threads, one per dimension
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        if (sm_m[w] == -INFINITY) continue;
+        const float f = expf(sm_m[w] - M);
+        L = fmaf(sm_l[w], f, L);
+        O = fmaf(sm_o[w][d], f, O);
+    }
+    out[(size_t)t * nh * hd + (size_t)head * hd + d] = __float2bfloat16_rn(O / L);
 }
 
 }  // namespace m1

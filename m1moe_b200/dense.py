@@ -130,6 +130,17 @@ class DenseModel:
                   lg.data_ptr() if lg is not None else 0, _stream(stream))
         return tok, lg
 
+    def prefill(self, moe, tokens: torch.Tensor, *, logits: torch.Tensor | None = None, stream=None):
+        """Token-parallel prefill of the prompt tokens [T] (int32, CUDA) into
+        sequence slot 0 at the current position: returns the greedy next token
+        [1] (and fills `logits` [vocab] if given); the position advances by T."""
+        T = tokens.shape[0]
+        nxt = torch.empty((1,), dtype=torch.int32, device=tokens.device)
+        _check_cuda(tokens)
+        _lib.call("m1moe_cuda_prefill_step", self._ctx, moe._ctx, tokens.data_ptr(), T, nxt.data_ptr(),
+                  logits.data_ptr() if logits is not None else 0, _stream(stream))
+        return nxt
+
     def step(self, moe, tokens: torch.Tensor, *, next_tokens: torch.Tensor | None = None,
              logits: torch.Tensor | None = None, stream=None):
         """One decode step for tokens [B] (int32, CUDA): returns the next tokens

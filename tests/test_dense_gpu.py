@@ -286,3 +286,77 @@ def test_decode_step_replays_from_a_cuda_graph(oracle_lib):
     del g
     dm.close()
     blk.close()
+
+
+def _bits_cache(dm, layers):
+    return [(_bits(dm.kv_cache(L)[0]), _bits(dm.kv_cache(L)[1])) for L in range(layers)]
+
+
+@pytest.mark.parametrize("arch", ["olmoe", "mixtral"])
+def test_prefill_step_matches_token_serial_oracle(oracle_lib, arch):
+    """Token-parallel prefill (m1moe_cuda_prefill_step) of a 6-token prompt
+    against the reference's token-serial loop (bench/main.swift:139-141: one
+    forward() per prompt token), restated by the oracle: the last token's
+    logits and greedy token, every cached k/v row, and one decode step after
+    the prompt.  The prefill's projections take bf16 operands (cuBLAS) and
+    its MoE block fp16 ones (tensor cores), both with fp32 accumulation: the
+    bar is 2e-3 of the logits' L2 norm (the decode path's 1e-3 with room for
+    the two operand roundings), and cached k/v within a few bf16 ulps."""
+    olmoe = arch == "olmoe"
+    B, layers, vocab, h, T = 1, 2, 1000, 256, 6
+    nh, nkv = (2, 2) if olmoe else (4, 2)
+    dm, blk, dense, moe = _model(71 if olmoe else 81, h=h, nh=nh, nkv=nkv, layers=layers, vocab=vocab,
+                                 qk_norm=olmoe, theta=1e4 if olmoe else 1e6, E=8, K=2, inter=128,
+                                 norm=not olmoe, B=B, max_seq=32)
+    prompt = np.array([11, 250, 3, 999, 42, 7], dtype=np.int32)
+    lg = torch.empty((vocab,), dtype=torch.float32, device="cuda")
+    nxt = dm.prefill(blk, torch.from_numpy(prompt).cuda(), logits=lg)
+    dm.synchronize()
+    blk.synchronize()
+    assert dm.position() == T
+    kv = [(np.zeros((B, nkv, 32, 128), np.uint16), np.zeros((B, nkv, 32, 128), np.uint16))
+          for _ in range(layers)]
+    for pos in range(T):
+        ref_tok, ref_lg = oracle_lib.decode_step(dense, moe, kv, [int(prompt[pos])], pos, nthreads=4)
+    got = lg.cpu().numpy()
+    assert rel_max_err(got, ref_lg[0]) < 2e-3
+    srt = np.sort(ref_lg[0])[::-1]
+    if srt[0] - srt[1] > 2e-3 * (srt[0] - srt[-1]):
+        assert int(nxt.item()) == int(ref_tok[0])
+    gpu_kv = _bits_cache(dm, layers)
+    for L in range(layers):
+        for a, b in zip(gpu_kv[L], kv[L]):
+            ga, gb = synth.bf16_to_f32(a[0, :, :T]), synth.bf16_to_f32(b[0, :, :T])
+            assert np.max(np.abs(ga - gb)) <= 2e-2 * np.abs(gb).max(), L
+    # one decode step after the prompt continues from the prefilled cache
+    lg2 = torch.empty((1, vocab), dtype=torch.float32, device="cuda")
+    t2 = dm.step(blk, nxt.clone(), logits=lg2)
+    dm.synchronize()
+    ref_tok2, ref_lg2 = oracle_lib.decode_step(dense, moe, kv, [int(nxt.item())], T, nthreads=4)
+    assert rel_max_err(lg2.cpu().numpy()[0], ref_lg2[0]) < 2e-3
+    dm.close()
+    blk.close()
+
+
+def test_prefill_step_config2_shape(oracle_lib):
+    """Config 2's shapes (h 2048, 16 heads with QK-norm, 64 experts top-8,
+    vocab 50304) with 2 layers: a 16-token prompt from position 0 against the
+    token-serial oracle (the last token's logits and greedy token)."""
+    layers, T = 2, 16
+    dm, blk, dense, moe = _model(91, h=2048, nh=16, nkv=16, layers=layers, vocab=50304, qk_norm=True,
+                                 theta=1e4, E=64, K=8, inter=1024, norm=False, B=1, max_seq=64)
+    prompt = np.random.default_rng(5).integers(0, 50304, size=T).astype(np.int32)
+    lg = torch.empty((50304,), dtype=torch.float32, device="cuda")
+    nxt = dm.prefill(blk, torch.from_numpy(prompt).cuda(), logits=lg)
+    dm.synchronize()
+    blk.synchronize()
+    kv = [(np.zeros((1, 16, 64, 128), np.uint16), np.zeros((1, 16, 64, 128), np.uint16))
+          for _ in range(layers)]
+    for pos in range(T):
+        ref_tok, ref_lg = oracle_lib.decode_step(dense, moe, kv, [int(prompt[pos])], pos, nthreads=8)
+    assert rel_max_err(lg.cpu().numpy(), ref_lg[0]) < 2e-3
+    srt = np.sort(ref_lg[0])[::-1]
+    if srt[0] - srt[1] > 2e-3 * (srt[0] - srt[-1]):
+        assert int(nxt.item()) == int(ref_tok[0])
+    dm.close()
+    blk.close()

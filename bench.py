@@ -36,7 +36,9 @@ decode_step    (1 GPU) configs 2 and 4: whole greedy decode steps (dense
            attention half + MoE blocks + LM head) through m1moe_cuda_decode_step,
            tok/s at batch 1 and 8 after the KV cache is prefilled to the
            context length; the config-2 batch-1 step is checked against the
-           oracle's decode step.
+           oracle's decode step.  Its "prefill" entry: a 512-token prompt through
+           m1moe_cuda_prefill_step (token-parallel: cuBLAS bf16 projections,
+           causal attention, tensor-core MoE), tok/s and TFLOP/s.
 prefill  = (1 GPU) config 3's prefill mode beside the decode line: one
            Mixtral-shaped layer over 512 tokens through m1moe_cuda_moe_prefill
            (tensor-core grouped GEMMs), TFLOP/s against the measured bf16 peak.
@@ -592,7 +594,8 @@ DECODE = {
 }
 
 
-def decode_step_measure(dev, name: str, batches=(1, 8), tokens: int = 128, parity: bool = False) -> dict:
+def decode_step_measure(dev, name: str, batches=(1, 8), tokens: int = 128, parity: bool = False,
+                        prompt: int = 512) -> dict:
     """Full decode steps (BASELINE configs 2 and 4) through m1moe_cuda_decode_step:
     embedding, per layer the input RMSNorm + q/k/v GEMV, QK-norm + RoPE + KV
     store + split-K attention, o_proj + residual + post-norm, the MoE block,
@@ -684,9 +687,54 @@ def decode_step_measure(dev, name: str, batches=(1, 8), tokens: int = 128, parit
             entry["parity"] = par
         res[f"b{B}"] = entry
         del graph
+    res["prefill"] = prompt_prefill_measure(dm, blk, c, seed, dev, stream, prompt)
     dm.close()
     blk.close()
     return res
+
+
+def prompt_prefill_measure(dm, blk, c, seed, dev, stream, T: int) -> dict:
+    """A T-token prompt through m1moe_cuda_prefill_step from position 0 (the
+    reference runs its prompt token by token, bench/main.swift:139-141): per
+    layer cuBLAS bf16 q|k|v and o GEMMs over all tokens, causal attention, the
+    tensor-core MoE block; the last token's LM head and greedy token.  FLOPs
+    count the projections, the attention scores and sums over the causal
+    prefix, the K routed experts of every token and the one LM-head row."""
+    import torch
+
+    hd, h, L = 128, c["h"], c["layers"]
+    qd, kvd = c["nh"] * hd, c["nkv"] * hd
+    prompt = torch.from_numpy(np.random.default_rng(seed + 9).integers(
+        0, c["vocab"], size=T).astype(np.int32)).to(dev)
+    total, n = 0.0, 5
+    for i in range(3 + n):
+        dm.set_position(0)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            dm.prefill(blk, prompt, stream=stream)
+            b.record(stream)
+        torch.cuda.synchronize()
+        if i >= 3:
+            total += a.elapsed_time(b)
+    dm.synchronize()
+    blk.synchronize()
+    assert dm.position() == T
+    ms = total / n
+    proj = 2.0 * h * (qd + 2 * kvd) + 2.0 * qd * h
+    moe = c["K"] * 6.0 * h * c["I"]
+    attn = 4.0 * qd * (T * (T + 1) / 2) / T
+    flops = L * T * (proj + moe + attn) + 2.0 * c["vocab"] * h
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak = tensor_peak()
+    return {"tokens": T, "ms": ms, "tok_s": T / (ms * 1e-3), "ms_per_token": ms / T,
+            "flops": flops, "value": tflops, "unit": "TFLOP/s", "frac": tflops / peak[0],
+            "peak_source": peak[1], "calls": n,
+            "kernels": "k_embed; per layer k_rmsnorm_bf16, cuBLAS GEMM (q|k|v), k_qk_rope_store, "
+                       "k_attn_prefill, cuBLAS GEMM (o, accumulate), k_rmsnorm, MoE prefill "
+                       "(router, gather, k_prefill_gemm gate/up + down, combine); "
+                       "k_dense_gemv (LM head + argmax)"}
 
 
 def decode_parity(dm, blk, dw, c, seed, toks, next_tok, logits) -> dict:

@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdarg>
 #include <cstdio>
@@ -25,6 +26,7 @@
 
 #include "m1moe_cuda.h"
 #include "common.cuh"
+#include "host_io.cuh"
 #include "matvec4.cuh"
 #include "moe_layer.cuh"
 #include "pipeline.cuh"
@@ -208,7 +210,11 @@ struct m1moe_cuda_ctx {
     // [out | idx | w], each laid out per call so that one copy moves them,
     // and a pinned host mirror of both
     float *hin = nullptr, *hio = nullptr;
-    void *hpin = nullptr;
+    void *hpin = nullptr;           // mapped pinned: [x | residual | out | idx | w | flag]
+    void *hpin_dev = nullptr;       // hpin as the device sees it
+    unsigned *hflag = nullptr;      // host word k_stage_out stores the sequence number to
+    unsigned *hseq_dev = nullptr;   // device copy of the last sequence number
+    unsigned host_seq = 0;          // the last sequence number the host saw
     cudaStream_t stream = nullptr;  // for the *_host calls and staging copies
     void *pinned[2] = {nullptr, nullptr};
     cudaEvent_t staged[2] = {nullptr, nullptr};
@@ -258,6 +264,9 @@ struct DeviceGuard {
     }
 };
 
+// Bytes of the host call's [out | idx | w] block, a whole number of float4s.
+size_t host_out_bytes(size_t B, size_t h, size_t K) { return (B * h * 4 + 2 * B * K * 4 + 15) & ~size_t(15); }
+
 void free_ctx(m1moe_cuda_ctx *c) {
     if (!c) return;
     cudaFree(c->table);
@@ -270,6 +279,7 @@ void free_ctx(m1moe_cuda_ctx *c) {
     cudaFree(c->staging);
     cudaFree(c->hin);
     cudaFree(c->hio);
+    cudaFree(c->hseq_dev);
     if (c->hpin) cudaFreeHost(c->hpin);
     for (void *q : {(void *)c->pf_idx, (void *)c->pf_tok_slot, (void *)c->pf_slot_tok,
                     (void *)c->pf_ntiles, (void *)c->pf_w, (void *)c->pf_ypart, (void *)c->pf_tiles,
@@ -826,15 +836,25 @@ m1moe_status m1moe_cuda_create(const m1moe_cuda_cfg *cfg, m1moe_cuda_ctx **out_c
     M1_ALLOC(c->epochs, kEpochBytes);
     M1_ALLOC(c->err, 4);
     M1_ALLOC(c->hin, 2 * B * g.hidden_dim * 4);
-    M1_ALLOC(c->hio, B * g.hidden_dim * 4 + 2 * B * K * 4);
+    M1_ALLOC(c->hio, host_out_bytes(B, g.hidden_dim, K));
+    M1_ALLOC(c->hseq_dev, 4);
 #undef M1_ALLOC
-    e = cudaHostAlloc(&c->hpin, 3 * B * g.hidden_dim * 4 + 2 * B * K * 4, cudaHostAllocDefault);
-    if (e != cudaSuccess) {
-        m1moe_status st_ = cuda_fail(e, "cudaHostAlloc host-call staging");
-        free_ctx(c);
-        return st_;
+    {
+        // [x | residual] (2·B·h floats), [out | idx | w] rounded up to 16
+        // bytes, then the flag word on its own 64 bytes
+        const size_t in_b = 2 * B * g.hidden_dim * 4, out_b = host_out_bytes(B, g.hidden_dim, K);
+        e = cudaHostAlloc(&c->hpin, in_b + out_b + 64, cudaHostAllocMapped);
+        if (e == cudaSuccess) e = cudaHostGetDevicePointer(&c->hpin_dev, c->hpin, 0);
+        if (e != cudaSuccess) {
+            m1moe_status st_ = cuda_fail(e, "cudaHostAlloc host-call staging");
+            free_ctx(c);
+            return st_;
+        }
+        c->hflag = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(c->hpin) + in_b + out_b);
+        *reinterpret_cast<volatile unsigned *>(c->hflag) = 0;
     }
     e = cudaMemset(c->err, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(c->hseq_dev, 0, 4);
     if (e == cudaSuccess) e = clear_exchange(c);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -1513,30 +1533,51 @@ m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *c, int32_t layer, const f
         return fail(M1MOE_ERR_INVALID_ARG, "batch %d outside [1,%d]", B, c->cfg.max_batch);
     DeviceGuard dg(c->cfg.device);
     const size_t n = (size_t)B * c->cfg.hidden_dim, hb = n * 4, kb = (size_t)B * c->cfg.top_k * 4;
-    // one copy each way through the pinned mirror: x and the residual in,
-    // out, indices and weights back (each host-to-device or device-to-host
-    // copy costs a few microseconds of its own on the stream)
+    // inputs and outputs pass through mapped pinned memory: k_stage_in loads
+    // [x | residual] into device memory, the layer runs, k_stage_out stores
+    // [out | idx | w] back and then a sequence number that this thread polls
     float *pin_in = static_cast<float *>(c->hpin);
-    float *pin_out = pin_in + 2 * n;
+    float *pin_out = pin_in + 2 * c->cfg.max_batch * (size_t)c->cfg.hidden_dim;
     if (!c->router_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "router of layer %d not loaded", layer);
     if (!c->layer_loaded[layer]) return fail(M1MOE_ERR_NOT_LOADED, "experts of layer %d not loaded", layer);
-    // the copies and the layer launch go out as one CUDA graph (captured on
-    // the first call of this layer, batch and residual flag), which costs one
-    // launch instead of three stream operations
+    // the three kernels go out as one CUDA graph (captured on the first call
+    // of this layer, batch and residual flag), chained by programmatic
+    // dependent launch
     const size_t key = ((size_t)layer * m1::kMaxTok + (B - 1)) * 2 + (h_res ? 1 : 0);
     if (c->host_graphs.empty()) c->host_graphs.assign((size_t)c->cfg.num_layers * m1::kMaxTok * 2, nullptr);
     if (!c->host_graphs[key]) {
         float *d_out = c->hio;
         int32_t *d_idx = reinterpret_cast<int32_t *>(d_out + n);
         float *d_w = reinterpret_cast<float *>(d_idx) + (size_t)B * c->cfg.top_k;
+        // the residual sits right after x (at n) in both the pinned and the
+        // device block, so one stage-in moves both
+        float *dev_in = static_cast<float *>(c->hpin_dev);
+        float *dev_out = dev_in + (pin_out - pin_in);
+        const int in4 = (int)((h_res ? 2 * hb : hb) / 16), out4 = (int)((hb + 2 * kb + 15) / 16);
         M1_CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-        cudaError_t e = cudaMemcpyAsync(c->hin, pin_in, h_res ? 2 * hb : hb, cudaMemcpyHostToDevice, c->stream);
+        m1::k_stage_in<<<(in4 + 255) / 256, 256, 0, c->stream>>>(reinterpret_cast<const float4 *>(dev_in),
+                                                                 reinterpret_cast<float4 *>(c->hin), in4);
+        cudaError_t e = cudaGetLastError();
         m1moe_status st = M1MOE_OK;
         if (e == cudaSuccess)
             st = m1moe_cuda_moe_layer(c, layer, c->hin, M1MOE_DTYPE_F32, h_res ? c->hin + n : nullptr,
                                       M1MOE_DTYPE_F32, d_out, M1MOE_DTYPE_F32, B, d_idx, d_w, c->stream);
-        if (e == cudaSuccess && st == M1MOE_OK)
-            e = cudaMemcpyAsync(pin_out, d_out, hb + 2 * kb, cudaMemcpyDeviceToHost, c->stream);
+        if (e == cudaSuccess && st == M1MOE_OK) {
+            cudaLaunchConfig_t lc = {};
+            lc.gridDim = dim3(1);
+            lc.blockDim = dim3(std::min(1024, std::max(32, (out4 + 31) / 32 * 32)));
+            lc.stream = c->stream;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[0].val.programmaticStreamSerializationAllowed = 1;
+            lc.attrs = at;
+            lc.numAttrs = 1;
+            e = cudaLaunchKernelEx(&lc, m1::k_stage_out, reinterpret_cast<const float4 *>(d_out),
+                                   reinterpret_cast<float4 *>(dev_out), out4, c->hseq_dev,
+                                   reinterpret_cast<unsigned *>(static_cast<uint8_t *>(c->hpin_dev) +
+                                                                (reinterpret_cast<uint8_t *>(c->hflag) -
+                                                                 static_cast<uint8_t *>(c->hpin))));
+        }
         cudaGraph_t graph = nullptr;
         const cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
         if (st != M1MOE_OK) {
@@ -1552,9 +1593,29 @@ m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *c, int32_t layer, const f
     }
     memcpy(pin_in, h_x, hb);
     if (h_res) memcpy(pin_in + n, h_res, hb);
+    const unsigned want = c->host_seq + 1;
     M1_CK(cudaGraphLaunch(c->host_graphs[key], c->stream));
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    M1_CK(cudaStreamSynchronize(c->stream));
+    g_launches.fetch_add(3, std::memory_order_relaxed);
+    // poll the flag; every 256 polls ask the stream whether it failed or
+    // finished without the flag (bounded: a minute)
+    const volatile unsigned *flag = c->hflag;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint32_t it = 1;; ++it) {
+        if (*flag == want) break;
+        if ((it & 255u) == 0) {
+            const cudaError_t q = cudaStreamQuery(c->stream);
+            if (q == cudaSuccess && *flag == want) break;
+            if (q != cudaSuccess && q != cudaErrorNotReady) return cuda_fail(q, "host-call graph");
+            if (q == cudaSuccess || std::chrono::steady_clock::now() - t0 > std::chrono::seconds(60)) {
+                cudaStreamSynchronize(c->stream);
+                c->host_seq = *flag;
+                return fail(M1MOE_ERR_DEVICE, "host call: no completion flag (sequence %u, saw %u)", want,
+                            c->host_seq);
+            }
+        }
+    }
+    c->host_seq = want;
+    std::atomic_thread_fence(std::memory_order_acquire);
     memcpy(h_out, pin_out, hb);
     if (h_idx) memcpy(h_idx, pin_out + n, kb);
     if (h_w) memcpy(h_w, reinterpret_cast<const uint8_t *>(pin_out + n) + kb, kb);

@@ -151,12 +151,16 @@ def test_forward_host_matches_device_path(golden):
     blk = _block([g["layer_00"], g["layer_01"]], routers, h=h, I=I, E=E, K=2, norm=False)
     x = synth.bf16_to_f32(synth.hidden_states(1, 4, h))
     r = synth.bf16_to_f32(synth.hidden_states(2, 4, h))
-    for layer in range(2):
-        oh, ih, wh = blk.forward_host(layer, x, r)
-        od, idd, wd = blk.forward(layer, torch.from_numpy(x).cuda(), torch.from_numpy(r).cuda(),
-                                  return_topk=True)
+    # batches below the context's maximum, with and without a residual, and
+    # repeated calls (each call's results arrive behind its own sequence number)
+    for layer, B, res in [(0, 4, True), (1, 4, True), (0, 1, False), (1, 3, True), (0, 4, False),
+                          (0, 4, True), (1, 2, False)]:
+        xb, rb = x[:B], (r[:B] if res else None)
+        oh, ih, wh = blk.forward_host(layer, xb, rb)
+        od, idd, wd = blk.forward(layer, torch.from_numpy(xb).cuda(),
+                                  torch.from_numpy(rb).cuda() if res else None, return_topk=True)
         # expert contributions are summed by atomics in no fixed order
-        assert rel_max_err(oh, od.cpu().numpy()) < 1e-6
+        assert rel_max_err(oh, od.cpu().numpy()) < 1e-6, (layer, B, res)
         assert np.array_equal(ih, idd.cpu().numpy()) and np.array_equal(wh, wd.cpu().numpy())
     blk.close()
 

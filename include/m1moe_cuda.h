@@ -283,8 +283,10 @@ M1MOE_API m1moe_status m1moe_cuda_moe_layer_ep(m1moe_cuda_ctx *ctx, int32_t laye
 /* Synchronous host-buffer form of m1moe_cuda_moe_layer with the reference's
  * f32 buffers (buf_h_mid, buf_residual -> buf_moe_out, MetalContext.swift
  * :134-152): copies in, runs, copies out and waits.  h_topk_* may be NULL.
- * The copies go through one pinned buffer of the context, so calls on one
- * context must come from one thread at a time. */
+ * The copies go through one mapped pinned buffer of the context (kernels load
+ * and store it; the calling thread polls a completion word there, and returns
+ * M1MOE_ERR_DEVICE if the stream ends or a minute passes without it), so
+ * calls on one context must come from one thread at a time. */
 M1MOE_API m1moe_status m1moe_cuda_moe_layer_host(m1moe_cuda_ctx *ctx, int32_t layer,
                                        const float *h_x, const float *h_residual,
                                        float *h_out, int32_t batch, int32_t *h_topk_idx,

@@ -124,6 +124,29 @@ def test_matvec_strided_stream_of_experts(oracle_lib, batch):
             assert rel_max_err(yc[e, t], ref) < TOL, (e, t)
 
 
+@pytest.mark.parametrize("out_dim", [1028, 1020])
+def test_matvec_stream_ragged_tiles(oracle_lib, out_dim):
+    """A stream of 12 matrices whose row count the ring's 36-row tiles do not
+    divide (1028 = 28 x 36 + 20, 1020 = 28 x 36 + 12: a short tail tile per
+    matrix): every row of every matrix."""
+    from m1moe_b200 import matvec4_strided
+    in_dim, M = 2048, 12
+    rng = np.random.default_rng(out_dim)
+    mats = [synth.quant_matrix(rng, out_dim, in_dim, 64)[:3] for _ in range(M)]
+    wb, sb = out_dim * in_dim // 2, out_dim * (in_dim // 64) * 2
+    stride = wb + 2 * sb
+    blob = np.concatenate([np.concatenate([W.view(np.uint8).ravel(), S.view(np.uint8).ravel(),
+                                           B.view(np.uint8).ravel()]) for W, S, B in mats])
+    d = torch.from_numpy(blob).cuda()
+    xb = synth.hidden_states(7, 1, in_dim)
+    xf = synth.bf16_to_f32(xb)
+    y = matvec4_strided(d, d[wb:], d[wb + sb:], stride, M, out_dim, in_dim, _x_dev(xb, torch.bfloat16))
+    yc = y.cpu().numpy()
+    for m, (W, S, B) in enumerate(mats):
+        ref = oracle_lib.matvec4bit(W, S, B, xf[0], 64, nthreads=8)
+        assert rel_max_err(yc[m, 0], ref) < TOL, m
+
+
 def test_matvec_rejects_bad_shapes():
     from m1moe_b200 import M1MoECudaError, matvec4
     w = torch.zeros((4, 12), dtype=torch.int32, device="cuda")  # in_dim 96: not % 64

@@ -1637,7 +1637,9 @@ m1moe_status m1moe_cuda_synchronize(m1moe_cuda_ctx *c) {
         // so that the next call starts from a clean state.
         M1_CK(cudaMemset(c->err, 0, 4));
         M1_CK(clear_exchange(c));
-        return fail(M1MOE_ERR_DEVICE, "device error word 0x%x (1: a bounded wait timed out)", word);
+        return fail(M1MOE_ERR_DEVICE, "device error word 0x%x (1: a bounded wait timed out; 2: an index out of "
+                                      "range; 4: a value beyond the fp16 range of the tensor-core operands)",
+                    word);
     }
     return M1MOE_OK;
 }

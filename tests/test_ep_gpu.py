@@ -28,7 +28,7 @@ TOL = 1e-3
 GAP = 1e-5
 
 SHAPES = {
-    # h, I, E, K, norm, tokens per rank, layers, calls
+    # h, I, E, K, norm, tokens per rank (at most 8 / world), layers, calls
     "small": (512, 256, 8, 2, True, 2, 2, 5),
     "mixtral": (4096, 14336, 8, 2, True, 1, 1, 2),
 }
@@ -48,6 +48,7 @@ def _worker(rank, world, port, shape, q):
     from m1moe_b200 import MoEBlock, synth
     from m1moe_b200.expert_parallel import EPFused, shard
     H, I, E, K, norm, b, layers, calls = SHAPES[shape]
+    b = min(b, 8 // world)  # the gathered batch world * b is at most 8 (kMaxTok)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     try:

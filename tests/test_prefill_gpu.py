@@ -173,3 +173,35 @@ def test_prefill_unsupported_shape_is_an_error(golden):
     with pytest.raises(M1MoECudaError, match="UNSUPPORTED"):
         blk.prefill(0, torch.zeros((4, h), device="cuda"))
     blk.close()
+
+
+def test_prefill_large_magnitudes_and_range_error(golden, oracle_lib):
+    """Tokens enter the tensor cores as fp16.  Inputs 100x larger than the
+    synthetic N(0,1) (within fp16 range, and so are the SwiGLU activations
+    here) keep the parity bar, fp16's relative precision being scale-free.
+    A token value beyond fp16's range (1e5 > 65504) is not turned into an
+    infinity: the call reports it (M1MOE_ERR_DEVICE from synchronize, the
+    error word's range bit), and the context works again afterwards."""
+    from golden.make_golden import router_weights
+    from m1moe_b200._lib import M1MoECudaError
+    g = golden("mixtral_tiny")
+    L, E, h, I, gs, seed = (int(v) for v in g["meta"])
+    router = router_weights(seed, L, E, h)[0]
+    img = g["layer_00"]
+    blk = _block([img], [router], h=h, I=I, E=E, K=2, norm=True, max_batch=8)
+    T = 40
+    xf = (synth.bf16_to_f32(synth.hidden_states(91, T, h)) * 100.0).astype(np.float32)
+    out, idx, w = blk.prefill(0, torch.from_numpy(xf).cuda(), return_topk=True)
+    blk.synchronize()
+    _check_against_oracle(oracle_lib, img, router, out.cpu().numpy(), idx.cpu().numpy(),
+                          w.cpu().numpy(), xf, None, h=h, I=I, E=E, K=2, norm=True)
+    bad = xf.copy()
+    bad[3, 17] = 1.0e5
+    blk.prefill(0, torch.from_numpy(bad).cuda())
+    with pytest.raises(M1MoECudaError) as ei:
+        blk.synchronize()
+    assert "0x4" in str(ei.value) or "range" in str(ei.value)
+    out2, idx2, w2 = blk.prefill(0, torch.from_numpy(xf).cuda(), return_topk=True)
+    blk.synchronize()
+    assert torch.equal(idx2, idx) and rel_max_err(out2.cpu().numpy(), out.cpu().numpy()) < 1e-6
+    blk.close()

@@ -300,7 +300,7 @@ M1MOE_API m1moe_status m1moe_cuda_synchronize(m1moe_cuda_ctx *ctx);
 M1MOE_API int64_t m1moe_cuda_launch_count(void);
 
 /* Phase tracing (the reference only has wall-clock timing, bench/main.swift
- * :51-54).  With a non-NULL device buffer of 160 x 24 uint64, every MoE call
+ * :51-54).  With a non-NULL device buffer of 160 x 32 uint64, every MoE call
  * made afterwards records, per CTA (first 160), the SM cycle counter at each
  * phase event (slots 0-13, 16-19, 22, 23) and the global nanosecond timer at
  * events 0 and 10 (slots 20 and 21); NULL turns tracing off (the default).
@@ -311,7 +311,10 @@ M1MOE_API int64_t m1moe_cuda_launch_count(void);
  * 10 end, 11 producer issued its first tile, 12 every logit seen, 13 ranks
  * counted, 16 producer's geometry done, 17 gate/up items done, 18 first down
  * item started, 19 producer saw the routing, 22 first and 23 last down tile
- * seen landed.  Slots 14 and 15 hold values, not times: the CTA's gate/up
+ * seen landed; expert parallel calls add 24 this rank's tokens pushed (CTAs
+ * 0..world-1), 25 every rank's tokens seen, 26 every CTA's sums seen (the
+ * grid arrival), 27 this CTA's slices sent to the peers, 28 the peers'
+ * slices of this rank's tokens seen.  Slots 14 and 15 hold values, not times: the CTA's gate/up
  * row range (first | end << 32) and its tile counts (gate/up | down << 32). */
 M1MOE_API m1moe_status m1moe_cuda_set_trace(m1moe_cuda_ctx *ctx, uint64_t *d_trace);
 

@@ -1152,8 +1152,10 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             // store of the flag (release is cumulative): one system-scope
             // release instead of a system fence in every thread
             __syncthreads();
-            if (tid == 0)
+            if (tid == 0) {
                 st_release_sys_u32(reinterpret_cast<unsigned *>(p.ep_base[o]) + p.ep_rank * 32, ep_tag);
+                trace_event(p.trace, 0, 24);
+            }
         }
         // every rank's tokens have arrived
         if (tid < p.ep_world) {
@@ -1170,6 +1172,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
             if (!ok) set_abort(ctl, p.err);
         }
         __syncthreads();
+        if (tid == 0) trace_event(p.trace, 0, 25);
         X = reinterpret_cast<const float *>(mine + el.xs_off) + (size_t)ep_par * p.ep_world * nb * h;
         Xbf16 = 0;
     }
@@ -1860,6 +1863,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                         nap = min(nap * 2, 64u);
                     }
                     if (!ok && !*vabort) set_abort(ctl, p.err);
+                    trace_event(p.trace, 0, 26);
                 }
                 named_sync(1, kConsumerThreads);
                 const int sr = i1 - i0;
@@ -1874,6 +1878,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                     }
                 }
                 named_sync(1, kConsumerThreads);  // then the release stores below
+                if (tid == 0) trace_event(p.trace, 0, 27);
                 if (tid < W && tid != me && !ctl.abort)
                     st_release_sys_u32(reinterpret_cast<unsigned *>(p.ep_base[tid] + el.sf_off) + (size_t)me * kMaxCtas + blk,
                                        ep_tag);
@@ -1891,6 +1896,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                     if (!ok) set_abort(ctl, p.err);
                 }
                 named_sync(1, kConsumerThreads);
+                if (tid == 0) trace_event(p.trace, 0, 28);
                 const float *rv = reinterpret_cast<const float *>(mine + el.recv_off) + (size_t)ep_par * W * nb * h;
                 for (int q = tid; q < nb * sr; q += kConsumerThreads) {
                     const int t = q / sr, i = i0 + (q - t * sr);

@@ -104,7 +104,7 @@ __device__ __forceinline__ void pdl_trigger() {
 // timer at events 0 and 10, which places each CTA on a common time axis and
 // gives the cycle length (off by default; m1moe_cuda_set_trace).
 constexpr int kTraceEvents = 20;
-constexpr int kTraceSlots = 24;
+constexpr int kTraceSlots = 32;
 constexpr int kTraceCtas = 160;
 __device__ __forceinline__ void trace_event(unsigned long long *trace, int kernel, int event) {
     if (trace == nullptr || blockIdx.x >= kTraceCtas) return;

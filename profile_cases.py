@@ -6,6 +6,7 @@
     python profile_cases.py prefill mixtral 512  # k_prefill_gemm, 512 tokens
     python profile_cases.py decode olmoe 1    # whole decode steps, config-2 shapes, 2 layers
     python profile_cases.py trace olmoe 1     # k_moe_layer phase trace summary (no profiler)
+    torchrun --nproc-per-node 2 profile_cases.py trace_ep olmoe   # the expert-parallel kernel's trace
 
 Each case builds synthetic weights (m1moe_b200.synth), runs the kernel a few
 times and exits 0; the device footprint stays at a few GB so that a profiler
@@ -13,6 +14,7 @@ capture of one launch ends quickly.  Intended for `ncu -k ... -s ... -c 1`.
 """
 from __future__ import annotations
 
+import os
 import sys
 
 
@@ -165,7 +167,7 @@ def trace_case(workload: str, batch: int, layers: int = 4, calls: int = 20) -> N
         blk.load_router(layer, synth.router_weights(100 + layer, e, h))
     x = torch.randn(batch, h, device="cuda")
     out = torch.empty(batch, h, device="cuda")
-    trace = torch.zeros((160, 24), dtype=torch.int64, device="cuda")
+    trace = torch.zeros((160, 32), dtype=torch.int64, device="cuda")
     names = {0: "start", 1: "out rows init", 2: "logits published", 12: "all logits seen",
              13: "ranks counted", 3: "top-K ranked", 19: "producer saw routing",
              16: "geometry", 11: "first tile issued", 4: "consumers released", 5: "first tile landed",
@@ -214,6 +216,87 @@ def trace_case(workload: str, batch: int, layers: int = 4, calls: int = 20) -> N
     blk.close()
 
 
+TRACE_NAMES = {0: "start", 1: "out rows init", 2: "logits published", 12: "all logits seen",
+               13: "ranks counted", 3: "top-K ranked", 19: "producer saw routing",
+               16: "geometry", 11: "first tile issued", 4: "consumers released",
+               5: "first tile landed", 9: "all tiles issued", 17: "gate/up done",
+               6: "activations quantised", 18: "first down item", 22: "first down tile",
+               23: "last down tile", 7: "epochs seen", 8: "down items done", 10: "end",
+               24: "ep: own tokens pushed", 25: "ep: every rank's tokens seen",
+               26: "ep: every CTA's sums seen", 27: "ep: slices sent", 28: "ep: peers' slices seen"}
+
+
+def trace_ep_case(workload: str, layers: int = 2, calls: int = 20) -> None:
+    """Phase trace of the expert-parallel layer kernel (m1moe_cuda_moe_layer_ep)
+    on every rank of a torchrun job, one token per rank; rank 0 prints, per
+    event, the median over CTAs and calls of its time after the call's first
+    CTA start on that rank (us), and each rank's median call span."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from m1moe_b200 import MoEBlock, _lib, synth
+    from m1moe_b200.expert_parallel import EPFused, shard
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo")
+    if workload == "olmoe":
+        h, inter, e, k, norm = 2048, 1024, 64, 8, False
+    else:
+        h, inter, e, k, norm = 4096, 14336, 8, 2, True
+    e0, ne = shard(e, world, rank)
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=inter, num_experts=e, top_k=k, num_layers=layers,
+                   max_batch=8, norm_topk_prob=norm, device=rank, expert_begin=e0, expert_count=ne)
+    for layer in range(layers):
+        img = synth.layer_image_device(e, h, inter, 64, seed=layer, device="cuda")
+        blk.load_expert_layer(layer, img)
+        del img
+        blk.load_router(layer, synth.router_weights(100 + layer, e, h))
+    ep = EPFused(blk, 1)
+    x = torch.randn(1, h, device="cuda")
+    trace = torch.zeros((160, 32), dtype=torch.int64, device="cuda")
+    rows = {ev: [] for ev in TRACE_NAMES}
+    spans = []
+    for it in range(calls + 3):
+        for layer in range(layers):
+            rec = it >= 3 and layer == layers - 1
+            _lib.call("m1moe_cuda_set_trace", blk._ctx, trace.data_ptr() if rec else 0)
+            ep(layer, x, x, out=x)
+            if rec:
+                torch.cuda.synchronize()
+                t = trace.cpu().numpy().astype(np.int64)
+                G = 148
+                ns0, ns1 = t[:G, 20], t[:G, 21]
+                c0, c1 = t[:G, 0], t[:G, 10]
+                scale = (ns1 - ns0) / np.maximum(c1 - c0, 1)
+                t0 = ns0.min()
+                for ev in TRACE_NAMES:
+                    vals = ns0 + (t[:G, ev] - c0) * scale - t0
+                    ok = t[:G, ev] != 0
+                    if ok.any():
+                        rows[ev].append(np.median(vals[ok]) / 1e3)
+                spans.append((ns1.max() - t0) / 1e3)
+                trace.zero_()
+    _lib.call("m1moe_cuda_set_trace", blk._ctx, 0)
+    blk.synchronize()
+    med = {ev: float(np.median(v)) for ev, v in rows.items() if v}
+    allspans = [None] * world
+    dist.all_gather_object(allspans, float(np.median(spans)))
+    if rank == 0:
+        print(f"expert-parallel k_moe_layer trace: {workload}, {world} ranks, 1 token per rank, "
+              f"rank 0, median over CTAs and {calls} calls")
+        print("| event | us after the call's first CTA start |")
+        print("|---|---|")
+        for ev in sorted(med, key=med.get):
+            print(f"| {TRACE_NAMES[ev]} | {med[ev]:.2f} |")
+        print("\nmedian call span (first CTA start to last CTA end) per rank, us: " +
+              ", ".join(f"{v:.1f}" for v in allspans))
+    dist.barrier()
+    blk.close()
+    dist.destroy_process_group()
+
+
 def main(argv: list[str]) -> None:
     if len(argv) >= 1 and argv[0] == "layer":
         layer_case(argv[1] if len(argv) > 1 else "olmoe", int(argv[2]) if len(argv) > 2 else 1)
@@ -221,6 +304,8 @@ def main(argv: list[str]) -> None:
         prefill_case(argv[1] if len(argv) > 1 else "mixtral", int(argv[2]) if len(argv) > 2 else 512)
     elif len(argv) >= 1 and argv[0] == "decode":
         decode_case(argv[1] if len(argv) > 1 else "olmoe", int(argv[2]) if len(argv) > 2 else 1)
+    elif len(argv) >= 1 and argv[0] == "trace_ep":
+        trace_ep_case(argv[1] if len(argv) > 1 else "olmoe")
     elif len(argv) >= 1 and argv[0] == "trace":
         trace_case(argv[1] if len(argv) > 1 else "olmoe", int(argv[2]) if len(argv) > 2 else 1)
     elif len(argv) >= 1 and argv[0] == "matvec":

@@ -79,24 +79,23 @@ constexpr int kMaxRanks = 8;      // expert-parallel ranks joined over peer memo
 //   [0]                   x-ready flags, one 128-byte line per source rank
 //   [world*128]           done flags, one 128-byte line per source rank
 //   [2*world*128]         the call counter (one line)
-//   [sf_off]              slice flags, u32 [world][kMaxCtas]
 //   [xs_off]              gathered x, f32 [2][world*b][h] (by call parity)
 //   [rt_off]              gathered routing: idx int32 [2][world*b][kMaxTopK], then
 //                         weights f32 [2][world*b][kMaxTopK]
-//   [recv_off]            partial sums received, f32 [2][world][b][h]
+//   [recv_off]            partial sums received, tagged words {call tag, f32}
+//                         [2][world][b][h]: each value carries its call's tag, so
+//                         a receiver polls the values themselves (no flag, no
+//                         system-scope fence on the sender's side)
 struct EpLayout {
-    long long sf_off, xs_off, rt_off, recv_off, bytes;
+    long long xs_off, rt_off, recv_off, bytes;
 };
 
 __host__ __device__ inline EpLayout ep_layout(int world, int b, int h) {
     EpLayout l;
-    // [sf_off] slice flags u32 [world][kMaxCtas]: source rank r's CTA c has
-    // written its slice of this rank's tokens' partial sums
-    l.sf_off = (2LL * world + 1) * 128;
-    l.xs_off = l.sf_off + (long long)world * kMaxCtas * 4;
+    l.xs_off = (2LL * world + 1) * 128;
     l.rt_off = l.xs_off + 2LL * world * b * h * 4;
     l.recv_off = l.rt_off + 2LL * 2 * world * b * 16 * 4;
-    l.bytes = l.recv_off + 2LL * world * b * h * 4;
+    l.bytes = l.recv_off + 2LL * world * b * h * 8;
     return l;
 }
 
@@ -288,6 +287,16 @@ __device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p) {
 
 __device__ __forceinline__ void st_release_sys_u32(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long tagged(unsigned tag, uint32_t payload) {
@@ -1848,9 +1857,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                 // expert parallel, spread over every CTA: once all CTAs' sums
                 // are in the accumulator (a grid-wide arrival count: the
                 // launch is cooperative), CTA c sends each peer its slice
-                // [i0, i1) of h for that peer's tokens and raises one flag
-                // there, waits for its slice of this rank's tokens from every
-                // peer, and writes residual + the ranks' sums in rank order
+                // [i0, i1) of h for that peer's tokens as tagged words {call
+                // tag, value} (one 8-byte store each: no flag, no fence),
+                // polls (bounded) its slice of this rank's tokens from every
+                // peer until the words carry this call's tag, and writes
+                // residual + the ranks' sums in rank order
                 const EpLayout el = ep_layout(p.ep_world, p.ep_b, h);
                 const int W = p.ep_world, nb = p.ep_b, me = p.ep_rank;
                 uint8_t *mine = p.ep_base[me];
@@ -1872,43 +1883,47 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
                         const int o = q / (nb * sr);
                         if (o == me) continue;
                         const int rem = q - o * nb * sr, t = rem / sr, i = i0 + (rem - t * sr);
-                        float *rv = reinterpret_cast<float *>(p.ep_base[o] + el.recv_off) +
-                                    ((size_t)ep_par * W + me) * nb * h;
-                        rv[(size_t)t * h + i] = __ldcg(p.acc + ((size_t)o * nb + t) * h + i);
+                        unsigned long long *rv = reinterpret_cast<unsigned long long *>(p.ep_base[o] + el.recv_off) +
+                                                 ((size_t)ep_par * W + me) * nb * h;
+                        st_relaxed_sys_u64(rv + (size_t)t * h + i,
+                                           tagged(ep_tag, __float_as_uint(__ldcg(p.acc + ((size_t)o * nb + t) * h + i))));
                     }
                 }
-                named_sync(1, kConsumerThreads);  // then the release stores below
                 if (tid == 0) trace_event(p.trace, 0, 27);
-                if (tid < W && tid != me && !ctl.abort)
-                    st_release_sys_u32(reinterpret_cast<unsigned *>(p.ep_base[tid] + el.sf_off) + (size_t)me * kMaxCtas + blk,
-                                       ep_tag);
-                if (tid < W && tid != me && !ctl.abort) {
-                    const unsigned *fl = reinterpret_cast<const unsigned *>(mine + el.sf_off) + (size_t)tid * kMaxCtas + blk;
-                    bool ok = false;
-                    for (uint32_t it = 0, nap = 32; it < p.ep_wait_limit; ++it) {
-                        if (ld_acquire_sys_u32(fl) == ep_tag) {
-                            ok = true;
-                            break;
-                        }
-                        __nanosleep(nap);
-                        nap = min(nap * 2, 64u);
-                    }
-                    if (!ok) set_abort(ctl, p.err);
-                }
-                named_sync(1, kConsumerThreads);
-                if (tid == 0) trace_event(p.trace, 0, 28);
-                const float *rv = reinterpret_cast<const float *>(mine + el.recv_off) + (size_t)ep_par * W * nb * h;
-                for (int q = tid; q < nb * sr; q += kConsumerThreads) {
+                const unsigned long long *rv =
+                    reinterpret_cast<const unsigned long long *>(mine + el.recv_off) + (size_t)ep_par * W * nb * h;
+                bool got = ctl.abort == 0;
+                for (int q = tid; got && q < nb * sr; q += kConsumerThreads) {
                     const int t = q / sr, i = i0 + (q - t * sr);
                     const size_t oi = (size_t)t * h + i;
                     float v = p.res ? load_act(p.res, p.res_bf16, oi) : 0.f;
-                    for (int o = 0; o < W; ++o)
-                        v += o == me ? __ldcg(p.acc + (size_t)me * nb * h + oi) : __ldcv(rv + (size_t)o * nb * h + oi);
+                    for (int o = 0; got && o < W; ++o) {
+                        if (o == me) {
+                            v += __ldcg(p.acc + (size_t)me * nb * h + oi);
+                            continue;
+                        }
+                        unsigned long long wd = 0;
+                        for (uint32_t it = 0, nap = 32;; ++it) {
+                            wd = ld_relaxed_sys_u64(rv + (size_t)o * nb * h + oi);
+                            if ((unsigned)(wd >> 32) == ep_tag) break;
+                            if (it >= p.ep_wait_limit || *vabort) {
+                                got = false;
+                                break;
+                            }
+                            __nanosleep(nap);
+                            nap = min(nap * 2, 64u);
+                        }
+                        v += __uint_as_float((unsigned)wd);
+                    }
+                    if (!got) break;
                     if (p.out_bf16)
                         reinterpret_cast<__nv_bfloat16 *>(p.out)[oi] = __float2bfloat16_rn(v);
                     else
                         reinterpret_cast<float *>(p.out)[oi] = v;
                 }
+                if (!got && !*vabort) set_abort(ctl, p.err);
+                named_sync(1, kConsumerThreads);
+                if (tid == 0) trace_event(p.trace, 0, 28);
                 // the last CTA through resets the counts and advances the
                 // region's call counter, which names the next call
                 named_sync(1, kConsumerThreads);

@@ -639,6 +639,8 @@ m1moe_status m1moe_cuda_prefill_step(m1moe_dense_ctx *c, m1moe_cuda_ctx *moe, co
     if (m1moe_status st = m1abi::moe_compatible(moe, g.hidden_dim, g.num_layers, 1, g.device)) return st;
     DevGuard dg(g.device);
     if (m1moe_status st = pf_dense_reserve(c, T)) return st;
+    D_CK(cudaFuncSetAttribute(m1::k_attn_prefill_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)m1::attn_prefill_smem()));
     cudaStream_t st = as_stream(stream);
     const int h = g.hidden_dim, hd = c->hd;
     const size_t cache_layer = (size_t)g.max_batch * g.num_kv_heads * g.max_seq * hd;
@@ -665,9 +667,11 @@ m1moe_status m1moe_cuda_prefill_step(m1moe_dense_ctx *c, m1moe_cuda_ctx *moe, co
                                         (int)g.num_kv_heads, (const int *)c->pos, (int)g.max_seq, qn, kn,
                                         (float)g.rms_norm_eps, (float)g.rope_theta, kc, vc, c->err))
             return s;
-        if (m1moe_status s = launch_pdl(m1::k_attn_prefill, dim3(T, g.num_heads), dim3(128), 0, st,
-                                        "k_attn_prefill launch", (const float *)c->pf_qkv, c->qkv_rows,
-                                        (int)g.num_heads, (int)g.num_kv_heads, (const int *)c->pos, (int)g.max_seq,
+        if (m1moe_status s = launch_pdl(m1::k_attn_prefill_tiled,
+                                        dim3((T + m1::kPfQ - 1) / m1::kPfQ, g.num_heads), dim3(256),
+                                        m1::attn_prefill_smem(), st, "k_attn_prefill_tiled launch",
+                                        (const float *)c->pf_qkv, c->qkv_rows, (int)g.num_heads,
+                                        (int)g.num_kv_heads, (int)T, (const int *)c->pos, (int)g.max_seq,
                                         1.0f / sqrtf((float)hd), (const uint16_t *)kc, (const uint16_t *)vc,
                                         c->pf_attn))
             return s;

@@ -833,83 +833,147 @@ __global__ void k_qk_rope_store(float *qkv, int qkv_stride, int nh, int nkv, con
     }
 }
 
-// Causal attention of the T prompt tokens over the cache (sequence slot 0):
-// token t (position pos0 + t) attends positions 0 .. pos0 + t.  One CTA per
-// (token, q head), four warps over the positions with an online softmax,
-// merged in shared memory; bf16 output (the o-projection GEMM's operand).
-__global__ void __launch_bounds__(128) k_attn_prefill(const float *qkv, int qkv_stride, int nh, int nkv,
-                                                      const int *pos0p, int max_seq, float scale,
-                                                      const uint16_t *kc, const uint16_t *vc,
-                                                      __nv_bfloat16 *out) {
-    constexpr int P = 8, NW = 4;
-    __shared__ float sm_m[NW], sm_l[NW];
-    __shared__ __align__(16) float sm_o[NW][kHeadDim];
+// Tiled causal attention for a prompt (token-parallel prefill): one CTA per
+// (block of kPfQ consecutive tokens, q head), 8 warps of kPfQ / 8 tokens each.
+// The block's K and V rows come into shared memory once per tile of kPfKT
+// positions and serve all its tokens (a per-token kernel reads a token's whole
+// causal prefix from L2 on its own: ~1 GB per layer for 512 tokens).  Scores:
+// lane j takes positions j and j + 32 of the tile for the warp's tokens (K rows
+// padded by one word, so the lanes' rows fall in different banks; the tokens'
+// q rows are broadcast from shared memory).  Online softmax per token in fp32;
+// P.V with lane = 4 dimensions.  Token t (position pos0 + t) attends positions
+// 0 .. pos0 + t; bf16 output (the o-projection GEMM's operand).
+constexpr int kPfQ = 32, kPfKT = 64, kPfQW = kPfQ / 8;
+static_assert(kPfQW == 4, "P.V reads one float4 of probabilities per position");
+constexpr int kPfKRow = kHeadDim / 2 + 1;  // words per padded K row
+__host__ __device__ constexpr size_t attn_prefill_smem() {
+    return (size_t)kPfQ * kHeadDim * 4 + (size_t)kPfKT * kPfKRow * 4 + (size_t)kPfKT * kHeadDim * 2 +
+           (size_t)8 * kPfKT * kPfQW * 4;
+}
+__global__ void __launch_bounds__(256) k_attn_prefill_tiled(const float *qkv, int qkv_stride, int nh, int nkv,
+                                                            int T, const int *pos0p, int max_seq, float scale,
+                                                            const uint16_t *kc, const uint16_t *vc,
+                                                            __nv_bfloat16 *out) {
+    extern __shared__ __align__(16) uint8_t pf_att_smem[];
+    float *sq = reinterpret_cast<float *>(pf_att_smem);                       // [kPfQ][hd]
+    uint32_t *sk = reinterpret_cast<uint32_t *>(sq + kPfQ * kHeadDim);         // [kPfKT][kPfKRow]
+    uint32_t *sv = sk + kPfKT * kPfKRow;                                        // [kPfKT][hd/2]
+    float *sp = reinterpret_cast<float *>(sv + kPfKT * (kHeadDim / 2));         // [8][kPfKT][kPfQW]
     pdl_trigger();
     pdl_wait();
-    const int t = blockIdx.x, head = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int hd = kHeadDim, g = head / (nh / nkv);
-    const int seq = max(1, min(*pos0p + t + 1, max_seq));
-    float q[4];
-    load4(qkv + (size_t)t * qkv_stride + (size_t)head * hd + 4 * lane, q);
-    const uint16_t *kb = kc + (size_t)g * max_seq * hd, *vb = vc + (size_t)g * max_seq * hd;
-    float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int pb = warp * P; pb < seq; pb += NW * P) {
-        uint2 kw[P], vw[P];
-#pragma unroll
-        for (int j = 0; j < P; ++j) {
-            const int pp = min(pb + j, seq - 1);
-            kw[j] = __ldcg(reinterpret_cast<const uint2 *>(kb + (size_t)pp * hd + 4 * lane));
-            vw[j] = __ldcg(reinterpret_cast<const uint2 *>(vb + (size_t)pp * hd + 4 * lane));
-        }
-        float acc[P];
-#pragma unroll
-        for (int j = 0; j < P; ++j) {
-            const float k0 = __uint_as_float(kw[j].x << 16), k1 = __uint_as_float(kw[j].x & 0xFFFF0000u);
-            const float k2 = __uint_as_float(kw[j].y << 16), k3 = __uint_as_float(kw[j].y & 0xFFFF0000u);
-            acc[j] = fmaf(q[3], k3, fmaf(q[2], k2, fmaf(q[1], k1, q[0] * k0)));
-        }
-        const float tot = warp_reduce_multi(acc);
-        float sc[P], mx = m;
-#pragma unroll
-        for (int j = 0; j < P; ++j) {
-            sc[j] = __shfl_sync(0xffffffffu, tot, j * (32 / P)) * scale;
-            if (pb + j >= seq) sc[j] = -INFINITY;
-            mx = fmaxf(mx, sc[j]);
-        }
-        const float corr = expf(m - mx);
-        l *= corr;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] *= corr;
-#pragma unroll
-        for (int j = 0; j < P; ++j) {
-            const float e = expf(sc[j] - mx);
-            l += e;
-            o[0] = fmaf(e, __uint_as_float(vw[j].x << 16), o[0]);
-            o[1] = fmaf(e, __uint_as_float(vw[j].x & 0xFFFF0000u), o[1]);
-            o[2] = fmaf(e, __uint_as_float(vw[j].y << 16), o[2]);
-            o[3] = fmaf(e, __uint_as_float(vw[j].y & 0xFFFF0000u), o[3]);
-        }
-        m = mx;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int t0 = blockIdx.x * kPfQ, head = blockIdx.y, g = head / (nh / nkv);
+    const int pos0 = *pos0p;
+    const int tlast = min(T, t0 + kPfQ) - 1;
+    const int kmax = max(1, min(pos0 + tlast + 1, max_seq));  // positions the block reads
+    // the block's q rows (rows past T are zero)
+    for (int i = tid; i < kPfQ * kHeadDim / 4; i += 256) {
+        const int r = i / (kHeadDim / 4), c4 = i - r * (kHeadDim / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t0 + r < T)
+            v = *reinterpret_cast<const float4 *>(qkv + (size_t)(t0 + r) * qkv_stride + (size_t)head * kHeadDim + 4 * c4);
+        *reinterpret_cast<float4 *>(sq + r * kHeadDim + 4 * c4) = v;
     }
-    if (lane == 0) {
-        sm_m[warp] = m;
-        sm_l[warp] = l;
-    }
-    *reinterpret_cast<float4 *>(&sm_o[warp][4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
-    __syncthreads();
-    const int d = threadIdx.x;  // 128 threads, one per dimension
-    float M = -INFINITY;
+    const uint16_t *kb = kc + (size_t)g * max_seq * kHeadDim, *vb = vc + (size_t)g * max_seq * kHeadDim;
+    int seq[kPfQW];  // positions each of the warp's tokens attends
+    float m[kPfQW], l[kPfQW], o[kPfQW][4];
 #pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w]);
-    float L = 0.f, O = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-        if (sm_m[w] == -INFINITY) continue;
-        const float f = expf(sm_m[w] - M);
-        L = fmaf(sm_l[w], f, L);
-        O = fmaf(sm_o[w][d], f, O);
+    for (int qi = 0; qi < kPfQW; ++qi) {
+        const int t = t0 + warp * kPfQW + qi;
+        seq[qi] = t < T ? max(1, min(pos0 + t + 1, max_seq)) : 0;
+        m[qi] = -INFINITY;
+        l[qi] = 0.f;
+        o[qi][0] = o[qi][1] = o[qi][2] = o[qi][3] = 0.f;
     }
-    out[(size_t)t * nh * hd + (size_t)head * hd + d] = __float2bfloat16_rn(O / L);
+    float *spw = sp + warp * kPfKT * kPfQW;
+    for (int k0 = 0; k0 < kmax; k0 += kPfKT) {
+        __syncthreads();  // the previous tile is consumed (and sq is written, first time)
+        for (int i = tid; i < kPfKT * (kHeadDim / 8); i += 256) {
+            const int r = i / (kHeadDim / 8), c8 = i - r * (kHeadDim / 8);
+            const int pp = min(k0 + r, kmax - 1);  // rows past the block's range repeat the last one
+            const uint4 kw = __ldcg(reinterpret_cast<const uint4 *>(kb + (size_t)pp * kHeadDim) + c8);
+            const uint4 vw = __ldcg(reinterpret_cast<const uint4 *>(vb + (size_t)pp * kHeadDim) + c8);
+            uint32_t *kr = sk + r * kPfKRow + 4 * c8;
+            kr[0] = kw.x;
+            kr[1] = kw.y;
+            kr[2] = kw.z;
+            kr[3] = kw.w;
+            *reinterpret_cast<uint4 *>(sv + r * (kHeadDim / 2) + 4 * c8) = vw;
+        }
+        __syncthreads();
+        // scores of positions k0 + lane and k0 + lane + 32 for the warp's tokens
+        float s[kPfQW][2];
+#pragma unroll
+        for (int qi = 0; qi < kPfQW; ++qi) s[qi][0] = s[qi][1] = 0.f;
+        const uint32_t *k_a = sk + lane * kPfKRow, *k_b = sk + (lane + 32) * kPfKRow;
+        const float *qw = sq + warp * kPfQW * kHeadDim;
+#pragma unroll 4
+        for (int d2 = 0; d2 < kHeadDim / 2; ++d2) {
+            const uint32_t ka = k_a[d2], kbw = k_b[d2];
+            const float a0 = __uint_as_float(ka << 16), a1 = __uint_as_float(ka & 0xFFFF0000u);
+            const float b0 = __uint_as_float(kbw << 16), b1 = __uint_as_float(kbw & 0xFFFF0000u);
+#pragma unroll
+            for (int qi = 0; qi < kPfQW; ++qi) {
+                const float2 qv = *reinterpret_cast<const float2 *>(qw + qi * kHeadDim + 2 * d2);
+                s[qi][0] = fmaf(qv.y, a1, fmaf(qv.x, a0, s[qi][0]));
+                s[qi][1] = fmaf(qv.y, b1, fmaf(qv.x, b0, s[qi][1]));
+            }
+        }
+        // online softmax per token; the probabilities go to shared memory as
+        // [position][token] so that P.V reads one float4 per position
+#pragma unroll
+        for (int qi = 0; qi < kPfQW; ++qi) {
+            const float sa = (k0 + lane < seq[qi]) ? s[qi][0] * scale : -INFINITY;
+            const float sb = (k0 + lane + 32 < seq[qi]) ? s[qi][1] * scale : -INFINITY;
+            float mx = fmaxf(sa, sb);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(m[qi], mx);
+            float pa = 0.f, pb = 0.f, corr = 1.f;
+            if (mn != -INFINITY) {
+                pa = expf(sa - mn);
+                pb = expf(sb - mn);
+                corr = expf(m[qi] - mn);
+            }
+            float ps = pa + pb;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            l[qi] = l[qi] * corr + ps;
+            m[qi] = mn;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[qi][i] *= corr;
+            spw[lane * kPfQW + qi] = pa;
+            spw[(lane + 32) * kPfQW + qi] = pb;
+        }
+        __syncwarp();
+        const int jn = min(kPfKT, kmax - k0);
+        for (int j = 0; j < jn; ++j) {
+            const uint2 vw = *reinterpret_cast<const uint2 *>(sv + j * (kHeadDim / 2) + 2 * lane);
+            const float v0 = __uint_as_float(vw.x << 16), v1 = __uint_as_float(vw.x & 0xFFFF0000u);
+            const float v2 = __uint_as_float(vw.y << 16), v3 = __uint_as_float(vw.y & 0xFFFF0000u);
+            const float4 pj = *reinterpret_cast<const float4 *>(spw + j * kPfQW);
+            const float pq[4] = {pj.x, pj.y, pj.z, pj.w};
+#pragma unroll
+            for (int qi = 0; qi < kPfQW; ++qi) {
+                o[qi][0] = fmaf(pq[qi], v0, o[qi][0]);
+                o[qi][1] = fmaf(pq[qi], v1, o[qi][1]);
+                o[qi][2] = fmaf(pq[qi], v2, o[qi][2]);
+                o[qi][3] = fmaf(pq[qi], v3, o[qi][3]);
+            }
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (int qi = 0; qi < kPfQW; ++qi) {
+        const int t = t0 + warp * kPfQW + qi;
+        if (t < T) {
+            const float inv = 1.0f / l[qi];
+            const float v[4] = {o[qi][0] * inv, o[qi][1] * inv, o[qi][2] * inv, o[qi][3] * inv};
+            *reinterpret_cast<uint2 *>(out + (size_t)t * nh * kHeadDim + (size_t)head * kHeadDim + 4 * lane) =
+                pack4_bf16(v);
+        }
+    }
 }
+
 
 }  // namespace m1

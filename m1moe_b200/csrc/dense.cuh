@@ -862,7 +862,8 @@ __global__ void __launch_bounds__(256) k_attn_prefill_tiled(const float *qkv, in
     pdl_trigger();
     pdl_wait();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int t0 = blockIdx.x * kPfQ, head = blockIdx.y, g = head / (nh / nkv);
+    // the last blocks attend the longest prefixes: they start first
+    const int t0 = (gridDim.x - 1 - blockIdx.x) * kPfQ, head = blockIdx.y, g = head / (nh / nkv);
     const int pos0 = *pos0p;
     const int tlast = min(T, t0 + kPfQ) - 1;
     const int kmax = max(1, min(pos0 + tlast + 1, max_seq));  // positions the block reads

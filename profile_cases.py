@@ -5,6 +5,7 @@
     python profile_cases.py matvec 1          # k_matvec4_ring over 2048 matrices
     python profile_cases.py prefill mixtral 512  # k_prefill_gemm, 512 tokens
     python profile_cases.py decode olmoe 1    # whole decode steps, config-2 shapes, 2 layers
+    python profile_cases.py prefill_step olmoe 512   # token-parallel prompt prefill, 2 layers
     python profile_cases.py trace olmoe 1     # k_moe_layer phase trace summary (no profiler)
     torchrun --nproc-per-node 2 profile_cases.py trace_ep olmoe   # the expert-parallel kernel's trace
 
@@ -133,6 +134,44 @@ def decode_case(workload: str, batch: int, layers: int = 2, steps: int = 4) -> N
     tok = torch.arange(batch, dtype=torch.int32, device=dev)
     for _ in range(steps):
         tok = dm.step(blk, tok).clone()
+    torch.cuda.synchronize()
+    dm.synchronize()
+    blk.synchronize()
+    dm.close()
+    blk.close()
+    print("ok")
+
+
+def prefill_step_case(workload: str, tokens: int, layers: int = 2) -> None:
+    """A prompt of `tokens` tokens through m1moe_cuda_prefill_step (token-parallel
+    dense prefill) at config 2 or 4 shapes with `layers` layers, twice: for a
+    launch list of every kernel of the call."""
+    import torch
+
+    from m1moe_b200 import MoEBlock, synth
+    from m1moe_b200.dense import DenseModel
+
+    if workload == "olmoe":
+        h, nh, nkv, V, qk, th, E, K, I, norm = 2048, 16, 16, 50304, True, 1e4, 64, 8, 1024, False
+    else:
+        h, nh, nkv, V, qk, th, E, K, I, norm = 4096, 32, 8, 32000, False, 1e6, 8, 2, 14336, True
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    dm = DenseModel(hidden_dim=h, num_heads=nh, num_kv_heads=nkv, num_layers=layers, vocab_size=V,
+                    qk_norm=qk, rope_theta=th, max_batch=1, max_seq=tokens + 1)
+    dm.load_all(synth.dense_weights_device(1, h=h, nh=nh, nkv=nkv, hd=128, layers=layers, vocab=V,
+                                           qk_norm=qk, device=dev))
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, num_layers=layers,
+                   max_batch=8, norm_topk_prob=norm)
+    for layer in range(layers):
+        img = synth.layer_image_device(E, h, I, 64, seed=layer, device=dev)
+        blk.load_expert_layer(layer, img)
+        del img
+        blk.load_router(layer, synth.router_weights(100 + layer, E, h))
+    prompt = torch.randint(0, V, (tokens,), dtype=torch.int32, device=dev)
+    for _ in range(2):
+        dm.set_position(0)
+        dm.prefill(blk, prompt)
     torch.cuda.synchronize()
     dm.synchronize()
     blk.synchronize()
@@ -304,6 +343,8 @@ def main(argv: list[str]) -> None:
         prefill_case(argv[1] if len(argv) > 1 else "mixtral", int(argv[2]) if len(argv) > 2 else 512)
     elif len(argv) >= 1 and argv[0] == "decode":
         decode_case(argv[1] if len(argv) > 1 else "olmoe", int(argv[2]) if len(argv) > 2 else 1)
+    elif len(argv) >= 1 and argv[0] == "prefill_step":
+        prefill_step_case(argv[1] if len(argv) > 1 else "olmoe", int(argv[2]) if len(argv) > 2 else 512)
     elif len(argv) >= 1 and argv[0] == "trace_ep":
         trace_ep_case(argv[1] if len(argv) > 1 else "olmoe")
     elif len(argv) >= 1 and argv[0] == "trace":

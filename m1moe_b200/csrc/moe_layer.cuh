@@ -1583,76 +1583,136 @@ __global__ void __launch_bounds__(kLayerThreads, 1) k_moe_layer(const LayerParam
         }
         if (tid == 0) trace_event(p.trace, 0, 17);
         named_sync(1, kConsumerThreads);  // every gate/up item of this CTA is done
-        // Activations of this CTA's rows, in two short passes: (1) one thread
+        // Activations of this CTA's rows.  Other group sizes than 64 take two
+        // short passes: (1) one thread
         // per (row, token) sums the column slices in order and applies SwiGLU
         // where items left partial sums, and the 8 lanes of a column block
         // reduce its max |a| and sum; (2) one per (block, token): the group's
         // (gs rows) max from its blocks, the block as int16 pairs in the dp2a
         // layout (4 words, as for x), and per group the scale and fp32 sum.
         const int ncb_cta = (b - a) >> 3, arows = p.act_cb * 8;
-        {
-            // passes 1 and 2 together: thread (token k, row lr), rows inner, so
-            // the 8 rows of a column block are 8 consecutive lanes and the
-            // block's max |a| and sum come from shuffles
-            const int nrows = b - a, total = nrows * NT;
-            for (int base = warp * 32; base < total; base += kConsumerThreads) {
-                const int i = base + lane, k = i / max(nrows, 1), lr = i - k * nrows;
-                float v = 0.f;
-                if (i < total) {
-                    float *af = actf + (size_t)k * arows + lr;
-                    if (nslg > 1) {
-                        const int e = rs.ulist[fdiv(a + lr, p.fd_I)];
-                        if (!ctl.abort && ((rs.tmask[e] >> k) & 1u)) {
+        if (p.gs == 64) {
+            // Groups of 64 rows (every shipped model): one warp per (group of
+            // this CTA's range, token), lane l holding rows 2l and 2l+1 of the
+            // group -- SwiGLU where items left partial sums, the group's max
+            // |a| and fp32 sum by warp reductions, the int16 quantisation, and
+            // the dp2a packing (lanes 4c+j hold rows 8c+2j, 8c+2j+1 of column
+            // block c) by one shuffle: no block-wide pass in between
+            const int ngr = b > a ? fdiv(b - 1, p.fd_gs) - ag + 1 : 0;
+            for (int wi = warp; wi < ngr * NT; wi += kConsumerWarps) {
+                const int gi = wi / NT, k = wi - gi * NT, gg = ag + gi;
+                const int r_lo = max(gg * 64, a), r_hi = min(gg * 64 + 64, b);
+                const int u = fdiv(r_lo, p.fd_I);  // 64 | I: a group lies in one expert
+                // k: a token (row groups) or a token slot of expert u (slot path)
+                if (ctl.abort || (SL ? k >= sl.ute[rs.ulist[u]] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
+                float v[2] = {0.f, 0.f};
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    const int R = gg * 64 + 2 * lane + h2;
+                    if (R >= r_lo && R < r_hi) {
+                        const int lr = R - a;
+                        if (nslg > 1) {
                             float gv = 0.f, uv = 0.f;
                             const float *gp = gup + (size_t)lr * nslg * (2 * NT) + 2 * k;
                             for (int jj = 0; jj < nslg; ++jj) {
                                 gv += gp[jj * 2 * NT];
                                 uv += gp[jj * 2 * NT + 1];
                             }
-                            v = swiglu(gv, uv);
-                            *af = v;
+                            v[h2] = swiglu(gv, uv);
+                        } else {
+                            v[h2] = actf[(size_t)k * arows + lr];
                         }
-                    } else {
-                        v = *af;
                     }
                 }
-                float m = fabsf(v), sm = v;
+                float m = fmaxf(fabsf(v[0]), fabsf(v[1])), sm = v[0] + v[1];
 #pragma unroll
-                for (int o = 1; o < 8; o <<= 1) {
+                for (int o = 16; o > 0; o >>= 1) {
                     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
                     sm += __shfl_xor_sync(0xffffffffu, sm, o);
                 }
-                if (i < total && (lane & 7) == 0) {
-                    const int bi = (lr >> 3) * NT + k;
-                    bst[2 * bi] = m;
-                    bst[2 * bi + 1] = sm;
+                const float inv = m > 0.f ? 32767.0f / m : 0.f;
+                const uint32_t q0 = (uint32_t)(__float2int_rn(v[0] * inv) & 0xFFFF);
+                const uint32_t q1 = (uint32_t)(__float2int_rn(v[1] * inv) & 0xFFFF);
+                const uint32_t n0 = __shfl_down_sync(0xffffffffu, q0, 1), n1 = __shfl_down_sync(0xffffffffu, q1, 1);
+                const int R0 = gg * 64 + 8 * (lane >> 2);  // first row of this lane's column block
+                if ((lane & 1) == 0 && R0 >= r_lo && R0 < r_hi) {
+                    // words 0/1: rows (0,2) / (4,6) of the block; 2/3: rows (1,3) / (5,7)
+                    const int w = (lane & 3) >> 1;
+                    uint32_t *o = act + (((size_t)k * p.act_cb + ((R0 - a) >> 3)) << 2);
+                    o[w] = q0 | (n0 << 16);
+                    o[2 + w] = q1 | (n1 << 16);
+                }
+                if (lane == 0) {
+                    float *xg = xseg + ((size_t)(gg - ag) * NT + k) * 2;
+                    xg[0] = sm;
+                    xg[1] = m * (1.0f / 32767.0f);
                 }
             }
-        }
-        named_sync(1, kConsumerThreads);
-        for (int i = tid; i < ncb_cta * NT; i += kConsumerThreads) {
-            const int cb = i / NT, k = i % NT;
-            const int R0 = a + 8 * cb, u = fdiv(R0, p.fd_I);
-            // k: a token (row groups) or a token slot of expert u (slot path)
-            if (ctl.abort || (SL ? k >= sl.ute[rs.ulist[u]] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
-            const int gg = fdiv(a8 + cb, p.fd_gcb);
-            const int c_lo = max(gg * gcb, a8) - a8, c_hi = min((gg + 1) * gcb, b >> 3) - a8;
-            float m = 0.f;
-            for (int c = c_lo; c < c_hi; ++c) m = fmaxf(m, bst[2 * (c * NT + k)]);
-            const float inv = m > 0.f ? 32767.0f / m : 0.f;
-            const float *x = actf + (size_t)k * arows + 8 * cb;
-            auto qz = [&](float v) { return (uint32_t)(__float2int_rn(v * inv) & 0xFFFF); };
-            uint32_t *o = act + (((size_t)k * p.act_cb + cb) << 2);
-            o[0] = qz(x[0]) | (qz(x[2]) << 16);
-            o[1] = qz(x[4]) | (qz(x[6]) << 16);
-            o[2] = qz(x[1]) | (qz(x[3]) << 16);
-            o[3] = qz(x[5]) | (qz(x[7]) << 16);
-            if (cb == c_lo) {  // the group's first block of this range: scale and sum
-                float sum = 0.f;
-                for (int c = c_lo; c < c_hi; ++c) sum += bst[2 * (c * NT + k) + 1];
-                float *xg = xseg + ((size_t)(gg - ag) * NT + k) * 2;
-                xg[0] = sum;
-                xg[1] = m * (1.0f / 32767.0f);
+        } else {
+            {
+                // passes 1 and 2 together: thread (token k, row lr), rows inner, so
+                // the 8 rows of a column block are 8 consecutive lanes and the
+                // block's max |a| and sum come from shuffles
+                const int nrows = b - a, total = nrows * NT;
+                for (int base = warp * 32; base < total; base += kConsumerThreads) {
+                    const int i = base + lane, k = i / max(nrows, 1), lr = i - k * nrows;
+                    float v = 0.f;
+                    if (i < total) {
+                        float *af = actf + (size_t)k * arows + lr;
+                        if (nslg > 1) {
+                            const int e = rs.ulist[fdiv(a + lr, p.fd_I)];
+                            if (!ctl.abort && ((rs.tmask[e] >> k) & 1u)) {
+                                float gv = 0.f, uv = 0.f;
+                                const float *gp = gup + (size_t)lr * nslg * (2 * NT) + 2 * k;
+                                for (int jj = 0; jj < nslg; ++jj) {
+                                    gv += gp[jj * 2 * NT];
+                                    uv += gp[jj * 2 * NT + 1];
+                                }
+                                v = swiglu(gv, uv);
+                                *af = v;
+                            }
+                        } else {
+                            v = *af;
+                        }
+                    }
+                    float m = fabsf(v), sm = v;
+    #pragma unroll
+                    for (int o = 1; o < 8; o <<= 1) {
+                        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                        sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                    }
+                    if (i < total && (lane & 7) == 0) {
+                        const int bi = (lr >> 3) * NT + k;
+                        bst[2 * bi] = m;
+                        bst[2 * bi + 1] = sm;
+                    }
+                }
+            }
+            named_sync(1, kConsumerThreads);
+            for (int i = tid; i < ncb_cta * NT; i += kConsumerThreads) {
+                const int cb = i / NT, k = i % NT;
+                const int R0 = a + 8 * cb, u = fdiv(R0, p.fd_I);
+                // k: a token (row groups) or a token slot of expert u (slot path)
+                if (ctl.abort || (SL ? k >= sl.ute[rs.ulist[u]] : !((rs.tmask[rs.ulist[u]] >> k) & 1u))) continue;
+                const int gg = fdiv(a8 + cb, p.fd_gcb);
+                const int c_lo = max(gg * gcb, a8) - a8, c_hi = min((gg + 1) * gcb, b >> 3) - a8;
+                float m = 0.f;
+                for (int c = c_lo; c < c_hi; ++c) m = fmaxf(m, bst[2 * (c * NT + k)]);
+                const float inv = m > 0.f ? 32767.0f / m : 0.f;
+                const float *x = actf + (size_t)k * arows + 8 * cb;
+                auto qz = [&](float v) { return (uint32_t)(__float2int_rn(v * inv) & 0xFFFF); };
+                uint32_t *o = act + (((size_t)k * p.act_cb + cb) << 2);
+                o[0] = qz(x[0]) | (qz(x[2]) << 16);
+                o[1] = qz(x[4]) | (qz(x[6]) << 16);
+                o[2] = qz(x[1]) | (qz(x[3]) << 16);
+                o[3] = qz(x[5]) | (qz(x[7]) << 16);
+                if (cb == c_lo) {  // the group's first block of this range: scale and sum
+                    float sum = 0.f;
+                    for (int c = c_lo; c < c_hi; ++c) sum += bst[2 * (c * NT + k) + 1];
+                    float *xg = xseg + ((size_t)(gg - ag) * NT + k) * 2;
+                    xg[0] = sum;
+                    xg[1] = m * (1.0f / 32767.0f);
+                }
             }
         }
         named_sync(1, kConsumerThreads);

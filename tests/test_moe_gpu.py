@@ -23,9 +23,9 @@ def _bf16_dev(a: np.ndarray, dtype=torch.bfloat16) -> torch.Tensor:
     return t if dtype == torch.bfloat16 else t.to(dtype)
 
 
-def _block(img, routers, *, h, I, E, K, norm, max_batch=8, expert_begin=0, expert_count=0):
+def _block(img, routers, *, h, I, E, K, norm, max_batch=8, expert_begin=0, expert_count=0, gs=64):
     from m1moe_b200 import MoEBlock
-    blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, group_size=64,
+    blk = MoEBlock(hidden_dim=h, intermediate_dim=I, num_experts=E, top_k=K, group_size=gs,
                    num_layers=len(routers), norm_topk_prob=norm, max_batch=max_batch,
                    expert_begin=expert_begin, expert_count=expert_count)
     for L, r in enumerate(routers):
@@ -51,8 +51,8 @@ def _check_routing(idx, w, ref_idx, ref_w, x_f32, router, K):
 
 
 def _run_case(oracle_lib, img, router, *, h, I, E, K, norm, B, xdt=torch.bfloat16,
-              odt=torch.float32, with_res=True, seed=0):
-    blk = _block([img], [router], h=h, I=I, E=E, K=K, norm=norm)
+              odt=torch.float32, with_res=True, seed=0, gs=64):
+    blk = _block([img], [router], h=h, I=I, E=E, K=K, norm=norm, gs=gs)
     xb = synth.hidden_states(seed + 1, B, h)
     rb = synth.hidden_states(seed + 2, B, h)
     xf, rf = synth.bf16_to_f32(xb), synth.bf16_to_f32(rb)
@@ -61,7 +61,7 @@ def _run_case(oracle_lib, img, router, *, h, I, E, K, norm, B, xdt=torch.bfloat1
     out = out.float().cpu().numpy()
     idx, w = idx.cpu().numpy(), w.cpu().numpy()
     ref, ridx, rw = oracle_lib.moe_layer(img, router, xf, rf if with_res else None, h=h, inter=I,
-                                         E=E, K=K, gs=64, norm=norm, nthreads=8)
+                                         E=E, K=K, gs=gs, norm=norm, nthreads=8)
     blk.synchronize()  # raises if a bounded device wait gave up
     _check_routing(idx, w, ridx, rw, xf, router, K)
     checked = 0
@@ -263,3 +263,14 @@ def test_moe_layer_not_loaded_is_an_error():
     with pytest.raises(M1MoECudaError, match="INVALID_ARG"):
         blk.load_expert_layer(0, np.zeros(10, np.uint8))
     blk.close()
+
+
+@pytest.mark.parametrize("gs,h,B", [(128, 512, 1), (128, 512, 2), (128, 2048, 4), (128, 2048, 8)])
+def test_layer_other_group_sizes(oracle_lib, gs, h, B):
+    """A group size of 128 (the layer accepts any multiple of 32 dividing h and
+    I; the shipped models use 64): the kernel's activation pass takes its
+    general two-pass form there, against the oracle at the same group size."""
+    E, K, I = 8, 2, 256
+    img = synth.layer_image(5 + gs, E, h, I, gs)
+    router = synth.router_weights(6 + gs, E, h)
+    _run_case(oracle_lib, img, router, h=h, I=I, E=E, K=K, norm=True, B=B, seed=gs + B, gs=gs)

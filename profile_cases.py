@@ -207,12 +207,7 @@ def trace_case(workload: str, batch: int, layers: int = 4, calls: int = 20) -> N
     x = torch.randn(batch, h, device="cuda")
     out = torch.empty(batch, h, device="cuda")
     trace = torch.zeros((160, 32), dtype=torch.int64, device="cuda")
-    names = {0: "start", 1: "out rows init", 2: "logits published", 12: "all logits seen",
-             13: "ranks counted", 3: "top-K ranked", 19: "producer saw routing",
-             16: "geometry", 11: "first tile issued", 4: "consumers released", 5: "first tile landed",
-             9: "all tiles issued", 17: "gate/up done", 6: "activations quantised",
-             18: "first down item", 22: "first down tile", 23: "last down tile", 7: "epochs seen",
-             8: "down items done", 10: "end"}
+    names = dict(TRACE_NAMES)  # events a call did not record are left out
     rows = {ev: [] for ev in names}
     spread = {ev: [] for ev in names}
     tiles = []

@@ -299,19 +299,22 @@ __device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) {
     return d;
 }
 
-// Q = sum_j q_j * x16_j over one 16-byte weight chunk.
+// Q = sum_j q_j * x16_j over one 16-byte weight chunk.  The odd nibbles stay
+// in the high half of each byte (one AND, no shift: 16 * q), summed in their
+// own chain and scaled down once at the end -- exact, since that chain is a
+// multiple of 16 and |chain| <= 16 * 240 * 32767 < 2^31.
 __device__ __forceinline__ int dot_chunk_i16(const uint4 w, const uint32_t (&xq)[16]) {
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
     int a0 = 0, a1 = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const uint32_t lo = ws[i] & 0x0F0F0F0Fu, hi = (ws[i] >> 4) & 0x0F0F0F0Fu;
+        const uint32_t lo = ws[i] & 0x0F0F0F0Fu, hi = ws[i] & 0xF0F0F0F0u;
         a0 = dp2a_lo(xq[4 * i + 0], lo, a0);
-        a1 = dp2a_hi(xq[4 * i + 1], lo, a1);
-        a0 = dp2a_lo(xq[4 * i + 2], hi, a0);
+        a0 = dp2a_hi(xq[4 * i + 1], lo, a0);
+        a1 = dp2a_lo(xq[4 * i + 2], hi, a1);
         a1 = dp2a_hi(xq[4 * i + 3], hi, a1);
     }
-    return a0 + a1;
+    return a0 + (a1 >> 4);
 }
 
 // The chunk's nibble planes, for reuse by several token vectors: lo[i] holds
